@@ -1,0 +1,174 @@
+/*
+ * rl_sampler.h -- C ABI of the B200 (sm_100a) logits -> token sampler.
+ *
+ * Drop-in device backend for the sampling path of chenyusolar/rust-llm
+ * (src/decoder.rs). Plain pointers and sizes only; every entry point returns
+ * an rl_status and never aborts, throws or traps (the reference's release
+ * profile is panic = "abort", Cargo.toml:40-43, so errors must come back as
+ * values). The last error message of the calling thread is rl_last_error().
+ *
+ * Device pointers: every logits / history / mask / params / uniforms / output
+ * pointer passed to an entry point without a _host suffix is a device pointer
+ * on the handle's device. Work is enqueued on `stream` (a cudaStream_t passed
+ * as void*, NULL = legacy default stream) and is asynchronous unless stated.
+ *
+ * Layouts:
+ *  - logits: row-major [B, V] with row stride `ld` elements (ld >= V).
+ *  - history: row-major [B, hist_stride] int32 token ids; hist_len[b] of them
+ *    are valid. Ids outside [0, V) are ignored.
+ *  - mask: row-major [B, mask_stride] uint32 words; bit (i & 31) of word
+ *    (i >> 5) set <=> token id i is allowed (LSB first). A row with no bit set
+ *    allows every id (src/decoder.rs:362-364).
+ *  - uniforms: one float in [0, 1) per row; it replaces rand_secure()
+ *    (src/decoder.rs:170-188), which cannot be seeded.
+ */
+#ifndef RL_SAMPLER_H
+#define RL_SAMPLER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  RL_OK = 0,
+  RL_ERR_INVALID_ARG = 1, /* null pointer, bad enum, negative size           */
+  RL_ERR_SHAPE = 2,       /* size beyond the handle's limits or the kernel's */
+  RL_ERR_OOM = 3,         /* device allocation failed (create only)          */
+  RL_ERR_CUDA = 4,        /* a CUDA runtime call failed                      */
+  RL_ERR_NCCL = 5,        /* an NCCL call failed (sharded sampling)          */
+  RL_ERR_TIMEOUT = 6,     /* a bounded device-side wait expired              */
+  RL_ERR_UNSUPPORTED = 7, /* feature not built into this library             */
+  RL_ERR_NONFINITE = 8    /* a row's inputs were not finite (see row_status) */
+} rl_status;
+
+typedef enum { RL_F32 = 0, RL_BF16 = 1 } rl_dtype;
+
+/* Per-row sampling parameters (24 bytes). SamplingParams, src/decoder.rs:294-316,
+ * plus presence/frequency penalties (absent from the reference). */
+typedef struct {
+  float temperature;       /* <= 0: greedy (argmax, lowest id on ties)        */
+  float top_p;             /* >= 1: no nucleus cut                            */
+  int32_t top_k;           /* <= 0: off (k = number of allowed ids)           */
+  float repeat_penalty;    /* history ids: x<0 ? x*rp : x/rp (decoder.rs:102) */
+  float presence_penalty;  /* history ids: x -= pres                          */
+  float frequency_penalty; /* history ids: x -= count*freq                    */
+} rl_row_params;
+
+typedef struct rl_sampler rl_sampler;
+
+/* Creates a sampler on `device`. The handle owns a small device workspace
+ * sized by the limits (allocated here, never in a sampling call).
+ * Replaces the per-call construction of Decoder / Sampler
+ * (src/decoder.rs:19-29, :325-331). flags: reserved, pass 0. */
+rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max_vocab,
+                            int max_history, uint32_t flags);
+rl_status rl_sampler_destroy(rl_sampler* h);
+
+/* Thread-local message of the last failing call on this thread ("" if none). */
+const char* rl_last_error(void);
+
+/* Library version string. */
+const char* rl_version(void);
+
+/*
+ * Batched spec sampling: penalties -> mask -> temperature -> softmax ->
+ * top-k -> top-p -> draw, one token per row.
+ * Replaces the serial per-sequence loop of ContinuousBatchingEngine::step
+ * (src/inference.rs:112-138) calling Model::sample_with_params
+ * (src/model.rs:484-486 -> src/decoder.rs:35-100), extended with the
+ * reference's top_k_logits / sample_top_p / sample_multinomial helpers
+ * (src/decoder.rs:112-158) and history penalties.
+ *  out_tok[B]   sampled ids (device)
+ *  out_prob[B]  probability of the sampled id after the top-p renormalisation
+ *               (device, nullable)
+ *  row_status[B] per-row status, 0 ok / RL_ERR_NONFINITE (device, nullable)
+ */
+rl_status rl_sample_batch(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V,
+                          int64_t ld, const int32_t* hist, const int32_t* hist_len,
+                          int hist_stride, const uint32_t* mask, int64_t mask_stride,
+                          const rl_row_params* params, const float* uniforms, int32_t* out_tok,
+                          float* out_prob, int32_t* row_status, void* stream);
+
+/*
+ * Same as rl_sample_batch, and also writes each row's ordered top-k list
+ * (ids and full-vocabulary probabilities, in (logit desc, id asc) order) for
+ * inspection: list_ids / list_probs are [B, list_cap], list_len[B] gets
+ * min(K, list_cap). Requires every row's K (top_k, or the allowed count when
+ * top_k is off) to be <= 1024.
+ */
+rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtype, int B,
+                                int V, int64_t ld, const int32_t* hist, const int32_t* hist_len,
+                                int hist_stride, const uint32_t* mask, int64_t mask_stride,
+                                const rl_row_params* params, const float* uniforms,
+                                int32_t* out_tok, float* out_prob, int32_t* row_status,
+                                int32_t* list_ids, float* list_probs, int32_t* list_len,
+                                int list_cap, void* stream);
+
+/*
+ * Host-buffer convenience wrapper of rl_sample_batch (f32 logits): copies the
+ * inputs to the handle's device staging buffers, samples, copies the outputs
+ * back and synchronises. Backs the &[f32] Rust signatures
+ * (Decoder::sample_with_params, src/decoder.rs:35). hist/hist_len/mask/out_prob
+ * may be NULL.
+ */
+rl_status rl_sample_host(rl_sampler* h, const float* logits, int B, int V, const int32_t* hist,
+                         const int32_t* hist_len, int hist_stride, const uint32_t* mask,
+                         int64_t mask_stride, const rl_row_params* params, const float* uniforms,
+                         int32_t* out_tok, float* out_prob);
+
+/*
+ * ref_exact profile: Decoder::sample_with_params (src/decoder.rs:35-100)
+ * reproduced quirk for quirk, per row: temperature softmax; if top_p < 1 a
+ * stable descending sort, cumsum >= top_p cutoff, zeroing of ORIGINAL ids
+ * greater than the cutoff position (decoder.rs:71-75), renormalisation; then
+ * the id-order draw r <= cumsum and the last-max argmax fallback.
+ * Decoder::sample (decoder.rs:31-33) is temperature = 1, top_p = 0.9.
+ *  temperature[B], top_p[B], uniforms[B]: device arrays.
+ *  out_prob[B]: the returned id's entry of the final probability array (nullable).
+ * V must be <= 53248 (the row is held in one CTA's shared memory).
+ */
+rl_status rl_decoder_sample(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
+                            const float* temperature, const float* top_p, const float* uniforms,
+                            int32_t* out_tok, float* out_prob, void* stream);
+
+/* Decoder::greedy_sample (src/decoder.rs:160-167): argmax, LAST maximum on ties. */
+rl_status rl_greedy(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
+                    int32_t* out_tok, void* stream);
+
+/* Sampler::sample_with_grammar (src/decoder.rs:359-376): argmax over the
+ * allowed ids of the bit-packed mask, LOWEST allowed id on ties; an all-zero
+ * mask row allows every id. */
+rl_status rl_grammar_greedy(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
+                            const uint32_t* mask, int64_t mask_stride, int32_t* out_tok,
+                            void* stream);
+
+/*
+ * One beam-search step for `items` independent searches of `beams` beams
+ * (BeamSearch::search, src/decoder.rs:227-270, batched over items and beams).
+ *  logits      [items*beams, V] (row = item*beams + beam), stride ld
+ *  beam_scores [items*beams] cumulative scores
+ *  beam_done   [items*beams] 1 if the hypothesis is complete (carried over)
+ *  beam_len    [items*beams] current token count (used when alpha != 1)
+ * Candidates: a completed beam carries itself (token -1); a live beam offers
+ * its top 2*beams ids with score (s + v) / lp(len+1), v = x - logsumexp(x)
+ * when log_softmax != 0 (spec) or the raw logit x when 0 (the reference's
+ * decoder.rs:249), lp = 1 if alpha == 1 else ((len+7)/6)^alpha
+ * (decoder.rs:278-284); done = (id == eos). Output per item: the best n_out
+ * candidates ordered by score desc, then beam asc, then logit desc, then id asc
+ * (the reference's stable-sort order), n_out <= 2*beams:
+ *  out_beam/out_tok/out_score/out_done [items, n_out].
+ * beams <= 16, 2*beams <= 32.
+ */
+rl_status rl_beam_step(rl_sampler* h, const float* logits, int items, int beams, int V,
+                       int64_t ld, const float* beam_scores, const uint8_t* beam_done,
+                       const int32_t* beam_len, float alpha, int eos, int log_softmax, int n_out,
+                       int32_t* out_beam, int32_t* out_tok, float* out_score, uint8_t* out_done,
+                       void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RL_SAMPLER_H */
