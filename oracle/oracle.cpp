@@ -210,6 +210,7 @@ int32_t orc_grammar_greedy(const float* logits, int V, const uint32_t* mask_row)
 //  1. penalties on history ids (unique id i with count c): x1 = x<0 ? x*rp : x/rp;
 //     x2 = x1 - (float)c*freq; x3 = x2 - pres. History ids outside [0, V) ignored.
 //  2. mask: bit clear -> id excluded. A row whose mask allows nothing allows all.
+//     Ids whose logit is -inf after the penalties are excluded as well.
 //  3. T <= 0: greedy over allowed x3, ties -> lowest id, prob 1.
 //  4. m = max allowed x3; l_i = (x3_i - m) / T (f32, IEEE); e_i = expf(l_i);
 //     Z = sum(double e_i); p_i = e_i / Z (double).
@@ -218,8 +219,8 @@ int32_t orc_grammar_greedy(const float* logits, int V, const uint32_t* mask_row)
 //     else K; cutoff = min(cutoff, K-1). top_p >= 1: cutoff = K-1.
 //  7. S = cum_cutoff; draw j = first j <= cutoff with cum_j > u*S (else cutoff).
 //     token = L[j], prob = (float)(p_j / S).
-// Return value: 0 ok, 1 non-finite input (NaN or +inf among allowed ids, or every
-// allowed logit -inf, or non-finite T).
+// Return value: 0 ok, 1 non-finite input (NaN or +inf on an allowed id, no
+// finite allowed logit, or non-finite T).
 struct orc_spec_out {
   int32_t token;
   float prob;
@@ -270,17 +271,24 @@ int orc_spec_sample_row(const float* x_in, int V, const int32_t* hist, int hlen,
   }
   out->draw_margin = INFINITY;
   out->cut_margin = INFINITY;
-  // validity
+  // validity; a -inf logit (after penalties) has zero probability and is
+  // excluded from the list like a masked id
   float m = -INFINITY;
   int argmax = -1;
   for (int i = 0; i < V; ++i) {
     if (!allowed[i]) continue;
     if (std::isnan(x[i]) || x[i] == INFINITY) return 1;
+    if (x[i] == -INFINITY) {
+      allowed[i] = 0;
+      --n_allowed;
+      continue;
+    }
     if (argmax < 0 || x[i] > m) {
       m = x[i];
       argmax = i;
     }
   }
+  if (n_allowed == 0) return 1;
   out->max_x = m;
   const float T = prm->temperature;
   if (!std::isfinite(T)) return 1;
@@ -297,7 +305,6 @@ int orc_spec_sample_row(const float* x_in, int V, const int32_t* hist, int hlen,
     }
     return 0;
   }
-  if (m == -INFINITY) return 1;
   // 4. softmax
   std::vector<float> e(V, 0.0f);
   double Z = 0.0;

@@ -1,0 +1,245 @@
+// C ABI of the sampler (include/rl_sampler.h): handle lifetime, argument
+// validation, error reporting and the launches.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "rl_sampler.h"
+#include "spec_kernel.cuh"
+#include "internal.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+rl_status fail(rl_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return st;
+}
+
+rl_status cuda_fail(cudaError_t e, const char* what) {
+  return fail(RL_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// Makes the handle's device current for the scope of a call.
+struct DeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace
+
+namespace rl {
+rl_status set_error(rl_status st, const char* msg) { return fail(st, "%s", msg); }
+void clear_error() { g_err.clear(); }
+}  // namespace rl
+
+extern "C" {
+#pragma GCC visibility push(default)
+
+const char* rl_last_error(void) { return g_err.c_str(); }
+
+const char* rl_version(void) { return "rl_sampler 0.1 (sm_100a)"; }
+
+rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max_vocab,
+                            int max_history, uint32_t flags) {
+  if (!out) return fail(RL_ERR_INVALID_ARG, "rl_sampler_create: out is NULL");
+  *out = nullptr;
+  if (max_batch <= 0 || max_vocab <= 0 || max_history < 0)
+    return fail(RL_ERR_INVALID_ARG, "rl_sampler_create: limits must be positive");
+  if (max_batch > 65535) return fail(RL_ERR_SHAPE, "rl_sampler_create: max_batch > 65535");
+  if (max_history > rl::kHmax)
+    return fail(RL_ERR_SHAPE, "rl_sampler_create: max_history %d > %d", max_history, rl::kHmax);
+  int ndev = 0;
+  cudaError_t e = cudaGetDeviceCount(&ndev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev)
+    return fail(RL_ERR_INVALID_ARG, "rl_sampler_create: device %d not present (%d devices)", device, ndev);
+  DeviceGuard g(device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "rl_sampler_create: cudaSetDevice(%d) failed", device);
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major < 10)
+    return fail(RL_ERR_UNSUPPORTED, "rl_sampler_create: device %d is sm_%d%d; this library is built for sm_100a",
+                device, prop.major, prop.minor);
+  rl_sampler* h = new (std::nothrow) rl_sampler();
+  if (!h) return fail(RL_ERR_OOM, "rl_sampler_create: host allocation failed");
+  h->device = device;
+  h->max_batch = max_batch;
+  h->max_vocab = max_vocab;
+  h->max_history = max_history;
+  h->num_sms = prop.multiProcessorCount;
+  h->flags = flags;
+  rl_status st = rl::alloc_workspace(h);
+  if (st != RL_OK) {
+    rl::free_workspace(h);
+    delete h;
+    return st;
+  }
+  *out = h;
+  rl::clear_error();
+  return RL_OK;
+}
+
+rl_status rl_sampler_destroy(rl_sampler* h) {
+  if (!h) return RL_OK;
+  DeviceGuard g(h->device);
+  rl::free_workspace(h);
+  delete h;
+  return RL_OK;
+}
+
+static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V,
+                               int64_t ld, const int32_t* hist, const int32_t* hist_len,
+                               int hist_stride, const uint32_t* mask, int64_t mask_stride,
+                               const rl_row_params* params, const float* uniforms, int32_t* out_tok,
+                               float* out_prob, int32_t* row_status, int32_t* list_ids,
+                               float* list_probs, int32_t* list_len, int list_cap, void* stream,
+                               int vocab_offset) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: handle is NULL");
+  if (B < 0 || V <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: B=%d V=%d", B, V);
+  if (B == 0) return RL_OK;
+  if (!logits || !params || !uniforms || !out_tok)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: logits, params, uniforms and out_tok are required");
+  if (dtype != RL_F32 && dtype != RL_BF16) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: bad dtype %d", dtype);
+  if (ld < V) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: ld %lld < V %d", (long long)ld, V);
+  if (B > h->max_batch || V > h->max_vocab)
+    return fail(RL_ERR_SHAPE, "rl_sample_batch: B=%d V=%d beyond the handle's limits (%d, %d)", B, V,
+                h->max_batch, h->max_vocab);
+  if (hist) {
+    if (!hist_len) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: hist without hist_len");
+    if (hist_stride < 0 || hist_stride > h->max_history)
+      return fail(RL_ERR_SHAPE, "rl_sample_batch: hist_stride %d beyond max_history %d", hist_stride,
+                  h->max_history);
+  }
+  if (mask && mask_stride < (V + 31) / 32)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: mask_stride %lld < ceil(V/32)", (long long)mask_stride);
+  if (list_len && (!list_ids || !list_probs || list_cap <= 0))
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list buffers required");
+  const int es = dtype == RL_BF16 ? 2 : 4;
+  const int C = rl::spec_pick_cluster(B, V, es, h->num_sms);
+  const int L = (((V + C - 1) / C + 127) / 128) * 128;
+  if (rl::spec_smem_bytes(L, es) > 227 * 1024)
+    return fail(RL_ERR_SHAPE, "rl_sample_batch: V=%d too large for one cluster of %d CTAs", V, C);
+  DeviceGuard g(h->device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  rl::SpecArgs a = {};
+  a.logits = logits;
+  a.ld = ld;
+  a.B = B;
+  a.V = V;
+  a.hist = hist;
+  a.hist_len = hist_len;
+  a.hist_stride = hist ? hist_stride : 0;
+  a.mask = mask;
+  a.mask_stride = mask_stride;
+  a.params = params;
+  a.uniforms = uniforms;
+  a.out_tok = out_tok;
+  a.out_prob = out_prob;
+  a.row_status = row_status;
+  a.list_ids = list_ids;
+  a.list_probs = list_probs;
+  a.list_len = list_len;
+  a.list_cap = list_cap;
+  a.vocab_offset = vocab_offset;
+  a.mode = rl::kModeSample;
+  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
+  return RL_OK;
+}
+
+rl_status rl_sample_batch(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V, int64_t ld,
+                          const int32_t* hist, const int32_t* hist_len, int hist_stride,
+                          const uint32_t* mask, int64_t mask_stride, const rl_row_params* params,
+                          const float* uniforms, int32_t* out_tok, float* out_prob, int32_t* row_status,
+                          void* stream) {
+  return sample_common(h, logits, dtype, B, V, ld, hist, hist_len, hist_stride, mask, mask_stride, params,
+                       uniforms, out_tok, out_prob, row_status, nullptr, nullptr, nullptr, 0, stream, 0);
+}
+
+rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V,
+                                int64_t ld, const int32_t* hist, const int32_t* hist_len,
+                                int hist_stride, const uint32_t* mask, int64_t mask_stride,
+                                const rl_row_params* params, const float* uniforms, int32_t* out_tok,
+                                float* out_prob, int32_t* row_status, int32_t* list_ids,
+                                float* list_probs, int32_t* list_len, int list_cap, void* stream) {
+  if (!list_len) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list_len is NULL");
+  return sample_common(h, logits, dtype, B, V, ld, hist, hist_len, hist_stride, mask, mask_stride, params,
+                       uniforms, out_tok, out_prob, row_status, list_ids, list_probs, list_len, list_cap,
+                       stream, 0);
+}
+
+rl_status rl_sample_host(rl_sampler* h, const float* logits, int B, int V, const int32_t* hist,
+                         const int32_t* hist_len, int hist_stride, const uint32_t* mask,
+                         int64_t mask_stride, const rl_row_params* params, const float* uniforms,
+                         int32_t* out_tok, float* out_prob) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_host: handle is NULL");
+  if (B < 0 || V <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_host: B=%d V=%d", B, V);
+  if (B == 0) return RL_OK;
+  if (!logits || !params || !uniforms || !out_tok)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_host: logits, params, uniforms and out_tok are required");
+  if (!h->stage_logits) return fail(RL_ERR_UNSUPPORTED, "rl_sample_host: handle created without staging buffers");
+  if (B > h->max_batch || V > h->max_vocab)
+    return fail(RL_ERR_SHAPE, "rl_sample_host: B=%d V=%d beyond the handle's limits", B, V);
+  if (hist && (!hist_len || hist_stride < 0 || hist_stride > h->max_history))
+    return fail(RL_ERR_SHAPE, "rl_sample_host: bad history arguments");
+  if (mask && (mask_stride < (V + 31) / 32 || mask_stride > h->mask_words))
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_host: mask_stride must be in [ceil(V/32), ceil(max_vocab/32)]");
+  DeviceGuard g(h->device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  cudaStream_t s = h->stream;
+  cudaError_t e;
+#define RL_TRY(call, what)                   \
+  do {                                       \
+    e = (call);                              \
+    if (e != cudaSuccess) return cuda_fail(e, what); \
+  } while (0)
+  RL_TRY(cudaMemcpyAsync(h->stage_logits, logits, sizeof(float) * (size_t)B * V, cudaMemcpyHostToDevice, s),
+         "rl_sample_host: copy logits");
+  if (hist) {
+    RL_TRY(cudaMemcpyAsync(h->stage_hist, hist, sizeof(int32_t) * (size_t)B * hist_stride, cudaMemcpyHostToDevice, s),
+           "rl_sample_host: copy history");
+    RL_TRY(cudaMemcpyAsync(h->stage_hist_len, hist_len, sizeof(int32_t) * B, cudaMemcpyHostToDevice, s),
+           "rl_sample_host: copy history lengths");
+  }
+  if (mask)
+    RL_TRY(cudaMemcpyAsync(h->stage_mask, mask, sizeof(uint32_t) * (size_t)B * mask_stride, cudaMemcpyHostToDevice, s),
+           "rl_sample_host: copy mask");
+  RL_TRY(cudaMemcpyAsync(h->stage_params, params, sizeof(rl_row_params) * B, cudaMemcpyHostToDevice, s),
+         "rl_sample_host: copy params");
+  RL_TRY(cudaMemcpyAsync(h->stage_u, uniforms, sizeof(float) * B, cudaMemcpyHostToDevice, s),
+         "rl_sample_host: copy uniforms");
+  rl_status st = sample_common(h, h->stage_logits, RL_F32, B, V, V, hist ? h->stage_hist : nullptr,
+                               hist ? h->stage_hist_len : nullptr, hist_stride, mask ? h->stage_mask : nullptr,
+                               mask_stride, h->stage_params, h->stage_u, h->stage_tok, h->stage_prob,
+                               h->stage_status, nullptr, nullptr, nullptr, 0, s, 0);
+  if (st != RL_OK) return st;
+  RL_TRY(cudaMemcpyAsync(out_tok, h->stage_tok, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, s),
+         "rl_sample_host: copy tokens");
+  if (out_prob)
+    RL_TRY(cudaMemcpyAsync(out_prob, h->stage_prob, sizeof(float) * B, cudaMemcpyDeviceToHost, s),
+           "rl_sample_host: copy probabilities");
+  RL_TRY(cudaStreamSynchronize(s), "rl_sample_host: synchronize");
+#undef RL_TRY
+  return RL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,35 @@
+// Handle layout and workspace management shared by the C ABI sources.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "rl_sampler.h"
+
+struct rl_sampler {
+  int device = 0;
+  int max_batch = 0;
+  int max_vocab = 0;
+  int max_history = 0;
+  int num_sms = 0;
+  uint32_t flags = 0;
+  cudaStream_t stream = nullptr;  // used by the host-buffer entry points
+  // device staging buffers of rl_sample_host (allocated at create)
+  float* stage_logits = nullptr;
+  int32_t* stage_hist = nullptr;
+  int32_t* stage_hist_len = nullptr;
+  uint32_t* stage_mask = nullptr;
+  int mask_words = 0;
+  rl_row_params* stage_params = nullptr;
+  float* stage_u = nullptr;
+  int32_t* stage_tok = nullptr;
+  float* stage_prob = nullptr;
+  int32_t* stage_status = nullptr;
+};
+
+namespace rl {
+rl_status alloc_workspace(rl_sampler* h);
+void free_workspace(rl_sampler* h);
+rl_status set_error(rl_status st, const char* msg);
+void clear_error();
+}  // namespace rl

@@ -1,0 +1,48 @@
+// Device buffers owned by a sampler handle: allocated once at create, never
+// in a sampling call.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+
+#include "internal.h"
+
+namespace rl {
+
+template <typename T>
+static bool dalloc(T** p, size_t n) {
+  return cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * (n ? n : 1)) == cudaSuccess;
+}
+
+rl_status alloc_workspace(rl_sampler* h) {
+  if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return set_error(RL_ERR_CUDA, "rl_sampler_create: cudaStreamCreate failed");
+  const size_t B = static_cast<size_t>(h->max_batch);
+  h->mask_words = (h->max_vocab + 31) / 32;
+  bool ok = dalloc(&h->stage_logits, B * static_cast<size_t>(h->max_vocab)) &&
+            dalloc(&h->stage_hist, B * static_cast<size_t>(h->max_history)) &&
+            dalloc(&h->stage_hist_len, B) && dalloc(&h->stage_mask, B * h->mask_words) &&
+            dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
+            dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
+  if (!ok) {
+    cudaGetLastError();
+    return set_error(RL_ERR_OOM, "rl_sampler_create: device allocation failed");
+  }
+  return RL_OK;
+}
+
+void free_workspace(rl_sampler* h) {
+  cudaFree(h->stage_logits);
+  cudaFree(h->stage_hist);
+  cudaFree(h->stage_hist_len);
+  cudaFree(h->stage_mask);
+  cudaFree(h->stage_params);
+  cudaFree(h->stage_u);
+  cudaFree(h->stage_tok);
+  cudaFree(h->stage_prob);
+  cudaFree(h->stage_status);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  h->stage_logits = nullptr;
+  h->stream = nullptr;
+}
+
+}  // namespace rl

