@@ -757,7 +757,14 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
           w.status = RL_ERR_UNSUPPORTED;  // cutoff beyond the 64-nat window
           p.op = kPlanDone;
         } else {
-          const int bF = (mass_mode && b2 <= b1) ? min(bA + 1, min(b1, kNB - 1)) : bA;
+          int bF = (mass_mode && b2 <= b1) ? min(bA + 1, min(b1, kNB - 1)) : bA;
+          if (a.list_len) {
+            // debug: also collect the first min(K, list_cap) list entries
+            const uint32_t want = static_cast<uint32_t>(min(Klist, a.list_cap));
+            int bL = bF;
+            while (bL < kNB - 1 && cnt[bL] < want) ++bL;
+            if (cnt[bL] <= static_cast<uint32_t>(kCap)) bF = max(bF, bL);
+          }
           if (cnt[bF] <= static_cast<uint32_t>(kCap)) {
             p.lo = 0;
             p.hi = bF;
@@ -859,7 +866,7 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
               a.list_probs[static_cast<int64_t>(row) * a.list_cap + j] =
                   static_cast<float>(static_cast<double>(expf(row_l(key_val(key), rc))) / w.Z);
             }
-            if (tid == 0) a.list_len[row] = (w.K <= ncol || w.K <= a.list_cap) ? nl : -1;
+            if (tid == 0) a.list_len[row] = (nl == min(w.K, a.list_cap)) ? nl : -1;
           }
         } else {
           next_lo = next_nonempty(cnt, w.seg_hi);
