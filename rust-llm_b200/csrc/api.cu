@@ -134,10 +134,8 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   if (list_len && (!list_ids || !list_probs || list_cap <= 0))
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list buffers required");
   const int es = dtype == RL_BF16 ? 2 : 4;
-  const int C = rl::spec_pick_cluster(B, V, es, h->num_sms);
-  const int L = (((V + C - 1) / C + 127) / 128) * 128;
-  if (rl::spec_smem_bytes(L, es) > 227 * 1024)
-    return fail(RL_ERR_SHAPE, "rl_sample_batch: V=%d too large for one cluster of %d CTAs", V, C);
+  if (rl::spec_chunks(V, es) > h->ws.smax)
+    return fail(RL_ERR_SHAPE, "rl_sample_batch: V=%d beyond the handle's max_vocab", V);
   DeviceGuard g(h->device);
   if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
   rl::SpecArgs a = {};
@@ -161,7 +159,8 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.list_cap = list_cap;
   a.vocab_offset = vocab_offset;
   a.mode = rl::kModeSample;
-  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
+  a.ws = h->ws;
+  cudaError_t e = rl::launch_spec(a, dtype, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
   return RL_OK;
 }

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include "rl_sampler.h"
+#include "spec_kernel.cuh"
 
 struct rl_sampler {
   int device = 0;
@@ -25,6 +26,8 @@ struct rl_sampler {
   int32_t* stage_tok = nullptr;
   float* stage_prob = nullptr;
   int32_t* stage_status = nullptr;
+  // workspace of the chunked spec kernel (arrival counters zeroed at create)
+  rl::Workspace ws = {};
 };
 
 namespace rl {

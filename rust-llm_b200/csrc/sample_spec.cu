@@ -1,5 +1,5 @@
 // Batched spec sampling: penalties -> mask -> temperature -> softmax ->
-// top-k -> top-p -> draw, one thread-block cluster per row.
+// top-k -> top-p -> draw.
 //
 // Reference behaviour (chenyusolar/rust-llm, src/decoder.rs):
 //   temperature softmax        Decoder::sample_with_params   decoder.rs:44-55
@@ -9,20 +9,22 @@
 //   strict '<' draw            Decoder::sample_multinomial   decoder.rs:146-158
 //   empty allowed set -> all   Sampler::sample_with_grammar  decoder.rs:362-364
 //
-// Design (B200, sm_100a): the row is split over the C CTAs of a cluster; each
-// CTA pulls its slice into shared memory with bulk async copies
-// (cp.async.bulk + mbarrier): one HBM read per logit. Every later pass runs
-// out of shared memory. Cross-CTA reductions go through distributed shared
-// memory and cluster barriers; rank 0 plans and finishes:
-//   B0  mask popcount exchange (overlaps the copy)
-//   P1  max / argmax / allowed count                         -> R1 exchange
-//   P2  exact l = (x - m)/T, e = exp(l), Z partials, count and
-//       mass histograms over l (16 bins per nat, 64 nats)    -> R2, rank 0 merges
-//   P3  collect the elements of the bins rank 0 asks for into its buffer
-//       (one round in the common case, a few for very large nuclei)
-//   rank 0 sorts the collected keys (value desc, id asc), runs exact
-//   cumulative sums from the histogram prefix, finds the cutoff and the draw.
-// No global scratch memory is used.
+// Design (B200, sm_100a). One launch; the grid is (chunks, rows). Every CTA
+// streams one 64 KB chunk of one row into shared memory with bulk async
+// copies (cp.async.bulk + mbarrier) -- the only HBM read of those logits --
+// and reduces it to a small summary in the handle's workspace:
+//   P1  chunk max / lowest argmax / allowed count / per-thread maxima
+//   P2  Z partial sum of exp((x - m_c)/T) (ex2 on a split log2(e)/T), and for
+//       rows without a small top_k, count + mass histograms on an absolute
+//       bin grid (16 bins per nat)
+//   P3  candidate keys (value desc, id asc) of everything that can be in the
+//       row's top-k: x >= tau, tau = k-th largest per-thread maximum (k <= 128),
+//       or the chunk's top 512 by the histogram.
+// The last CTA of a row to finish (arrival counter) merges the summaries:
+// global max, Z, the exact top-k list (sorted keys, exact exp), the inclusive
+// top-p cutoff and the draw. Rows without a small top_k walk the merged
+// histogram bin by bin; a bin not covered by the candidate lists is re-read
+// from the (L2-resident) row.
 #include <climits>
 
 #include "common.cuh"
@@ -30,31 +32,55 @@
 
 namespace rl {
 
-// bf16 slices cannot hold a penalised f32 value in place: the slot gets this
-// NaN pattern and the value lives in a side table.
-constexpr uint16_t kBf16Marker = 0x7fc1;
+constexpr uint16_t kBf16Marker = 0x7fc1;  // bf16 slot whose penalised value is in the side table
 constexpr uint16_t kBf16NegInf = 0xff80;
+constexpr double kLog2e = 1.4426950408889634074;
 
-struct RowCtx {
-  float m;        // max allowed (penalised) logit
-  float T, rT;    // temperature and RN(1/T)
-  bool fast_div;  // Markstein division is valid for this T
+// ---------------------------------------------------------------------------
+// Row arithmetic
+// ---------------------------------------------------------------------------
+struct RowT {
+  float T, rT;       // temperature, RN(1/T)
+  bool fast_div;     // Markstein division valid for T
+  float c_hi, c_lo;  // log2(e)/T split in two floats
+  float cb;          // absolute bins per logit unit: kRbin / T
 };
 
-__device__ __forceinline__ float temp_div(float d, const RowCtx& c) {
-  if (c.fast_div && (d == 0.0f || fabsf(d) >= 8.077935669e-28f /* 2^-90 */))
-    return div_fixed(d, c.T, c.rT);
-  return div_rn(d, c.T);
+__device__ __forceinline__ RowT make_rowt(float T) {
+  RowT r;
+  r.T = T;
+  r.rT = __frcp_rn(T);
+  r.fast_div = (T >= 9.5367431640625e-07f) && (T <= 1048576.0f);
+  const double c = kLog2e / static_cast<double>(T);
+  r.c_hi = static_cast<float>(c);
+  r.c_lo = static_cast<float>(c - static_cast<double>(r.c_hi));
+  r.cb = div_rn(kRbin, T);
+  return r;
 }
-// l = (x - m) / T exactly as the CPU restatement computes it.
-__device__ __forceinline__ float row_l(float x, const RowCtx& c) { return temp_div(sub_rn(x, c.m), c); }
-__device__ __forceinline__ int bin_of(float l) {
-  const float s = -l * kRbin;  // exact: kRbin is a power of two
-  return s < static_cast<float>(kNB) ? static_cast<int>(s) : kNB;
+// l = (x - m) / T with IEEE rounding, as the CPU restatement computes it.
+__device__ __forceinline__ float exact_l(float x, float m, const RowT& r) {
+  const float d = sub_rn(x, m);
+  if (r.fast_div && (d == 0.0f || fabsf(d) >= 8.077935669e-28f)) return div_fixed(d, r.T, r.rT);
+  return div_rn(d, r.T);
+}
+__device__ __forceinline__ float exact_e(float x, float m, const RowT& r) { return expf(exact_l(x, m, r)); }
+__device__ __forceinline__ float ex2_approx(float t) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
+  return y;
+}
+// exp((x - m)/T) for bulk sums: split-constant exponent, hardware ex2.
+__device__ __forceinline__ float fast_e(float x, float m, const RowT& r) {
+  const float d = sub_rn(x, m);
+  return ex2_approx(fmaf(d, r.c_lo, d * r.c_hi));
+}
+// Absolute bin of a logit: monotone in x, identical wherever it is computed.
+__device__ __forceinline__ int babs(float x, const RowT& r) {
+  return __float2int_rd(__fmul_rn(x, r.cb));
 }
 
 // ---------------------------------------------------------------------------
-// Slice access: values of G consecutive elements per 16-byte shared load.
+// Chunk access: values of G consecutive elements per 16-byte shared load.
 // ---------------------------------------------------------------------------
 template <typename E>
 struct Slice;
@@ -76,13 +102,13 @@ template <>
 struct Slice<uint16_t> {
   static constexpr int G = 8;
   const uint16_t* data;
-  const int32_t* pen_id;  // local ids of the penalised entries (-1: duplicate)
-  const float* pen_val;   // their penalised values
+  const int32_t* pen_id;  // local ids of penalised entries (-1: duplicate)
+  const float* pen_val;
   int n_pen;
   __device__ __noinline__ float lookup(int local) const {
     for (int t = 0; t < n_pen; ++t)
       if (pen_id[t] == local) return pen_val[t];
-    return __int_as_float(0x7fffffff);  // a NaN input stays NaN
+    return __int_as_float(0x7fffffff);
   }
   __device__ __forceinline__ void load(int g, float (&v)[8]) const {
     const uint4 q = reinterpret_cast<const uint4*>(data)[g];
@@ -97,14 +123,14 @@ struct Slice<uint16_t> {
 };
 
 // ---------------------------------------------------------------------------
-// Block helpers (kNT threads)
+// Block helpers (kCT threads)
 // ---------------------------------------------------------------------------
 struct RedScratch {
-  double d[kNWarp];
-  float f[kNWarp];
-  int i[kNWarp];
-  int j[kNWarp];
-  int k[kNWarp];
+  double d[kCW];
+  float f[kCW];
+  int i[kCW];
+  int j[kCW];
+  int k[kCW];
   double bcast_d;
   int bcast_i;
   int pad;
@@ -117,27 +143,12 @@ __device__ __forceinline__ double block_sum_d(double v, RedScratch* rs) {
   if (lane == 0) rs->d[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    double t = lane < kNWarp ? rs->d[lane] : 0.0;
+    double t = lane < kCW ? rs->d[lane] : 0.0;
     t = warp_sum_d(t);
     if (lane == 0) rs->bcast_d = t;
   }
   __syncthreads();
   return rs->bcast_d;
-}
-
-__device__ __forceinline__ int block_sum_i(int v, RedScratch* rs) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum_i(v);
-  __syncthreads();
-  if (lane == 0) rs->i[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int t = lane < kNWarp ? rs->i[lane] : 0;
-    t = warp_sum_i(t);
-    if (lane == 0) rs->bcast_i = t;
-  }
-  __syncthreads();
-  return rs->bcast_i;
 }
 
 __device__ __forceinline__ int block_min_i(int v, RedScratch* rs) {
@@ -148,9 +159,24 @@ __device__ __forceinline__ int block_min_i(int v, RedScratch* rs) {
   if (lane == 0) rs->i[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    int t = lane < kNWarp ? rs->i[lane] : INT_MAX;
+    int t = lane < kCW ? rs->i[lane] : INT_MAX;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) t = min(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (lane == 0) rs->bcast_i = t;
+  }
+  __syncthreads();
+  return rs->bcast_i;
+}
+
+__device__ __forceinline__ int block_or_i(int v, RedScratch* rs) {
+  v = __any_sync(0xffffffffu, v != 0);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) rs->i[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < kCW ? rs->i[lane] : 0;
+    t = __any_sync(0xffffffffu, t != 0);
     if (lane == 0) rs->bcast_i = t;
   }
   __syncthreads();
@@ -169,28 +195,29 @@ __device__ __forceinline__ double block_scan_d(double v, RedScratch* rs, double*
   if (lane == 31) rs->d[warp] = v;
   __syncthreads();
   if (warp == 0) {
-    double t = lane < kNWarp ? rs->d[lane] : 0.0;
+    double t = lane < kCW ? rs->d[lane] : 0.0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const double n = __shfl_up_sync(0xffffffffu, t, o);
       if (lane >= o) t += n;
     }
-    if (lane < kNWarp) rs->d[lane] = t;
+    if (lane < kCW) rs->d[lane] = t;
   }
   __syncthreads();
   const double off = warp > 0 ? rs->d[warp - 1] : 0.0;
-  *total = rs->d[kNWarp - 1];
+  *total = rs->d[kCW - 1];
   return v + off;
 }
 
-// Descending bitonic sort of P (power of two, <= kCap) 64-bit keys.
-__device__ void block_sort_desc(uint64_t* s, int P) {
+// Descending bitonic sort of P (power of two) keys in shared memory.
+template <typename K>
+__device__ void block_sort_desc(K* s, int P) {
   for (int k = 2; k <= P; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += kNT) {
+      for (int i = threadIdx.x; i < P; i += kCT) {
         const int ixj = i ^ j;
         if (ixj > i) {
-          const uint64_t a = s[i], b = s[ixj];
+          const K a = s[i], b = s[ixj];
           const bool desc = (i & k) == 0;
           if (desc ? (a < b) : (a > b)) {
             s[i] = b;
@@ -203,105 +230,74 @@ __device__ void block_sort_desc(uint64_t* s, int P) {
   }
 }
 
-__device__ __forceinline__ void cluster_arrive_relaxed() {
-  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+__device__ __forceinline__ int pow2_ceil(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
 }
 
 // ---------------------------------------------------------------------------
 // Shared-memory layout
 // ---------------------------------------------------------------------------
-struct Xch {
-  float max;
-  int argmax;
-  int nallow;
-  int bad;
-  int pop;
-  int pad;
-  double z;
-};
-
-enum PlanOp : int { kPlanDone = 0, kPlanCollect = 1 };
-
-struct Plan {
-  int op;
-  int lo, hi;  // inclusive bin range
-  float x_lo, x_hi;
-};
-
 struct Ctrl {
-  int n_local;
-  int cand_count;
-  int timeout;
-  int pad;
+  int n_local;   // history entries inside the chunk
+  int ncand;     // candidate keys written
+  int is_last;
+  int mask_on;
+  int overflow;
+  int nbin;      // keys gathered for the current bin (finisher)
+  int pad[2];
 };
 
-// Rank-0 state of the walk down the ordered list.
+// Finisher walk state (rank of the row's list, masses relative to the row max).
 struct Walk {
-  int phase;        // 0: find the cutoff, 1: find the draw, 2: done
-  int K;            // list length
-  int mass_mode;    // top_p < 1
-  int fast;         // the collected segment starts at the top of the list
-  int seg_lo, seg_hi;
-  int cut_in_seg;   // the cutoff element is in the current segment
-  int cut_idx;      // its index in the sorted segment
-  long long count_before;
-  double mass_before;  // e-units above the segment
-  double Z;
-  double t2;           // top_p * Z
-  double S;            // mass through the cutoff element
-  double t3;           // u * S
+  int phase;              // 0: find the cutoff, 1: find the draw, 2: done
+  int K;                  // list length
+  int mass_mode;          // top_p < 1
+  int cut_in_seg;         // the cutoff element is in the current segment
+  int cut_idx;
+  int status;
   int token;
   float prob;
-  int status;
-  int list_done;
+  long long count_before;
+  double mass_before;
+  double Z, t2, S, t3;
 };
 
 constexpr int kOffMbar = 0;
-constexpr int kOffXch = 128;
-constexpr int kOffPlan = kOffXch + kCmax * static_cast<int>(sizeof(Xch));
-constexpr int kOffCtrl = kOffPlan + 64;
-constexpr int kOffWalk = kOffCtrl + 64;
-constexpr int kOffRed = kOffWalk + 256;
-constexpr int kOffCnt = 2048;
-constexpr int kOffMass = kOffCnt + kNB * 4;
-constexpr int kOffCand = kOffMass + kNB * 8;
-constexpr int kOffHist = kOffCand + kCap * 8;
-constexpr int kOffPen = kOffHist + kHmax * 4;
-constexpr int kOffData = kOffPen + kHmax * 4;
-static_assert(sizeof(Walk) <= 256, "walk state");
-static_assert(kOffRed + sizeof(RedScratch) <= kOffCnt, "smem header overflow");
-static_assert(kOffData % 128 == 0, "data alignment");
+constexpr int kOffCtrl = 64;
+constexpr int kOffWalk = 128;
+constexpr int kOffRed = 256;
+constexpr int kOffTmax = 1024;                 // kCT floats
+constexpr int kOffCnt = kOffTmax + kCT * 4;    // kNB u32 / finisher: kNB doubles (counts)
+constexpr int kOffMass = kOffCnt + kNB * 8;    // kNB u64 / finisher: kNB doubles (masses)
+constexpr int kOffHist = kOffMass + kNB * 8;   // kHmax ints
+constexpr int kOffPen = kOffHist + kHmax * 4;  // kHmax floats
+constexpr int kOffSums = kOffPen + kHmax * 4;  // kSmax ChunkSum (finisher)
+constexpr int kOffData = ((kOffSums + kSmax * static_cast<int>(sizeof(ChunkSum)) + 127) / 128) * 128;
+static_assert(sizeof(Walk) <= 128, "walk");
+static_assert(kOffRed + sizeof(RedScratch) <= kOffTmax, "smem header");
 
-int spec_smem_bytes(int L, int es) { return kOffData + L * es; }
-
-// Conservative x-range of the bins [lo, hi]; the exact bin test follows.
-__device__ __forceinline__ void plan_bounds(Plan& p, float m, float T) {
-  p.x_lo = m - T * (static_cast<float>(p.hi + 1) / kRbin) * 1.001f - 1e-30f;
-  p.x_hi = p.lo == 0 ? RL_POS_INF : m - T * (static_cast<float>(p.lo) / kRbin) * 0.999f + 1e-30f;
+int spec_smem_bytes(int /*es*/) { return kOffData + kChunkBytes; }
+int spec_chunks(int V, int es) {
+  const int ce = kChunkBytes / es;
+  return (V + ce - 1) / ce;
 }
 
-// First nonempty bin after `b` (cumulative counts in cnt), kNB if none.
-__device__ __forceinline__ int next_nonempty(const uint32_t* cnt, int b) {
-  for (int q = b + 1; q < kNB; ++q)
-    if (cnt[q] > cnt[q - 1]) return q;
-  return kNB;
-}
-
-// Sweep over the sorted segment: first index j whose running cumulative mass
-// (mass_before + e_0 + ... + e_j) satisfies the condition. mode 0: cutoff
-// (list position K-1, or cum >= t2 when mass_mode); mode 1: cum > t3.
-// Returns INT_MAX if none; *cum_at receives the cumulative mass at j.
-__device__ int sweep_segment(const uint64_t* cand, int n, const Walk& w, const RowCtx& rc,
-                             int mode, RedScratch* rs, double* cum_at) {
+// ---------------------------------------------------------------------------
+// Finisher pieces
+// ---------------------------------------------------------------------------
+// Sweep over n sorted keys: first index j whose cumulative mass
+// (w.mass_before + e_0 + ... + e_j, e exact) meets the condition. mode 0:
+// cutoff (list position K-1, or cum >= t2 in mass mode); mode 1: cum > t3.
+__device__ int sweep(const uint64_t* keys, int n, const Walk& w, float m, const RowT& rt, int mode,
+                     RedScratch* rs, double* cum_at) {
   double run = w.mass_before;
-  for (int c0 = 0; c0 < n; c0 += kNT) {
+  for (int c0 = 0; c0 < n; c0 += kCT) {
     const int j = c0 + threadIdx.x;
     const bool valid = j < n;
     float e = 0.0f;
-    if (valid) e = expf(row_l(key_val(cand[j]), rc));
+    if (valid) e = exact_e(key_val(keys[j]), m, rt);
     double tot;
     const double cum = run + block_scan_d(static_cast<double>(e), rs, &tot);
     bool cond = false;
@@ -324,46 +320,61 @@ __device__ int sweep_segment(const uint64_t* cand, int n, const Walk& w, const R
   return INT_MAX;
 }
 
+// Penalised value of history id `id` from the finisher's sorted history
+// table (ids hid[0..nh), values hval), or `x` if not in the history.
+__device__ __forceinline__ float hist_value(float x, int id, const int32_t* hid, const float* hval, int nh) {
+  int lo = 0, hi = nh - 1;
+  while (lo <= hi) {
+    const int mid = (lo + hi) >> 1;
+    const int v = hid[mid];
+    if (v == id) return hval[mid];
+    if (v < id) lo = mid + 1;
+    else hi = mid - 1;
+  }
+  return x;
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 template <typename E>
-__global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
+__global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster_arrive_relaxed();  // matched by cluster_wait() before the first DSMEM access
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int C = static_cast<int>(cluster.num_blocks());
+  const int chunk = blockIdx.x;
   const int row = blockIdx.y;
+  const int S = gridDim.x;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
 
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + kOffMbar);
-  Xch* xch = reinterpret_cast<Xch*>(smem + kOffXch);
-  Plan* plan = reinterpret_cast<Plan*>(smem + kOffPlan);
   Ctrl* ctrl = reinterpret_cast<Ctrl*>(smem + kOffCtrl);
   Walk* wk = reinterpret_cast<Walk*>(smem + kOffWalk);
   RedScratch* rs = reinterpret_cast<RedScratch*>(smem + kOffRed);
+  float* tmax = reinterpret_cast<float*>(smem + kOffTmax);
   uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt);
   unsigned long long* mass = reinterpret_cast<unsigned long long*>(smem + kOffMass);
-  uint64_t* cand = reinterpret_cast<uint64_t*>(smem + kOffCand);
   int32_t* hist_local = reinterpret_cast<int32_t*>(smem + kOffHist);
   float* pen_val = reinterpret_cast<float*>(smem + kOffPen);
+  ChunkSum* sums_s = reinterpret_cast<ChunkSum*>(smem + kOffSums);
   E* data = reinterpret_cast<E*>(smem + kOffData);
 
-  const int L = a.L;
   const int V = a.V;
-  const int start = rank * L;
-  const int len = max(0, min(L, V - start));
+  const int CE = a.chunk_elems;
+  const int start = chunk * CE;
+  const int len = max(0, min(CE, V - start));
   constexpr int es = static_cast<int>(sizeof(E));
   constexpr int G = Slice<E>::G;
-  const int ngroups = L / G;
+  const int ngroups = CE / G;
+  const Workspace& ws = a.ws;
 
   const rl_row_params prm = a.params[row];
-  const float u = a.uniforms[row];
+  const float T = prm.temperature;
+  const bool greedy = !(T > 0.0f);  // also NaN: reported as non-finite by the finisher
+  const bool thr_path = prm.top_k > 0 && prm.top_k <= kKthr;
+  const bool hist_path = !greedy && !thr_path;
 
-  // ---- prologue: mbarriers, bulk copy of the slice ----
+  // ---- prologue: mbarriers, bulk copy ----
   const E* src = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start;
   const uint32_t bulk_bytes = static_cast<uint32_t>(len * es) & ~15u;
   const bool use_bulk = ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) && bulk_bytes > 0;
@@ -371,13 +382,14 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
     for (int p = 0; p < kNPiece; ++p) mbar_init(&mbar[p], 1);
     fence_mbar_init();
     ctrl->n_local = 0;
-    ctrl->cand_count = 0;
-    ctrl->timeout = 0;
+    ctrl->ncand = 0;
+    ctrl->overflow = 0;
   }
-  for (int b = tid; b < kNB; b += kNT) {
-    cnt[b] = 0u;
-    mass[b] = 0ull;
-  }
+  if (hist_path)
+    for (int b = tid; b < kNB; b += kCT) {
+      cnt[b] = 0u;
+      mass[b] = 0ull;
+    }
   __syncthreads();
   if (tid == 0 && use_bulk) {
     const uint32_t piece = ((bulk_bytes / kNPiece) + 15u) & ~15u;
@@ -392,64 +404,57 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
     }
   }
 
-  // history ids inside this slice (local index), overlapping the copy
+  // history ids inside this chunk, overlapping the copy
   const int vstart = a.vocab_offset + start;
   int hl = a.hist ? a.hist_len[row] : 0;
   hl = max(0, min(hl, min(a.hist_stride, kHmax)));
-  for (int j = tid; j < hl; j += kNT) {
+  for (int j = tid; j < hl; j += kCT) {
     const int h = a.hist[static_cast<int64_t>(row) * a.hist_stride + j];
     const int loc = h - vstart;
-    if (h >= a.vocab_offset && loc >= 0 && loc < len) {
-      const int idx = atomicAdd(&ctrl->n_local, 1);
-      hist_local[idx] = loc;
-    }
+    if (h >= a.vocab_offset && loc >= 0 && loc < len) hist_local[atomicAdd(&ctrl->n_local, 1)] = loc;
   }
-  // mask popcount over this slice (ids < V only)
-  int pop = 0;
+  // does the row's mask allow anything? (an all-zero mask allows every id)
   const uint32_t* mrow = a.mask ? a.mask + static_cast<int64_t>(row) * a.mask_stride : nullptr;
+  int mask_on = 0;
   if (mrow) {
-    const int w0 = start >> 5;
-    const int nw = (len + 31) >> 5;
-    for (int w = tid; w < nw; w += kNT) {
-      uint32_t bits = mrow[w0 + w];
-      const int rem = len - w * 32;
-      if (rem < 32) bits &= (1u << rem) - 1u;
-      pop += __popc(bits);
+    const int nw = (V + 31) >> 5;
+    int any = 0;
+    for (int w0 = 0; w0 < nw && !any; w0 += kCT) {
+      const int w = w0 + tid;
+      uint32_t bits = 0u;
+      if (w < nw) {
+        bits = mrow[w];
+        const int rem = V - w * 32;
+        if (rem < 32) bits &= (1u << rem) - 1u;
+      }
+      any = block_or_i(bits != 0u, rs);
     }
-  }
-  pop = block_sum_i(pop, rs);
-  cluster_wait();  // every CTA of the cluster has started
-  if (tid < C) cluster.map_shared_rank(&xch[rank], tid)->pop = pop;
-  cluster.sync();  // B0
-  bool mask_on = false;
-  if (mrow) {
-    int tot = 0;
-    for (int r = 0; r < C; ++r) tot += xch[r].pop;
-    mask_on = tot > 0;
+    mask_on = any;
   }
 
-  // ---- wait for the slice; unaligned remainder; pad the tail ----
+  // ---- wait for the chunk, unaligned remainder, tail padding ----
+  int timed_out = 0;
   if (use_bulk) {
     bool ok = true;
     for (int p = 0; p < kNPiece; ++p) ok &= mbar_wait(&mbar[p], 0, kWaitBudget);
-    if (!ok) ctrl->timeout = 1;
+    timed_out = !ok;
   }
   {
     const int first_plain = use_bulk ? static_cast<int>(bulk_bytes / es) : 0;
-    for (int i = first_plain + tid; i < len; i += kNT) data[i] = src[i];
+    for (int i = first_plain + tid; i < len; i += kCT) data[i] = src[i];
     E neg;
     if constexpr (sizeof(E) == 4) {
       neg = RL_NEG_INF;
     } else {
       neg = kBf16NegInf;
     }
-    for (int i = len + tid; i < L; i += kNT) data[i] = neg;
+    for (int i = len + tid; i < CE; i += kCT) data[i] = neg;
   }
   __syncthreads();
 
-  // ---- penalties on this slice's history ids (first occurrence applies) ----
+  // ---- penalties (first occurrence of an id applies them) ----
   const int n_local = min(ctrl->n_local, kHmax);
-  for (int t = tid; t < n_local; t += kNT) {
+  for (int t = tid; t < n_local; t += kCT) {
     const int h = hist_local[t];
     int c = 0;
     bool first = true;
@@ -467,8 +472,7 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
         v = bf16_bits_to_f32(data[h]);
       }
       const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
-      const float x2 = sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty));
-      const float x3 = sub_rn(x2, prm.presence_penalty);
+      const float x3 = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
       if constexpr (sizeof(E) == 4) {
         data[h] = x3;
       } else {
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
   Slice<E> sl;
   sl.data = data;
   if constexpr (sizeof(E) == 2) {
-    for (int t = tid; t < n_local; t += kNT) {
+    for (int t = tid; t < n_local; t += kCT) {
       const int h = hist_local[t];
       bool first = true;
       for (int j = 0; j < t; ++j)
@@ -488,7 +492,7 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
       if (first) data[h] = kBf16Marker;
     }
     __syncthreads();
-    for (int t = tid; t < n_local; t += kNT) {
+    for (int t = tid; t < n_local; t += kCT) {
       const int h = hist_local[t];
       bool first = true;
       for (int j = 0; j < t; ++j)
@@ -500,33 +504,51 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
     sl.pen_val = pen_val;
     sl.n_pen = n_local;
   }
+  // masked ids -> -inf in place
+  if (mask_on) {
+    for (int g = tid; g < ngroups; g += kCT) {
+      const int id0 = start + g * G;
+      const uint32_t bits = id0 < V ? (mrow[id0 >> 5] >> (id0 & 31)) : 0u;
+#pragma unroll
+      for (int k = 0; k < G; ++k) {
+        if (!((bits >> k) & 1u)) {
+          if constexpr (sizeof(E) == 4) {
+            data[g * G + k] = RL_NEG_INF;
+          } else {
+            data[g * G + k] = kBf16NegInf;
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
 
-  // ---- P1: max / lowest argmax / allowed count / non-finite ----
+  // ---- P1: chunk max / lowest argmax / allowed count / non-finite; thread maxima ----
   float mx = RL_NEG_INF;
   int amx = INT_MAX;
   int nallow = 0;
   int bad = 0;
-  for (int g = tid; g < ngroups; g += kNT) {
+  for (int g = tid; g < ngroups; g += kCT) {
     float v[G];
     sl.load(g, v);
-    uint32_t bits = 0xffffffffu;
-    if (mask_on) bits = (start + g * G < V) ? (mrow[(start + g * G) >> 5] >> ((g * G) & 31)) : 0u;
 #pragma unroll
     for (int k = 0; k < G; ++k) {
       const float x = v[k];
-      const bool on = (bits >> k) & 1u;
-      if (on && x > RL_NEG_INF) {
+      if (x > RL_NEG_INF) {
         if (!(x < RL_POS_INF)) bad = 1;
         ++nallow;
         if (x > mx) {
           mx = x;
           amx = g * G + k;
         }
-      } else if (on && x != x) {
+      } else if (x != x) {
         bad = 1;
       }
     }
   }
+  tmax[tid] = mx;
+  float m_c;
+  int argmax_c, nallow_c, bad_c;
   {
     const float wm = warp_max(mx);
     int wa = (mx == wm) ? amx : INT_MAX;
@@ -542,456 +564,547 @@ __global__ void __launch_bounds__(kNT, 2) spec_sample_kernel(const SpecArgs a) {
       rs->k[warp] = wb;
     }
     __syncthreads();
-    if (tid == 0) {
-      float bm = RL_NEG_INF;
-      int ba = INT_MAX, bn = 0, bb = 0;
-      for (int w = 0; w < kNWarp; ++w) {
-        bn += rs->j[w];
-        bb |= rs->k[w] ? 1 : 0;
-        if (rs->f[w] > bm) {
-          bm = rs->f[w];
-          ba = rs->i[w];
-        } else if (rs->f[w] == bm) {
-          ba = min(ba, rs->i[w]);
+    float bm = RL_NEG_INF;
+    int ba = INT_MAX, bn = 0, bb = 0;
+    for (int w = 0; w < kCW; ++w) {
+      bn += rs->j[w];
+      bb |= rs->k[w];
+      if (rs->f[w] > bm) {
+        bm = rs->f[w];
+        ba = rs->i[w];
+      } else if (rs->f[w] == bm) {
+        ba = min(ba, rs->i[w]);
+      }
+    }
+    m_c = bm;
+    argmax_c = ba == INT_MAX ? INT_MAX : ba + start;
+    nallow_c = bn;
+    bad_c = bb ? 1 : 0;
+  }
+
+  double z_c = 0.0;
+  int babs_m = 0;
+  int athr = INT_MIN;
+  float tau = RL_NEG_INF;
+  const RowT rt = make_rowt(greedy ? 1.0f : T);
+  if (!greedy && nallow_c > 0 && !bad_c) {
+    babs_m = babs(m_c, rt);
+    // ---- P2: Z partial (+ histograms) ----
+    float zsum = 0.0f;
+    for (int g = tid; g < ngroups; g += kCT) {
+      float v[G];
+      sl.load(g, v);
+#pragma unroll
+      for (int k = 0; k < G; ++k) {
+        const float x = v[k];
+        if (x > RL_NEG_INF) {
+          const float e = fast_e(x, m_c, rt);
+          zsum += e;
+          if (hist_path) {
+            const int b = babs_m - babs(x, rt);
+            if (b < kNB) {
+              atomicAdd(&cnt[b], 1u);
+              atomicAdd(&mass[b], __float2ull_rn(e * kMassScaleF));
+            }
+          }
         }
       }
-      rs->f[0] = bm;
-      rs->i[0] = ba == INT_MAX ? INT_MAX : ba + start;
-      rs->j[0] = bn;
-      rs->k[0] = bb | (ctrl->timeout ? 2 : 0);
     }
-    __syncthreads();
-    if (tid < C) {
-      Xch* dst = cluster.map_shared_rank(&xch[rank], tid);
-      dst->max = rs->f[0];
-      dst->argmax = rs->i[0];
-      dst->nallow = rs->j[0];
-      dst->bad = rs->k[0];
+    z_c = block_sum_d(static_cast<double>(zsum), rs);
+    // ---- collection threshold ----
+    if (thr_path) {
+      // k-th largest per-thread maximum: a lower bound of the chunk's k-th value
+      block_sort_desc(tmax, kCT);
+      tau = tmax[prm.top_k - 1];
+      if (!(tau > RL_NEG_INF)) tau = -3.402823466e38f;  // fewer than k threads hold a value: keep all
+    } else {
+      // first bin whose cumulative count reaches kKbig
+      uint32_t c0 = cnt[2 * tid], c1 = cnt[2 * tid + 1];
+      double tot;
+      const double incl = block_scan_d(static_cast<double>(c0 + c1), rs, &tot);
+      const double excl = incl - static_cast<double>(c0 + c1);
+      int bfound = INT_MAX;
+      if (excl < kKbig && excl + c0 >= kKbig) bfound = 2 * tid;
+      else if (excl + c0 < kKbig && incl >= kKbig) bfound = 2 * tid + 1;
+      bfound = block_min_i(bfound, rs);
+      if (bfound == INT_MAX) {
+        // fewer than kKbig elements in the window: keep the window, and all
+        // of the chunk when nothing lies below it
+        athr = (static_cast<int>(tot) >= nallow_c) ? INT_MIN : babs_m - (kNB - 1);
+      } else {
+        athr = babs_m - bfound;
+      }
+    }
+    // ---- P3: candidate keys into the workspace ----
+    uint64_t* cdst = ws.cands + (static_cast<int64_t>(row) * ws.smax + chunk) * kCapC;
+    for (int gb = warp * 32; gb < ngroups; gb += kCT) {
+      const int g = gb + lane;
+      float v[G];
+      bool anyt = false;
+      if (g < ngroups) {
+        sl.load(g, v);
+#pragma unroll
+        for (int k = 0; k < G; ++k) {
+          const bool t = thr_path ? (v[k] >= tau) : (v[k] > RL_NEG_INF && babs(v[k], rt) >= athr);
+          anyt |= t && (v[k] > RL_NEG_INF);
+        }
+      }
+      if (!__any_sync(0xffffffffu, anyt)) continue;
+#pragma unroll
+      for (int k = 0; k < G; ++k) {
+        bool take = false;
+        if (anyt) {
+          const float x = v[k];
+          take = x > RL_NEG_INF && (thr_path ? (x >= tau) : (babs(x, rt) >= athr));
+        }
+        const uint32_t bal = __ballot_sync(0xffffffffu, take);
+        if (bal) {
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&ctrl->ncand, __popc(bal));
+          base = __shfl_sync(0xffffffffu, base, 0);
+          if (take) {
+            const int idx = base + __popc(bal & ((1u << lane) - 1u));
+            if (idx < kCapC) cdst[idx] = cand_key(v[k], static_cast<uint32_t>(start + g * G + k));
+          }
+        }
+      }
+    }
+    if (hist_path) {
+      uint32_t* gc = ws.hcnt + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
+      unsigned long long* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
+      for (int b = tid; b < kNB; b += kCT) {
+        gc[b] = cnt[b];
+        gm[b] = mass[b];
+      }
     }
   }
-  cluster.sync();  // R1
+  __syncthreads();
+  if (tid == 0) {
+    ChunkSum s;
+    s.m = m_c;
+    s.argmax = argmax_c;
+    s.nallow = nallow_c;
+    s.flags = bad_c | (timed_out ? 2 : 0) | (ctrl->ncand > kCapC ? 4 : 0);
+    s.z = z_c;
+    s.ncand = min(ctrl->ncand, kCapC);
+    s.babs_m = babs_m;
+    s.athr = athr;
+    s.tau = tau;
+    ws.sums[static_cast<int64_t>(row) * ws.smax + chunk] = s;
+    __threadfence();
+    const int prev = atomicAdd(&ws.row_done[row], 1);
+    ctrl->is_last = prev == S - 1;
+  }
+  __syncthreads();
+  if (timed_out) {
+    // never leave with a copy still landing in this CTA's shared memory
+    for (int p = 0; p < kNPiece; ++p) mbar_wait(&mbar[p], 0, kWaitBudget);
+  }
+  if (!ctrl->is_last) return;
+
+  // =====================================================================
+  // Finisher: the last CTA of the row
+  // =====================================================================
+  __threadfence();
+  if (tid < S) {
+    const ChunkSum* src_s = ws.sums + static_cast<int64_t>(row) * ws.smax + tid;
+    ChunkSum s;
+    s.m = __ldcg(&src_s->m);
+    s.argmax = __ldcg(&src_s->argmax);
+    s.nallow = __ldcg(&src_s->nallow);
+    s.flags = __ldcg(&src_s->flags);
+    s.z = __ldcg(&src_s->z);
+    s.ncand = __ldcg(&src_s->ncand);
+    s.babs_m = __ldcg(&src_s->babs_m);
+    s.athr = __ldcg(&src_s->athr);
+    s.tau = __ldcg(&src_s->tau);
+    sums_s[tid] = s;
+  }
+  __syncthreads();
   float m = RL_NEG_INF;
-  int gargmax = INT_MAX;
-  int gallow = 0;
-  int gbad = 0;
-  for (int r = 0; r < C; ++r) {
-    const Xch& s = xch[r];
+  int gargmax = INT_MAX, gallow = 0, gflags = 0;
+  int athr_max = INT_MIN;
+  for (int c = 0; c < S; ++c) {
+    const ChunkSum& s = sums_s[c];
     gallow += s.nallow;
-    gbad |= s.bad;
-    if (s.max > m) {
-      m = s.max;
+    gflags |= s.flags;
+    athr_max = max(athr_max, s.athr);
+    if (s.m > m) {
+      m = s.m;
       gargmax = s.argmax;
-    } else if (s.max == m) {
+    } else if (s.m == m) {
       gargmax = min(gargmax, s.argmax);
     }
   }
-  const float T = prm.temperature;
   int row_st = 0;
-  if (gbad & 2)
-    row_st = RL_ERR_TIMEOUT;
-  else if (gbad || gallow == 0 || !(fabsf(T) < RL_POS_INF))
-    row_st = RL_ERR_NONFINITE;
-  if (row_st != 0 || T <= 0.0f) {
-    // greedy row (T <= 0) or invalid row: decided identically in every CTA
-    if (rank == 0 && tid == 0) {
+  if (gflags & 2) row_st = RL_ERR_TIMEOUT;
+  else if ((gflags & 1) || gallow == 0 || !(fabsf(T) < RL_POS_INF)) row_st = RL_ERR_NONFINITE;
+  else if (gflags & 4) row_st = RL_ERR_UNSUPPORTED;
+
+  auto finish = [&](int status, int token, float prob) {
+    if (tid == 0) {
+      const bool ok = status == 0;
+      a.out_tok[row] = ok ? token + a.vocab_offset : -1;
+      if (a.out_prob) a.out_prob[row] = ok ? prob : 0.0f;
+      if (a.row_status) a.row_status[row] = status;
+      ws.row_done[row] = 0;  // ready for the next launch
+    }
+  };
+
+  if (row_st != 0 || greedy) {
+    finish(row_st, gargmax, 1.0f);
+    if (a.list_len && tid == 0) {
       const bool ok = row_st == 0;
-      a.out_tok[row] = ok ? gargmax + a.vocab_offset : -1;
-      if (a.out_prob) a.out_prob[row] = ok ? 1.0f : 0.0f;
-      if (a.row_status) a.row_status[row] = row_st;
-      if (a.list_len) {
-        a.list_len[row] = (ok && a.list_cap > 0) ? 1 : 0;
-        if (ok && a.list_cap > 0) {
-          a.list_ids[static_cast<int64_t>(row) * a.list_cap] = gargmax + a.vocab_offset;
-          a.list_probs[static_cast<int64_t>(row) * a.list_cap] = 1.0f;
-        }
+      a.list_len[row] = (ok && a.list_cap > 0) ? 1 : 0;
+      if (ok && a.list_cap > 0) {
+        a.list_ids[static_cast<int64_t>(row) * a.list_cap] = gargmax + a.vocab_offset;
+        a.list_probs[static_cast<int64_t>(row) * a.list_cap] = 1.0f;
       }
     }
     return;
   }
 
-  // masked ids -> -inf in place, so that the later passes need no mask
-  if (mask_on) {
-    for (int g = tid; g < ngroups; g += kNT) {
-      const uint32_t bits =
-          (start + g * G < V) ? (mrow[(start + g * G) >> 5] >> ((g * G) & 31)) : 0u;
-#pragma unroll
-      for (int k = 0; k < G; ++k) {
-        if (!((bits >> k) & 1u)) {
-          if constexpr (sizeof(E) == 4) {
-            data[g * G + k] = RL_NEG_INF;
-          } else {
-            data[g * G + k] = kBf16NegInf;
-          }
-        }
-      }
-    }
-    __syncthreads();
-  }
-
-  RowCtx rc;
-  rc.m = m;
-  rc.T = T;
-  rc.rT = __frcp_rn(T);
-  rc.fast_div = (T >= 9.5367431640625e-07f) && (T <= 1048576.0f);
-  const int Klist = (prm.top_k > 0 && prm.top_k < gallow) ? prm.top_k : gallow;
-  const bool need_q1 = Klist < gallow;
+  // Z = sum_c z_c * 2^((m_c - m) log2(e) / T)
+  double zpart = 0.0;
+  if (tid < S && sums_s[tid].nallow > 0)
+    zpart = sums_s[tid].z * exp2((static_cast<double>(sums_s[tid].m) - static_cast<double>(m)) *
+                                 (kLog2e / static_cast<double>(T)));
+  const double Z = block_sum_d(zpart, rs);
+  const float u = a.uniforms[row];
+  const int K = (prm.top_k > 0 && prm.top_k < gallow) ? prm.top_k : gallow;
   const bool mass_mode = prm.top_p < 1.0f;
-  const bool want_mass = mass_mode || !need_q1;
-
-  // ---- P2: Z partials, count and mass histograms over l ----
-  float zsum = 0.0f;
-  for (int g = tid; g < ngroups; g += kNT) {
-    float v[G];
-    sl.load(g, v);
-#pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const float x = v[k];
-      if (x > RL_NEG_INF) {
-        const float l = row_l(x, rc);
-        const float e = expf(l);
-        zsum += e;
-        const int b = bin_of(l);
-        if (b < kNB) {
-          atomicAdd(&cnt[b], 1u);
-          if (want_mass) atomicAdd(&mass[b], __float2ull_rn(e * kMassScaleF));
-        }
-      }
-    }
-  }
-  {
-    const double zb = block_sum_d(static_cast<double>(zsum), rs);
-    if (tid == 0) cluster.map_shared_rank(&xch[rank], 0)->z = zb;
-  }
-  cluster.sync();  // R2
-
-  // ---- rank 0: merge histograms, first plan ----
-  if (rank == 0) {
-    double Z = 0.0;
-    for (int r = 0; r < C; ++r) Z += xch[r].z;
-    for (int b = tid; b < kNB; b += kNT) {
-      uint32_t c = cnt[b];
-      unsigned long long ms = mass[b];
-      for (int r = 1; r < C; ++r) {
-        c += *cluster.map_shared_rank(&cnt[b], r);
-        if (want_mass) ms += *cluster.map_shared_rank(&mass[b], r);
-      }
-      cnt[b] = c;
-      mass[b] = ms;
-    }
-    __syncthreads();
-    // inclusive prefix sums over the bins (kPer consecutive bins per thread)
-    constexpr int kPer = kNB / kNT;
-    uint32_t cc[kPer];
-    unsigned long long mm[kPer];
-    uint32_t csum = 0;
-    unsigned long long msum = 0;
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      csum += cnt[tid * kPer + q];
-      msum += mass[tid * kPer + q];
-      cc[q] = csum;
-      mm[q] = msum;
-    }
-    double ctot, mtot;
-    // doubles hold these integers exactly (counts < 2^31, masses < 2^53)
-    const double cpre = block_scan_d(static_cast<double>(csum), rs, &ctot) - static_cast<double>(csum);
-    const double mpre = block_scan_d(static_cast<double>(msum), rs, &mtot) - static_cast<double>(msum);
-#pragma unroll
-    for (int q = 0; q < kPer; ++q) {
-      cnt[tid * kPer + q] = cc[q] + static_cast<uint32_t>(cpre);
-      mass[tid * kPer + q] = mm[q] + static_cast<unsigned long long>(mpre);
-    }
-    __syncthreads();
-    // cnt / mass now hold inclusive cumulative counts / masses.
-    const double t2 = static_cast<double>(prm.top_p) * Z;
-    const double t2q = t2 * kMassScale;
-    const double t3z = static_cast<double>(u) * Z;  // draw target when the list is everything
-    const double t3zq = t3z * kMassScale;
-    int b1 = kNB, b2 = kNB, b3 = kNB;
-    for (int b = tid; b < kNB; b += kNT) {
-      const uint32_t pc = b ? cnt[b - 1] : 0u;
-      if (cnt[b] >= static_cast<uint32_t>(Klist) && pc < static_cast<uint32_t>(Klist)) b1 = b;
-      const double pm = b ? static_cast<double>(mass[b - 1]) : 0.0;
-      const double cm = static_cast<double>(mass[b]);
-      if (mass_mode && cm >= t2q && pm < t2q) b2 = b;
-      if (cm > t3zq && pm <= t3zq) b3 = b;
-    }
-    b1 = block_min_i(b1, rs);
-    b2 = block_min_i(b2, rs);
-    b3 = block_min_i(b3, rs);
-    if (tid == 0) {
-      Walk& w = *wk;
-      w.K = Klist;
-      w.mass_mode = mass_mode;
-      w.Z = Z;
-      w.t2 = t2;
-      w.S = 0.0;
-      w.t3 = 0.0;
-      w.status = 0;
-      w.token = -1;
-      w.prob = 0.0f;
-      w.cut_in_seg = 0;
-      w.cut_idx = -1;
-      w.list_done = 0;
-      Plan p;
-      p.op = kPlanCollect;
-      if (!need_q1 && !mass_mode) {
-        // the list is every allowed id: the cutoff is its end, S = Z
-        w.phase = 1;
-        w.S = Z;
-        w.t3 = t3z;
-        if (b3 >= kNB) {
-          w.status = RL_ERR_UNSUPPORTED;  // draw beyond the 64-nat window
-          p.op = kPlanDone;
-        } else if (cnt[b3] <= static_cast<uint32_t>(kCap)) {
-          p.lo = 0;
-          p.hi = b3;
-        } else {
-          p.lo = b3;
-          p.hi = b3;
-        }
-      } else {
-        w.phase = 0;
-        const int bA = min(b1, b2);
-        if (bA >= kNB) {
-          w.status = RL_ERR_UNSUPPORTED;  // cutoff beyond the 64-nat window
-          p.op = kPlanDone;
-        } else {
-          int bF = (mass_mode && b2 <= b1) ? min(bA + 1, min(b1, kNB - 1)) : bA;
-          if (a.list_len) {
-            // debug: also collect the first min(K, list_cap) list entries
-            const uint32_t want = static_cast<uint32_t>(min(Klist, a.list_cap));
-            int bL = bF;
-            while (bL < kNB - 1 && cnt[bL] < want) ++bL;
-            if (cnt[bL] <= static_cast<uint32_t>(kCap)) bF = max(bF, bL);
-          }
-          if (cnt[bF] <= static_cast<uint32_t>(kCap)) {
-            p.lo = 0;
-            p.hi = bF;
-          } else {
-            p.lo = bA;
-            p.hi = bA;
-          }
-        }
-      }
-      if (p.op == kPlanCollect) {
-        const uint32_t pop_lo = cnt[p.hi] - (p.lo ? cnt[p.lo - 1] : 0u);
-        if (pop_lo > static_cast<uint32_t>(kCap)) {
-          w.status = RL_ERR_UNSUPPORTED;  // one bin holds more than the buffer
-          p.op = kPlanDone;
-        }
-      }
-      w.fast = p.lo == 0;
-      w.seg_lo = p.lo;
-      w.seg_hi = p.hi;
-      w.count_before = p.lo ? cnt[p.lo - 1] : 0;
-      w.mass_before = p.lo ? static_cast<double>(mass[p.lo - 1]) / kMassScale : 0.0;
-      plan_bounds(p, m, T);
-      ctrl->cand_count = 0;
-      for (int r = 0; r < C; ++r) *cluster.map_shared_rank(plan, r) = p;
-    }
-  }
-
-  // ---- collection rounds (uniform across the cluster) ----
-  for (int round = 0;; ++round) {
-    cluster.sync();  // plan visible everywhere
-    const Plan p = *plan;
-    if (p.op == kPlanDone) break;
-    int* rcount = cluster.map_shared_rank(&ctrl->cand_count, 0);
-    uint64_t* rcand = cluster.map_shared_rank(cand, 0);
-    for (int gb = warp * 32; gb < ngroups; gb += kNT) {
-      const int g = gb + lane;
-      float v[G];
-      if (g < ngroups) {
-        sl.load(g, v);
-      } else {
-#pragma unroll
-        for (int k = 0; k < G; ++k) v[k] = RL_NEG_INF;
-      }
-#pragma unroll
-      for (int k = 0; k < G; ++k) {
-        const float x = v[k];
-        bool take = false;
-        if (x >= p.x_lo && x <= p.x_hi && x > RL_NEG_INF) {
-          const int b = bin_of(row_l(x, rc));
-          take = b >= p.lo && b <= p.hi;
-        }
-        const uint32_t bal = __ballot_sync(0xffffffffu, take);
-        if (bal) {
-          int base = 0;
-          if (lane == 0) base = atomicAdd(rcount, __popc(bal));
-          base = __shfl_sync(0xffffffffu, base, 0);
-          if (take) {
-            const int idx = base + __popc(bal & ((1u << lane) - 1u));
-            if (idx < kCap) rcand[idx] = cand_key(x, static_cast<uint32_t>(start + g * G + k));
-          }
-        }
-      }
-    }
-    cluster.sync();  // collected
-    if (rank != 0) continue;
-
-    // ---- rank 0: sort and walk the collected segment ----
+  uint64_t* keys = reinterpret_cast<uint64_t*>(data);  // the chunk is no longer needed
+  if (tid == 0) {
     Walk& w = *wk;
-    const int ncol = ctrl->cand_count;
-    int next_lo = -1;  // >= 0: collect this single bin next
-    if (ncol > kCap) {
-      if (tid == 0) w.status = RL_ERR_UNSUPPORTED;
-    } else if (ncol > 0) {
-      int P = 1;
-      while (P < ncol) P <<= 1;
-      for (int i = ncol + tid; i < P; i += kNT) cand[i] = 0ull;
-      __syncthreads();
-      block_sort_desc(cand, P);
-      double cum_at = 0.0;
-      if (w.phase == 0) {
-        const int f = sweep_segment(cand, ncol, w, rc, 0, rs, &cum_at);
-        if (f != INT_MAX) {
-          if (tid == 0) {
-            w.cut_in_seg = 1;
-            w.cut_idx = f;
-            w.S = cum_at;
-            w.t3 = static_cast<double>(u) * cum_at;
-            w.phase = 1;
-          }
-          __syncthreads();
-          if (a.list_len && w.fast && tid == 0) w.list_done = 1;
-          if (a.list_len && w.fast) {
-            // the ordered list from its top through the cutoff (or the K-th)
-            const int nl = min(min(w.K, ncol), a.list_cap);
-            for (int j = tid; j < nl; j += kNT) {
-              const uint64_t key = cand[j];
-              a.list_ids[static_cast<int64_t>(row) * a.list_cap + j] =
-                  static_cast<int>(key_id(key)) + a.vocab_offset;
-              a.list_probs[static_cast<int64_t>(row) * a.list_cap + j] =
-                  static_cast<float>(static_cast<double>(expf(row_l(key_val(key), rc))) / w.Z);
-            }
-            if (tid == 0) a.list_len[row] = (nl == min(w.K, a.list_cap)) ? nl : -1;
-          }
-        } else {
-          next_lo = next_nonempty(cnt, w.seg_hi);
-        }
-      } else if (tid == 0) {
-        w.cut_in_seg = 0;
+    w.phase = 0;
+    w.K = K;
+    w.mass_mode = mass_mode;
+    w.cut_in_seg = 0;
+    w.cut_idx = -1;
+    w.status = 0;
+    w.token = -1;
+    w.prob = 0.0f;
+    w.count_before = 0;
+    w.mass_before = 0.0;
+    w.Z = Z;
+    w.t2 = static_cast<double>(prm.top_p) * Z;
+    w.S = 0.0;
+    w.t3 = 0.0;
+  }
+  __syncthreads();
+
+  if (thr_path) {
+    // ---- merge the candidate lists, sort, exact top-k / top-p / draw ----
+    int off = 0;
+    for (int c = 0; c < S; ++c) {
+      const int n = sums_s[c].ncand;
+      const uint64_t* srcc = ws.cands + (static_cast<int64_t>(row) * ws.smax + c) * kCapC;
+      for (int i = tid; i < n && off + i < kMergeCap; i += kCT) keys[off + i] = __ldcg(srcc + i);
+      off += n;
+    }
+    if (off > kMergeCap) {
+      finish(RL_ERR_UNSUPPORTED, -1, 0.0f);
+      return;
+    }
+    const int P = pow2_ceil(off);
+    for (int i = off + tid; i < P; i += kCT) keys[i] = 0ull;
+    __syncthreads();
+    block_sort_desc(keys, P);
+    const int nlist = min(K, off);
+    double cum_at = 0.0;
+    const int f = sweep(keys, nlist, *wk, m, rt, 0, rs, &cum_at);
+    const int cut = (f == INT_MAX) ? nlist - 1 : f;
+    if (f == INT_MAX) {
+      // cumulative mass never reached top_p inside the list (rounding): the
+      // list end is the cutoff; recompute its cumulative mass
+      double tot = 0.0;
+      for (int c0 = 0; c0 < nlist; c0 += kCT) {
+        const int j = c0 + tid;
+        double t;
+        block_scan_d(j < nlist ? static_cast<double>(exact_e(key_val(keys[j]), m, rt)) : 0.0, rs, &t);
+        tot += t;
       }
-      __syncthreads();
-      if (w.phase == 1 && next_lo < 0) {
-        if (w.t3 < w.mass_before) {
-          // the draw lies above this segment: locate its bin
-          const double t3q = w.t3 * kMassScale;
-          int b3 = kNB;
-          for (int b = tid; b < kNB; b += kNT) {
-            const double pm = b ? static_cast<double>(mass[b - 1]) : 0.0;
-            if (static_cast<double>(mass[b]) > t3q && pm <= t3q) b3 = b;
+      cum_at = tot;
+    }
+    if (tid == 0) {
+      wk->S = cum_at;
+      wk->t3 = static_cast<double>(u) * cum_at;
+    }
+    __syncthreads();
+    const int d = sweep(keys, cut + 1, *wk, m, rt, 1, rs, &cum_at);
+    const int j = (d == INT_MAX) ? cut : d;
+    if (a.list_len) {
+      const int nl = min(nlist, a.list_cap);
+      for (int i = tid; i < nl; i += kCT) {
+        a.list_ids[static_cast<int64_t>(row) * a.list_cap + i] = static_cast<int>(key_id(keys[i])) + a.vocab_offset;
+        a.list_probs[static_cast<int64_t>(row) * a.list_cap + i] =
+            static_cast<float>(static_cast<double>(exact_e(key_val(keys[i]), m, rt)) / Z);
+      }
+      if (tid == 0) a.list_len[row] = nl;
+    }
+    const float ej = exact_e(key_val(keys[j]), m, rt);
+    finish(0, static_cast<int>(key_id(keys[j])), static_cast<float>(static_cast<double>(ej) / wk->S));
+    return;
+  }
+
+  // ---- histogram path: merge the chunk histograms on the row's grid ----
+  const int Bmax = babs(m, rt);
+  double* gcnt = reinterpret_cast<double*>(smem + kOffCnt);
+  double* gmass = reinterpret_cast<double*>(smem + kOffMass);
+  {
+    double c2[2] = {0.0, 0.0}, m2[2] = {0.0, 0.0};
+    for (int c = 0; c < S; ++c) {
+      const ChunkSum& s = sums_s[c];
+      if (s.nallow == 0) continue;
+      const int shift = Bmax - s.babs_m;
+      const double f = exp2((static_cast<double>(s.m) - static_cast<double>(m)) * (kLog2e / static_cast<double>(T))) /
+                       kMassScale;
+      const uint32_t* gc = ws.hcnt + (static_cast<int64_t>(row) * ws.smax + c) * kNB;
+      const unsigned long long* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + c) * kNB;
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int i = 2 * tid + q - shift;
+        if (i >= 0 && i < kNB) {
+          c2[q] += static_cast<double>(__ldcg(gc + i));
+          m2[q] += static_cast<double>(__ldcg(gm + i)) * f;
+        }
+      }
+    }
+    double tc, tm;
+    const double ci = block_scan_d(c2[0] + c2[1], rs, &tc);
+    const double mi = block_scan_d(m2[0] + m2[1], rs, &tm);
+    gcnt[2 * tid] = ci - c2[1];
+    gcnt[2 * tid + 1] = ci;
+    gmass[2 * tid] = mi - m2[1];
+    gmass[2 * tid + 1] = mi;
+    __syncthreads();
+  }
+  // gcnt / gmass: inclusive cumulative counts / masses per row bin j (absolute bin Bmax - j)
+  const bool need_q1 = K < gallow;
+  auto first_bin = [&](int kind, double target) -> int {
+    // kind 0: count >= target; 1: mass >= target; 2: mass > target
+    int b = INT_MAX;
+    for (int j = tid; j < kNB; j += kCT) {
+      const double cur = kind == 0 ? gcnt[j] : gmass[j];
+      const double prev = j ? (kind == 0 ? gcnt[j - 1] : gmass[j - 1]) : 0.0;
+      const bool hit = kind == 2 ? (cur > target && !(prev > target)) : (cur >= target && !(prev >= target));
+      if (hit) b = j;
+    }
+    return block_min_i(b, rs);
+  };
+  int bin;
+  if (!need_q1 && !mass_mode) {
+    // the list is every allowed id: cutoff at its end, S = Z
+    if (tid == 0) {
+      wk->phase = 1;
+      wk->S = Z;
+      wk->t3 = static_cast<double>(u) * Z;
+    }
+    __syncthreads();
+    bin = first_bin(2, wk->t3);
+  } else {
+    const int b1 = need_q1 ? first_bin(0, static_cast<double>(K)) : INT_MAX;
+    const int b2 = mass_mode ? first_bin(1, wk->t2) : INT_MAX;
+    bin = min(b1, b2);
+  }
+  // ---- bin-by-bin walk ----
+  int32_t* hid = reinterpret_cast<int32_t*>(smem + kOffHist);  // finisher history table (sorted)
+  float* hval = reinterpret_cast<float*>(smem + kOffPen);
+  uint64_t* bkeys = keys;                                       // keys of one bin (<= kMergeCap)
+  int nh = -1;  // history table built on first re-read
+  for (int round = 0; round < kMaxRounds; ++round) {
+    if (bin >= kNB) {
+      if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;  // beyond the 64-nat window
+      break;
+    }
+    const int A = Bmax - bin;
+    bool covered = true;
+    for (int c = 0; c < S; ++c)
+      if (sums_s[c].nallow > 0 && sums_s[c].athr > A) covered = false;
+    if (tid == 0) ctrl->nbin = 0;
+    __syncthreads();
+    if (covered) {
+      for (int c = 0; c < S; ++c) {
+        const int n = sums_s[c].ncand;
+        const uint64_t* srcc = ws.cands + (static_cast<int64_t>(row) * ws.smax + c) * kCapC;
+        for (int i = tid; i < n; i += kCT) {
+          const uint64_t key = __ldcg(srcc + i);
+          if (babs(key_val(key), rt) == A) {
+            const int idx = atomicAdd(&ctrl->nbin, 1);
+            if (idx < kMergeCap) bkeys[idx] = key;
           }
-          b3 = block_min_i(b3, rs);
-          next_lo = (b3 < w.seg_lo) ? b3 : max(0, w.seg_lo - 1);
-          if (tid == 0) w.cut_in_seg = 0;
-        } else {
-          const int f = sweep_segment(cand, ncol, w, rc, 1, rs, &cum_at);
-          if (tid == 0) {
-            int j = -1;
-            if (f != INT_MAX && (!w.cut_in_seg || f <= w.cut_idx)) j = f;
-            else if (w.cut_in_seg) j = w.cut_idx;  // u*S reached nowhere before the cutoff
-            if (j >= 0) {
-              const uint64_t key = cand[j];
-              const float e = expf(row_l(key_val(key), rc));
-              w.token = static_cast<int>(key_id(key));
-              w.prob = static_cast<float>(static_cast<double>(e) / w.S);
-              w.phase = 2;
-            }
-          }
-          __syncthreads();
-          if (w.phase != 2) next_lo = next_nonempty(cnt, w.seg_hi);
         }
       }
     } else {
-      // empty segment: move on
-      next_lo = next_nonempty(cnt, w.seg_hi);
-    }
-    __syncthreads();
-    if (tid == 0) {
-      Plan np;
-      np.op = kPlanDone;
-      if (w.status == 0 && w.phase != 2) {
-        if (next_lo < 0 || next_lo >= kNB || round + 1 >= kMaxRounds) {
-          w.status = RL_ERR_UNSUPPORTED;
-        } else {
-          const uint32_t popb = cnt[next_lo] - (next_lo ? cnt[next_lo - 1] : 0u);
-          if (popb > static_cast<uint32_t>(kCap)) {
-            w.status = RL_ERR_UNSUPPORTED;
-          } else {
-            np.op = kPlanCollect;
-            np.lo = next_lo;
-            np.hi = next_lo;
-            plan_bounds(np, m, T);
-            w.fast = next_lo == 0;
-            w.seg_lo = next_lo;
-            w.seg_hi = next_lo;
-            w.count_before = next_lo ? cnt[next_lo - 1] : 0;
-            w.mass_before = next_lo ? static_cast<double>(mass[next_lo - 1]) / kMassScale : 0.0;
+      // re-read the row (L2-resident) for the elements of bin A
+      if (nh < 0) {
+        // sorted, de-duplicated history ids with their penalised values
+        int hlr = a.hist ? a.hist_len[row] : 0;
+        hlr = max(0, min(hlr, min(a.hist_stride, kHmax)));
+        const int P = pow2_ceil(max(hlr, 1));
+        for (int j = tid; j < P; j += kCT) {
+          uint64_t h = ~0ull;
+          if (j < hlr) {
+            const int hv = a.hist[static_cast<int64_t>(row) * a.hist_stride + j] - a.vocab_offset;
+            if (hv >= 0 && hv < V) h = static_cast<uint64_t>(hv);
+          }
+          bkeys[j] = h;
+        }
+        __syncthreads();
+        block_sort_desc(bkeys, P);  // descending; position j ascending is P-1-j
+        const E* xr0 = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
+        // each thread owns ascending positions tid and tid + kCT (P <= kHmax <= 2 kCT)
+        int fl[2] = {0, 0};
+        uint64_t idv[2] = {~0ull, ~0ull};
+        int cntv[2] = {0, 0};
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int j = tid + q * kCT;
+          if (j < P) {
+            const uint64_t h = bkeys[P - 1 - j];
+            if (h != ~0ull && (j == 0 || bkeys[P - j] != h)) {
+              fl[q] = 1;
+              idv[q] = h;
+              int c = 0;
+              for (int t = j; t < P && bkeys[P - 1 - t] == h; ++t) ++c;
+              cntv[q] = c;
+            }
           }
         }
+        // output positions in ascending order: positions 0..kCT-1, then kCT..P-1
+        {
+          double t0;
+          const double i0 = block_scan_d(static_cast<double>(fl[0]), rs, &t0);
+          double t1;
+          const double i1 = block_scan_d(static_cast<double>(fl[1]), rs, &t1);
+          const int p0 = static_cast<int>(i0) - fl[0];
+          const int p1 = static_cast<int>(t0) + static_cast<int>(i1) - fl[1];
+          auto pen = [&](int id, int c) {
+            float v;
+            if constexpr (sizeof(E) == 4) {
+              v = __ldcg(xr0 + id);
+            } else {
+              v = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr0) + id));
+            }
+            const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
+            return sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
+          };
+          if (fl[0]) {
+            hid[p0] = static_cast<int32_t>(idv[0]);
+            hval[p0] = pen(static_cast<int>(idv[0]), cntv[0]);
+          }
+          if (fl[1]) {
+            hid[p1] = static_cast<int32_t>(idv[1]);
+            hval[p1] = pen(static_cast<int>(idv[1]), cntv[1]);
+          }
+          nh = static_cast<int>(t0 + t1);
+        }
+        if (tid == 0) ctrl->nbin = 0;
+        __syncthreads();
       }
-      ctrl->cand_count = 0;
-      for (int r = 0; r < C; ++r) *cluster.map_shared_rank(plan, r) = np;
+      const E* xr = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
+      for (int i = tid; i < V; i += kCT) {
+        float x;
+        if constexpr (sizeof(E) == 4) {
+          x = __ldcg(xr + i);
+        } else {
+          x = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr) + i));
+        }
+        if (nh > 0) x = hist_value(x, i, hid, hval, nh);
+        if (mask_on && !((mrow[i >> 5] >> (i & 31)) & 1u)) continue;
+        if (!(x > RL_NEG_INF)) continue;
+        if (babs(x, rt) == A) {
+          const int idx = atomicAdd(&ctrl->nbin, 1);
+          if (idx < kMergeCap) bkeys[idx] = cand_key(x, static_cast<uint32_t>(i));
+        }
+      }
     }
+    __syncthreads();
+    const int nb = ctrl->nbin;
+    if (nb > kMergeCap) {
+      if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;
+      break;
+    }
+    const int P = pow2_ceil(max(nb, 1));
+    for (int i = nb + tid; i < P; i += kCT) bkeys[i] = 0ull;
+    __syncthreads();
+    block_sort_desc(bkeys, P);
+    if (tid == 0) {
+      wk->count_before = bin ? static_cast<long long>(gcnt[bin - 1]) : 0;
+      wk->mass_before = bin ? gmass[bin - 1] : 0.0;
+    }
+    __syncthreads();
+    int next = INT_MAX;
+    double cum_at = 0.0;
+    if (wk->phase == 0) {
+      const int f = sweep(bkeys, nb, *wk, m, rt, 0, rs, &cum_at);
+      if (f != INT_MAX) {
+        if (tid == 0) {
+          wk->cut_in_seg = 1;
+          wk->cut_idx = f;
+          wk->S = cum_at;
+          wk->t3 = static_cast<double>(u) * cum_at;
+          wk->phase = 1;
+        }
+      } else {
+        next = bin + 1;
+      }
+    } else if (tid == 0) {
+      wk->cut_in_seg = 0;
+    }
+    __syncthreads();
+    if (wk->phase == 1 && next == INT_MAX) {
+      if (wk->t3 < wk->mass_before) {
+        const int b3 = first_bin(2, wk->t3);
+        next = (b3 < bin) ? b3 : max(0, bin - 1);
+      } else {
+        const int d = sweep(bkeys, nb, *wk, m, rt, 1, rs, &cum_at);
+        if (tid == 0) {
+          int j = -1;
+          if (d != INT_MAX && (!wk->cut_in_seg || d <= wk->cut_idx)) j = d;
+          else if (wk->cut_in_seg) j = wk->cut_idx;
+          if (j >= 0) {
+            const uint64_t key = bkeys[j];
+            wk->token = static_cast<int>(key_id(key));
+            wk->prob = static_cast<float>(static_cast<double>(exact_e(key_val(key), m, rt)) / wk->S);
+            wk->phase = 2;
+          }
+        }
+        __syncthreads();
+        if (wk->phase != 2) next = bin + 1;
+      }
+    }
+    __syncthreads();
+    if (wk->phase == 2) break;
+    bin = next;
   }
-
-  if (rank == 0 && tid == 0) {
-    const Walk& w = *wk;
-    const bool ok = w.status == 0 && w.phase == 2;
-    const int st = ok ? 0 : (w.status ? w.status : RL_ERR_UNSUPPORTED);
-    a.out_tok[row] = ok ? w.token + a.vocab_offset : -1;
-    if (a.out_prob) a.out_prob[row] = ok ? w.prob : 0.0f;
-    if (a.row_status) a.row_status[row] = st;
-    if (a.list_len && !w.list_done) a.list_len[row] = -1;
-  }
+  __syncthreads();
+  if (a.list_len && tid == 0) a.list_len[row] = -1;  // lists are reported on the threshold path only
+  const Walk& w = *wk;
+  if (w.phase == 2 && w.status == 0) finish(0, w.token, w.prob);
+  else finish(w.status ? w.status : RL_ERR_UNSUPPORTED, -1, 0.0f);
 }
 
 // ---------------------------------------------------------------------------
 // Host launcher
 // ---------------------------------------------------------------------------
-int spec_pick_cluster(int B, int V, int es, int num_sms) {
-  // smallest power of two keeping each slice <= 64 KB (two CTAs per SM)...
-  int C = 1;
-  while (C < kCmax && static_cast<int64_t>(V) * es > static_cast<int64_t>(C) * 65536) C <<= 1;
-  // ...then widen small batches so that one row spreads over more SMs
-  while (C < 8 && static_cast<int64_t>(B) * C * 2 <= num_sms) C <<= 1;
-  return C;
-}
-
 template <typename E>
-static cudaError_t launch_typed(const SpecArgs& a, int C, int smem, cudaStream_t stream) {
-  auto k = spec_sample_kernel<E>;
+static cudaError_t launch_typed(const SpecArgs& a, int S, int smem, cudaStream_t stream) {
+  auto k = spec_chunk_kernel<E>;
   cudaError_t err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (err == cudaSuccess && C > 8)
-    err = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   if (err != cudaSuccess) return err;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(C, a.B, 1);
-  cfg.blockDim = dim3(kNT, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = C;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, a);
+  k<<<dim3(S, a.B, 1), dim3(kCT, 1, 1), smem, stream>>>(a);
+  return cudaGetLastError();
 }
 
-cudaError_t launch_spec(const SpecArgs& args_in, int dtype, int num_sms, cudaStream_t stream) {
+cudaError_t launch_spec(const SpecArgs& args_in, int dtype, cudaStream_t stream) {
   SpecArgs a = args_in;
   const int es = dtype == RL_BF16 ? 2 : 4;
-  const int C = spec_pick_cluster(a.B, a.V, es, num_sms);
-  const int per = (a.V + C - 1) / C;
-  a.L = ((per + 127) / 128) * 128;
-  const int smem = spec_smem_bytes(a.L, es);
-  if (dtype == RL_BF16) return launch_typed<uint16_t>(a, C, smem, stream);
-  return launch_typed<float>(a, C, smem, stream);
+  a.chunk_elems = kChunkBytes / es;
+  const int S = spec_chunks(a.V, es);
+  const int smem = spec_smem_bytes(es);
+  if (dtype == RL_BF16) return launch_typed<uint16_t>(a, S, smem, stream);
+  return launch_typed<float>(a, S, smem, stream);
 }
 
 }  // namespace rl

@@ -1,4 +1,4 @@
-// Launch interface of the cluster-per-row spec sampling kernel.
+// Launch interface of the chunked spec sampling kernel.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -8,19 +8,45 @@
 
 namespace rl {
 
-constexpr int kNT = 512;               // threads per CTA
-constexpr int kNWarp = kNT / 32;
-constexpr int kNB = 1024;              // histogram bins over l = (x - m) / T
-constexpr float kRbin = 16.0f;         // bins per nat: the window covers 64 nats
-constexpr int kCap = 2048;             // rank-0 collection buffer (keys)
-constexpr int kHmax = 1024;            // max history entries per row
-constexpr int kCmax = 16;              // max CTAs per cluster
-constexpr int kNPiece = 4;             // bulk-copy pieces per slice
-constexpr int kMaxRounds = 16;         // collection rounds per row
+constexpr int kCT = 512;             // threads per chunk CTA
+constexpr int kCW = kCT / 32;        // warps per chunk CTA
+constexpr int kChunkBytes = 65536;   // logits bytes per chunk (16384 f32 / 32768 bf16)
+constexpr int kNB = 1024;            // histogram bins per chunk (absolute grid)
+constexpr float kRbin = 16.0f;       // bins per nat of (x - m) / T
+constexpr int kKthr = 128;           // top_k <= kKthr: thread-maximum threshold path
+constexpr int kKbig = 512;           // histogram path: each chunk keeps its top kKbig
+constexpr int kCapC = 1024;          // candidate keys per chunk in the workspace
+constexpr int kSmax = 64;            // max chunks per row
+constexpr int kHmax = 1024;          // max history entries per row
+constexpr int kNPiece = 4;           // bulk-copy pieces per chunk
+constexpr int kMaxRounds = 16;       // bin rounds of the finishing walk
+constexpr int kMergeCap = 8192;      // merged keys the finishing CTA holds (64 KB)
 constexpr double kMassScale = 1099511627776.0;  // 2^40 fixed point for bin masses
 constexpr float kMassScaleF = 1099511627776.0f;
 
-// Output modes of the kernel.
+// Per-chunk summary written by every chunk CTA.
+struct ChunkSum {
+  float m;       // chunk max over allowed finite (penalised) logits
+  int argmax;    // lowest row-local id at that max
+  int nallow;    // allowed finite logits in the chunk
+  int flags;     // bit0 non-finite input, bit1 copy timeout, bit2 candidate overflow
+  double z;      // sum of exp((x - m) / T) over the chunk, relative to m
+  int ncand;     // candidate keys written
+  int babs_m;    // absolute bin of m
+  int athr;      // histogram path: every element with absolute bin >= athr was kept
+  float tau;     // threshold path: every element >= tau was kept
+};
+
+// Device workspace owned by the handle (allocated at create).
+struct Workspace {
+  int32_t* row_done;           // [max_batch] arrival counters, reset by the finisher
+  ChunkSum* sums;              // [max_batch * smax]
+  uint64_t* cands;             // [max_batch * smax * kCapC]
+  uint32_t* hcnt;              // [max_batch * smax * kNB]
+  unsigned long long* hmass;   // [max_batch * smax * kNB]
+  int smax;
+};
+
 enum SpecMode : int {
   kModeSample = 0,  // draw one token per row
 };
@@ -44,13 +70,14 @@ struct SpecArgs {
   float* list_probs;
   int32_t* list_len;
   int list_cap;
-  int L;             // slice length per CTA (elements, multiple of 128)
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
   int mode;
+  int chunk_elems;   // elements per chunk
+  Workspace ws;
 };
 
-int spec_smem_bytes(int L, int es);
-int spec_pick_cluster(int B, int V, int es, int num_sms);
-cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream);
+int spec_smem_bytes(int es);
+int spec_chunks(int V, int es);
+cudaError_t launch_spec(const SpecArgs& args, int dtype, cudaStream_t stream);
 
 }  // namespace rl

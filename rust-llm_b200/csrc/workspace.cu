@@ -23,6 +23,18 @@ rl_status alloc_workspace(rl_sampler* h) {
             dalloc(&h->stage_hist_len, B) && dalloc(&h->stage_mask, B * h->mask_words) &&
             dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
             dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
+  // chunked spec kernel workspace: f32 chunks are the smallest (most chunks)
+  const int smax = (h->max_vocab + (kChunkBytes / 4) - 1) / (kChunkBytes / 4);
+  h->ws.smax = smax;
+  const size_t rows_chunks = B * static_cast<size_t>(smax);
+  ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, rows_chunks) &&
+       dalloc(&h->ws.cands, rows_chunks * kCapC) && dalloc(&h->ws.hcnt, rows_chunks * kNB) &&
+       dalloc(&h->ws.hmass, rows_chunks * kNB);
+  if (ok && smax > kSmax) {
+    return set_error(RL_ERR_SHAPE, "rl_sampler_create: max_vocab needs more chunks per row than supported");
+  }
+  if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
+               cudaDeviceSynchronize() == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
     return set_error(RL_ERR_OOM, "rl_sampler_create: device allocation failed");
@@ -40,6 +52,12 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->stage_tok);
   cudaFree(h->stage_prob);
   cudaFree(h->stage_status);
+  cudaFree(h->ws.row_done);
+  cudaFree(h->ws.sums);
+  cudaFree(h->ws.cands);
+  cudaFree(h->ws.hcnt);
+  cudaFree(h->ws.hmass);
+  h->ws = {};
   if (h->stream) cudaStreamDestroy(h->stream);
   h->stage_logits = nullptr;
   h->stream = nullptr;
