@@ -133,8 +133,7 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: mask_stride %lld < ceil(V/32)", (long long)mask_stride);
   if (list_len && (!list_ids || !list_probs || list_cap <= 0))
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list buffers required");
-  const int es = dtype == RL_BF16 ? 2 : 4;
-  if (rl::spec_chunks(V, es) > h->ws.smax)
+  if (rl::spec_chunks(V) > h->ws.smax)
     return fail(RL_ERR_SHAPE, "rl_sample_batch: V=%d beyond the handle's max_vocab", V);
   DeviceGuard g(h->device);
   if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);

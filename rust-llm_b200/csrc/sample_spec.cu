@@ -9,22 +9,24 @@
 //   strict '<' draw            Decoder::sample_multinomial   decoder.rs:146-158
 //   empty allowed set -> all   Sampler::sample_with_grammar  decoder.rs:362-364
 //
-// Design (B200, sm_100a). One launch; the grid is (chunks, rows). Every CTA
-// streams one 64 KB chunk of one row into shared memory with bulk async
-// copies (cp.async.bulk + mbarrier) -- the only HBM read of those logits --
-// and reduces it to a small summary in the handle's workspace:
-//   P1  chunk max / lowest argmax / allowed count / per-thread maxima
-//   P2  Z partial sum of exp((x - m_c)/T) (ex2 on a split log2(e)/T), and for
-//       rows without a small top_k, count + mass histograms on an absolute
-//       bin grid (16 bins per nat)
-//   P3  candidate keys (value desc, id asc) of everything that can be in the
-//       row's top-k: x >= tau, tau = k-th largest per-thread maximum (k <= 128),
+// Design (B200, sm_100a). One launch, grid (chunks, rows), three CTAs per SM.
+// Every CTA streams one 48 KB chunk (12288 logits) of one row into shared
+// memory with bulk async copies (cp.async.bulk + mbarrier) -- the only HBM
+// read of those logits -- applies the row's penalties and mask in place, and
+// reduces the chunk to a summary in the handle's workspace. Each pass keeps
+// its 32 values per thread in registers (8 unrolled 16-byte loads):
+//   P1  chunk max, allowed count, non-finite check, per-thread maxima
+//   P2  Z partial: sum of 2^((x - m_c) * log2(e)/T) (split constant, ex2)
+//       histogram rows also bin every logit on an absolute grid (16 bins per
+//       nat) and add its bin-relative mass (u32 fixed point; u32 atomics)
+//   P3  candidate keys (value desc, id asc) of every logit that can be in the
+//       row's top-k: x >= tau, tau from the per-thread maxima (top_k <= 128),
 //       or the chunk's top 512 by the histogram.
-// The last CTA of a row to finish (arrival counter) merges the summaries:
-// global max, Z, the exact top-k list (sorted keys, exact exp), the inclusive
-// top-p cutoff and the draw. Rows without a small top_k walk the merged
-// histogram bin by bin; a bin not covered by the candidate lists is re-read
-// from the (L2-resident) row.
+// The last CTA of a row to arrive (arrival counter) finishes the row: global
+// max and Z, the exact top-k list (tightened threshold + rank sort, exact
+// exp), the inclusive top-p cutoff and the draw. Rows without a small top_k
+// walk the merged histogram bin by bin; a bin not covered by the candidate
+// lists is re-read from the row (L2-resident by then).
 #include <climits>
 
 #include "common.cuh"
@@ -32,9 +34,9 @@
 
 namespace rl {
 
-constexpr uint16_t kBf16Marker = 0x7fc1;  // bf16 slot whose penalised value is in the side table
 constexpr uint16_t kBf16NegInf = 0xff80;
 constexpr double kLog2e = 1.4426950408889634074;
+constexpr int kBinsPT = (kNB + kCT - 1) / kCT;  // histogram bins per thread in scans (3)
 
 // ---------------------------------------------------------------------------
 // Row arithmetic
@@ -44,6 +46,7 @@ struct RowT {
   bool fast_div;     // Markstein division valid for T
   float c_hi, c_lo;  // log2(e)/T split in two floats
   float cb;          // absolute bins per logit unit: kRbin / T
+  float dlt;         // log2(e) / kRbin: log2 width of one bin
 };
 
 __device__ __forceinline__ RowT make_rowt(float T) {
@@ -55,6 +58,7 @@ __device__ __forceinline__ RowT make_rowt(float T) {
   r.c_hi = static_cast<float>(c);
   r.c_lo = static_cast<float>(c - static_cast<double>(r.c_hi));
   r.cb = div_rn(kRbin, T);
+  r.dlt = static_cast<float>(kLog2e / static_cast<double>(kRbin));
   return r;
 }
 // l = (x - m) / T with IEEE rounding, as the CPU restatement computes it.
@@ -75,62 +79,44 @@ __device__ __forceinline__ float fast_e(float x, float m, const RowT& r) {
   return ex2_approx(fmaf(d, r.c_lo, d * r.c_hi));
 }
 // Absolute bin of a logit: monotone in x, identical wherever it is computed.
-__device__ __forceinline__ int babs(float x, const RowT& r) {
-  return __float2int_rd(__fmul_rn(x, r.cb));
+__device__ __forceinline__ int babs(float x, const RowT& r) { return __float2int_rd(__fmul_rn(x, r.cb)); }
+
+// ---------------------------------------------------------------------------
+// Chunk access: 4 consecutive logits per 16-byte (f32) / 8-byte (bf16) load.
+// ---------------------------------------------------------------------------
+template <typename E>
+__device__ __forceinline__ void load4(const E* data, int g, float (&v)[4]);
+template <>
+__device__ __forceinline__ void load4<float>(const float* data, int g, float (&v)[4]) {
+  const float4 q = reinterpret_cast<const float4*>(data)[g];
+  v[0] = q.x;
+  v[1] = q.y;
+  v[2] = q.z;
+  v[3] = q.w;
+}
+template <>
+__device__ __forceinline__ void load4<uint16_t>(const uint16_t* data, int g, float (&v)[4]) {
+  const uint2 q = reinterpret_cast<const uint2*>(data)[g];
+  v[0] = __uint_as_float(q.x << 16);
+  v[1] = __uint_as_float(q.x & 0xffff0000u);
+  v[2] = __uint_as_float(q.y << 16);
+  v[3] = __uint_as_float(q.y & 0xffff0000u);
+}
+// all kGPT groups of this thread (group g = tid + k * kCT)
+template <typename E>
+__device__ __forceinline__ void load_all(const E* data, float (&v)[kGPT][4]) {
+#pragma unroll
+  for (int k = 0; k < kGPT; ++k) load4<E>(data, threadIdx.x + k * kCT, v[k]);
 }
 
 // ---------------------------------------------------------------------------
-// Chunk access: values of G consecutive elements per 16-byte shared load.
-// ---------------------------------------------------------------------------
-template <typename E>
-struct Slice;
-
-template <>
-struct Slice<float> {
-  static constexpr int G = 4;
-  const float* data;
-  __device__ __forceinline__ void load(int g, float (&v)[4]) const {
-    const float4 q = reinterpret_cast<const float4*>(data)[g];
-    v[0] = q.x;
-    v[1] = q.y;
-    v[2] = q.z;
-    v[3] = q.w;
-  }
-};
-
-template <>
-struct Slice<uint16_t> {
-  static constexpr int G = 8;
-  const uint16_t* data;
-  const int32_t* pen_id;  // local ids of penalised entries (-1: duplicate)
-  const float* pen_val;
-  int n_pen;
-  __device__ __noinline__ float lookup(int local) const {
-    for (int t = 0; t < n_pen; ++t)
-      if (pen_id[t] == local) return pen_val[t];
-    return __int_as_float(0x7fffffff);
-  }
-  __device__ __forceinline__ void load(int g, float (&v)[8]) const {
-    const uint4 q = reinterpret_cast<const uint4*>(data)[g];
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const uint32_t lo = w[k] & 0xffffu, hi = w[k] >> 16;
-      v[2 * k] = (lo == kBf16Marker) ? lookup(g * 8 + 2 * k) : bf16_bits_to_f32(lo);
-      v[2 * k + 1] = (hi == kBf16Marker) ? lookup(g * 8 + 2 * k + 1) : bf16_bits_to_f32(hi);
-    }
-  }
-};
-
-// ---------------------------------------------------------------------------
-// Block helpers (kCT threads)
+// Block / warp helpers (kCT threads)
 // ---------------------------------------------------------------------------
 struct RedScratch {
   double d[kCW];
   float f[kCW];
   int i[kCW];
   int j[kCW];
-  int k[kCW];
   double bcast_d;
   int bcast_i;
   int pad;
@@ -209,52 +195,68 @@ __device__ __forceinline__ double block_scan_d(double v, RedScratch* rs, double*
   return v + off;
 }
 
-// Descending bitonic sort of P (power of two) keys in shared memory.
-template <typename K>
-__device__ void block_sort_desc(K* s, int P) {
-  for (int k = 2; k <= P; k <<= 1) {
+// Descending sort of one float per lane across a warp (bitonic, shuffles).
+__device__ __forceinline__ float warp_sort_desc(float v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = threadIdx.x; i < P; i += kCT) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const K a = s[i], b = s[ixj];
-          const bool desc = (i & k) == 0;
-          if (desc ? (a < b) : (a > b)) {
-            s[i] = b;
-            s[ixj] = a;
-          }
-        }
-      }
-      __syncthreads();
+      const float o = __shfl_xor_sync(0xffffffffu, v, j);
+      const bool desc = (lane & k) == 0 || k == 32;
+      const bool lower = (lane & j) == 0;
+      v = (desc == lower) ? fmaxf(v, o) : fminf(v, o);
     }
   }
+  return v;
 }
 
-__device__ __forceinline__ int pow2_ceil(int n) {
-  int p = 1;
-  while (p < n) p <<= 1;
-  return p;
+// Lower bound of the k-th largest of the values held one per thread: every
+// warp holds at least ceil(k / kCW) values >= the result, so at least k
+// values are. -inf if some warp holds fewer finite values.
+__device__ __forceinline__ float block_kth_lower_bound(float v, int k, RedScratch* rs) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = min((k + kCW - 1) / kCW, 32);
+  const float s = warp_sort_desc(v);
+  const float wj = __shfl_sync(0xffffffffu, s, j - 1);
+  __syncthreads();
+  if (lane == 0) rs->f[warp] = wj;
+  __syncthreads();
+  float t = RL_POS_INF;
+  for (int w = 0; w < kCW; ++w) t = fminf(t, rs->f[w]);
+  return t;
+}
+
+// out[rank] = key for every key of rank < keep (keys unique; rank = number of
+// larger keys): the top `keep` keys in descending order.
+__device__ void rank_sort(const uint64_t* in, int n, uint64_t* out, int keep) {
+  for (int i = threadIdx.x; i < n; i += kCT) {
+    const uint64_t k = in[i];
+    int r = 0;
+    for (int j = 0; j < n; ++j) r += in[j] > k;
+    if (r < keep) out[r] = k;
+  }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
 // Shared-memory layout
 // ---------------------------------------------------------------------------
 struct Ctrl {
-  int n_local;   // history entries inside the chunk
-  int ncand;     // candidate keys written
+  int n_local;  // history entries inside the chunk
+  int ncand;    // candidate keys written
   int is_last;
-  int mask_on;
-  int overflow;
-  int nbin;      // keys gathered for the current bin (finisher)
-  int pad[2];
+  int nsel;     // finisher: keys selected
+  int nbin;     // finisher: keys gathered for the current bin
+  int pad[3];
 };
 
-// Finisher walk state (rank of the row's list, masses relative to the row max).
+// Finisher walk state (masses relative to the row max, e-units).
 struct Walk {
-  int phase;              // 0: find the cutoff, 1: find the draw, 2: done
-  int K;                  // list length
-  int mass_mode;          // top_p < 1
-  int cut_in_seg;         // the cutoff element is in the current segment
+  int phase;       // 0: find the cutoff, 1: find the draw, 2: done
+  int K;           // list length
+  int mass_mode;   // top_p < 1
+  int cut_in_seg;  // the cutoff element is in the current segment
   int cut_idx;
   int status;
   int token;
@@ -268,21 +270,19 @@ constexpr int kOffMbar = 0;
 constexpr int kOffCtrl = 64;
 constexpr int kOffWalk = 128;
 constexpr int kOffRed = 256;
-constexpr int kOffTmax = 1024;                 // kCT floats
-constexpr int kOffCnt = kOffTmax + kCT * 4;    // kNB u32 / finisher: kNB doubles (counts)
-constexpr int kOffMass = kOffCnt + kNB * 8;    // kNB u64 / finisher: kNB doubles (masses)
-constexpr int kOffHist = kOffMass + kNB * 8;   // kHmax ints
-constexpr int kOffPen = kOffHist + kHmax * 4;  // kHmax floats
+constexpr int kOffCnt = 1024;                  // kNB u32 counts
+constexpr int kOffMass = kOffCnt + kNB * 4;    // kNB u32 masses
+constexpr int kOffHist = kOffMass + kNB * 4;   // kHmax ints (finisher: sorted history ids)
+constexpr int kOffPen = kOffHist + kHmax * 4;  // kHmax floats (finisher: their values)
 constexpr int kOffSums = kOffPen + kHmax * 4;  // kSmax ChunkSum (finisher)
 constexpr int kOffData = ((kOffSums + kSmax * static_cast<int>(sizeof(ChunkSum)) + 127) / 128) * 128;
+constexpr int kDataBytes = kCE * 4;            // f32 chunk; finisher: keys + merged histograms
+static_assert(kMergeCap * 8 + kNB * 16 <= kDataBytes, "finisher region");
 static_assert(sizeof(Walk) <= 128, "walk");
-static_assert(kOffRed + sizeof(RedScratch) <= kOffTmax, "smem header");
+static_assert(kOffRed + sizeof(RedScratch) <= kOffCnt, "smem header");
 
-int spec_smem_bytes(int /*es*/) { return kOffData + kChunkBytes; }
-int spec_chunks(int V, int es) {
-  const int ce = kChunkBytes / es;
-  return (V + ce - 1) / ce;
-}
+int spec_smem_bytes(int /*es*/) { return kOffData + kDataBytes; }
+int spec_chunks(int V) { return (V + kCE - 1) / kCE; }
 
 // ---------------------------------------------------------------------------
 // Finisher pieces
@@ -320,8 +320,7 @@ __device__ int sweep(const uint64_t* keys, int n, const Walk& w, float m, const 
   return INT_MAX;
 }
 
-// Penalised value of history id `id` from the finisher's sorted history
-// table (ids hid[0..nh), values hval), or `x` if not in the history.
+// Penalised value of id from the finisher's sorted history table, or x.
 __device__ __forceinline__ float hist_value(float x, int id, const int32_t* hid, const float* hval, int nh) {
   int lo = 0, hi = nh - 1;
   while (lo <= hi) {
@@ -338,7 +337,7 @@ __device__ __forceinline__ float hist_value(float x, int id, const int32_t* hid,
 // The kernel
 // ---------------------------------------------------------------------------
 template <typename E>
-__global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
+__global__ void __launch_bounds__(kCT, 3) spec_chunk_kernel(const SpecArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int chunk = blockIdx.x;
   const int row = blockIdx.y;
@@ -351,26 +350,22 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   Ctrl* ctrl = reinterpret_cast<Ctrl*>(smem + kOffCtrl);
   Walk* wk = reinterpret_cast<Walk*>(smem + kOffWalk);
   RedScratch* rs = reinterpret_cast<RedScratch*>(smem + kOffRed);
-  float* tmax = reinterpret_cast<float*>(smem + kOffTmax);
   uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt);
-  unsigned long long* mass = reinterpret_cast<unsigned long long*>(smem + kOffMass);
+  uint32_t* mass = reinterpret_cast<uint32_t*>(smem + kOffMass);
   int32_t* hist_local = reinterpret_cast<int32_t*>(smem + kOffHist);
   float* pen_val = reinterpret_cast<float*>(smem + kOffPen);
   ChunkSum* sums_s = reinterpret_cast<ChunkSum*>(smem + kOffSums);
   E* data = reinterpret_cast<E*>(smem + kOffData);
 
   const int V = a.V;
-  const int CE = a.chunk_elems;
-  const int start = chunk * CE;
-  const int len = max(0, min(CE, V - start));
+  const int start = chunk * kCE;
+  const int len = max(0, min(kCE, V - start));
   constexpr int es = static_cast<int>(sizeof(E));
-  constexpr int G = Slice<E>::G;
-  const int ngroups = CE / G;
   const Workspace& ws = a.ws;
 
   const rl_row_params prm = a.params[row];
   const float T = prm.temperature;
-  const bool greedy = !(T > 0.0f);  // also NaN: reported as non-finite by the finisher
+  const bool greedy = !(T > 0.0f);  // NaN is reported as non-finite by the finisher
   const bool thr_path = prm.top_k > 0 && prm.top_k <= kKthr;
   const bool hist_path = !greedy && !thr_path;
 
@@ -383,12 +378,11 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     fence_mbar_init();
     ctrl->n_local = 0;
     ctrl->ncand = 0;
-    ctrl->overflow = 0;
   }
   if (hist_path)
     for (int b = tid; b < kNB; b += kCT) {
       cnt[b] = 0u;
-      mass[b] = 0ull;
+      mass[b] = 0u;
     }
   __syncthreads();
   if (tid == 0 && use_bulk) {
@@ -448,105 +442,113 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     } else {
       neg = kBf16NegInf;
     }
-    for (int i = len + tid; i < CE; i += kCT) data[i] = neg;
+    for (int i = len + tid; i < kCE; i += kCT) data[i] = neg;
   }
   __syncthreads();
 
-  // ---- penalties (first occurrence of an id applies them) ----
+  // ---- penalties: one warp per history entry (count + first occurrence) ----
   const int n_local = min(ctrl->n_local, kHmax);
-  for (int t = tid; t < n_local; t += kCT) {
+  for (int t = warp; t < n_local; t += kCW) {
     const int h = hist_local[t];
     int c = 0;
     bool first = true;
-    for (int j = 0; j < n_local; ++j) {
-      if (hist_local[j] == h) {
-        ++c;
-        if (j < t) first = false;
-      }
+    for (int j0 = 0; j0 < n_local; j0 += 32) {
+      const int j = j0 + lane;
+      const bool eq = j < n_local && hist_local[j] == h;
+      const uint32_t bal = __ballot_sync(0xffffffffu, eq);
+      c += __popc(bal);
+      if (eq && j < t) first = false;
     }
-    if (first) {
-      float v;
-      if constexpr (sizeof(E) == 4) {
-        v = data[h];
+    first = __all_sync(0xffffffffu, first);
+    if (lane == 0) {
+      if (first) {
+        float v;
+        if constexpr (sizeof(E) == 4) {
+          v = data[h];
+        } else {
+          v = bf16_bits_to_f32(data[h]);
+        }
+        const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
+        pen_val[t] = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
       } else {
-        v = bf16_bits_to_f32(data[h]);
-      }
-      const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
-      const float x3 = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
-      if constexpr (sizeof(E) == 4) {
-        data[h] = x3;
-      } else {
-        pen_val[t] = x3;
+        pen_val[t] = __int_as_float(0x7fffffff);  // duplicate entry: no-op
       }
     }
   }
   __syncthreads();
-  Slice<E> sl;
-  sl.data = data;
-  if constexpr (sizeof(E) == 2) {
-    for (int t = tid; t < n_local; t += kCT) {
-      const int h = hist_local[t];
-      bool first = true;
-      for (int j = 0; j < t; ++j)
-        if (hist_local[j] == h) first = false;
-      if (first) data[h] = kBf16Marker;
-    }
+  const bool dup_free = true;
+  (void)dup_free;
+  // f32: write the penalised values in place; bf16 chunks cannot hold them,
+  // so they are patched into the registers after every load (few slots).
+  if constexpr (sizeof(E) == 4) {
+    for (int t = tid; t < n_local; t += kCT)
+      if (!(pen_val[t] != pen_val[t])) data[hist_local[t]] = pen_val[t];
     __syncthreads();
-    for (int t = tid; t < n_local; t += kCT) {
-      const int h = hist_local[t];
-      bool first = true;
-      for (int j = 0; j < t; ++j)
-        if (hist_local[j] == h) first = false;
-      if (!first) hist_local[t] = -1;
-    }
-    __syncthreads();
-    sl.pen_id = hist_local;
-    sl.pen_val = pen_val;
-    sl.n_pen = n_local;
   }
   // masked ids -> -inf in place
   if (mask_on) {
-    for (int g = tid; g < ngroups; g += kCT) {
-      const int id0 = start + g * G;
+    for (int g = tid; g < kCE / 4; g += kCT) {
+      const int id0 = start + g * 4;
       const uint32_t bits = id0 < V ? (mrow[id0 >> 5] >> (id0 & 31)) : 0u;
 #pragma unroll
-      for (int k = 0; k < G; ++k) {
+      for (int k = 0; k < 4; ++k) {
         if (!((bits >> k) & 1u)) {
           if constexpr (sizeof(E) == 4) {
-            data[g * G + k] = RL_NEG_INF;
+            data[g * 4 + k] = RL_NEG_INF;
           } else {
-            data[g * G + k] = kBf16NegInf;
+            data[g * 4 + k] = kBf16NegInf;
           }
         }
       }
     }
     __syncthreads();
   }
-
-  // ---- P1: chunk max / lowest argmax / allowed count / non-finite; thread maxima ----
-  float mx = RL_NEG_INF;
-  int amx = INT_MAX;
-  int nallow = 0;
-  int bad = 0;
-  for (int g = tid; g < ngroups; g += kCT) {
-    float v[G];
-    sl.load(g, v);
+  // bf16: patch the penalised slots this thread owns (masked slots stay -inf)
+  auto patch = [&](float (&v)[kGPT][4]) {
+    if constexpr (sizeof(E) == 2) {
+      for (int t = 0; t < n_local; ++t) {
+        const float pv = pen_val[t];
+        if (pv != pv) continue;  // duplicate entry
+        const int h = hist_local[t];
+        const int g = h >> 2;
+        if ((g % kCT) != static_cast<int>(threadIdx.x)) continue;
+        const int q0 = g / kCT;
 #pragma unroll
-    for (int k = 0; k < G; ++k) {
-      const float x = v[k];
-      if (x > RL_NEG_INF) {
-        if (!(x < RL_POS_INF)) bad = 1;
-        ++nallow;
-        if (x > mx) {
-          mx = x;
-          amx = g * G + k;
-        }
-      } else if (x != x) {
-        bad = 1;
+        for (int q = 0; q < kGPT; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (q == q0 && k == (h & 3) && v[q][k] > RL_NEG_INF) v[q][k] = pv;
       }
     }
+  };
+
+  // ---- P1: chunk max / allowed count / non-finite; per-thread max ----
+  float mx = RL_NEG_INF;
+  int nallow = 0;
+  int bad = 0;
+  int amx = INT_MAX;
+  {
+    float v[kGPT][4];
+    load_all<E>(data, v);
+    patch(v);
+#pragma unroll
+    for (int q = 0; q < kGPT; ++q) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float x = v[q][k];
+        nallow += (x > RL_NEG_INF) ? 1 : 0;
+        bad |= (x != x) || (x == RL_POS_INF);
+        mx = fmaxf(mx, x);
+      }
+    }
+    if (greedy) {
+#pragma unroll
+      for (int q = 0; q < kGPT; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (v[q][k] == mx) amx = min(amx, (static_cast<int>(threadIdx.x) + q * kCT) * 4 + k);
+    }
   }
-  tmax[tid] = mx;
   float m_c;
   int argmax_c, nallow_c, bad_c;
   {
@@ -555,20 +557,19 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) wa = min(wa, __shfl_xor_sync(0xffffffffu, wa, o));
     const int wn = warp_sum_i(nallow);
-    const int wb = warp_sum_i(bad);
+    const int wb = __any_sync(0xffffffffu, bad);
     __syncthreads();
     if (lane == 0) {
       rs->f[warp] = wm;
       rs->i[warp] = wa;
-      rs->j[warp] = wn;
-      rs->k[warp] = wb;
+      rs->j[warp] = wn | (wb << 30);
     }
     __syncthreads();
     float bm = RL_NEG_INF;
     int ba = INT_MAX, bn = 0, bb = 0;
     for (int w = 0; w < kCW; ++w) {
-      bn += rs->j[w];
-      bb |= rs->k[w];
+      bn += rs->j[w] & 0x3fffffff;
+      bb |= rs->j[w] >> 30;
       if (rs->f[w] > bm) {
         bm = rs->f[w];
         ba = rs->i[w];
@@ -586,50 +587,64 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   int babs_m = 0;
   int athr = INT_MIN;
   float tau = RL_NEG_INF;
+  int binovf = 0;
   const RowT rt = make_rowt(greedy ? 1.0f : T);
   if (!greedy && nallow_c > 0 && !bad_c) {
     babs_m = babs(m_c, rt);
+    float v[kGPT][4];
+    load_all<E>(data, v);
+    patch(v);
     // ---- P2: Z partial (+ histograms) ----
-    float zsum = 0.0f;
-    for (int g = tid; g < ngroups; g += kCT) {
-      float v[G];
-      sl.load(g, v);
+    float z4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int k = 0; k < G; ++k) {
-        const float x = v[k];
-        if (x > RL_NEG_INF) {
-          const float e = fast_e(x, m_c, rt);
-          zsum += e;
-          if (hist_path) {
-            const int b = babs_m - babs(x, rt);
-            if (b < kNB) {
-              atomicAdd(&cnt[b], 1u);
-              atomicAdd(&mass[b], __float2ull_rn(e * kMassScaleF));
-            }
+    for (int q = 0; q < kGPT; ++q) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float x = v[q][k];
+        z4[k] += fast_e(x, m_c, rt);  // -inf contributes 0
+        if (hist_path && x > RL_NEG_INF) {
+          const float y = __fmul_rn(x, rt.cb);
+          const float af = floorf(y);
+          const int b = babs_m - static_cast<int>(af);
+          if (b < kNB) {
+            const float eb = ex2_approx((y - af - 1.0f) * rt.dlt);  // mass relative to the bin top
+            atomicAdd(&cnt[b], 1u);
+            atomicAdd(&mass[b], __float2uint_rn(eb * kMassQ));
           }
         }
       }
     }
-    z_c = block_sum_d(static_cast<double>(zsum), rs);
+    z_c = block_sum_d(static_cast<double>((z4[0] + z4[1]) + (z4[2] + z4[3])), rs);
     // ---- collection threshold ----
     if (thr_path) {
-      // k-th largest per-thread maximum: a lower bound of the chunk's k-th value
-      block_sort_desc(tmax, kCT);
-      tau = tmax[prm.top_k - 1];
-      if (!(tau > RL_NEG_INF)) tau = -3.402823466e38f;  // fewer than k threads hold a value: keep all
+      tau = block_kth_lower_bound(mx, prm.top_k, rs);
+      if (!(tau > RL_NEG_INF)) tau = -3.402823466e38f;  // too few values: keep all
     } else {
       // first bin whose cumulative count reaches kKbig
-      uint32_t c0 = cnt[2 * tid], c1 = cnt[2 * tid + 1];
+      uint32_t c[kBinsPT];
+      uint32_t csum = 0;
+#pragma unroll
+      for (int q = 0; q < kBinsPT; ++q) {
+        const int b = static_cast<int>(threadIdx.x) * kBinsPT + q;
+        c[q] = b < kNB ? cnt[b] : 0u;
+        csum += c[q];
+        if (c[q] > static_cast<uint32_t>(kBinCntSafe)) binovf = 1;
+      }
       double tot;
-      const double incl = block_scan_d(static_cast<double>(c0 + c1), rs, &tot);
-      const double excl = incl - static_cast<double>(c0 + c1);
+      const double incl = block_scan_d(static_cast<double>(csum), rs, &tot);
+      double run = incl - static_cast<double>(csum);
       int bfound = INT_MAX;
-      if (excl < kKbig && excl + c0 >= kKbig) bfound = 2 * tid;
-      else if (excl + c0 < kKbig && incl >= kKbig) bfound = 2 * tid + 1;
+#pragma unroll
+      for (int q = 0; q < kBinsPT; ++q) {
+        if (run < kKbig && run + c[q] >= kKbig && bfound == INT_MAX)
+          bfound = static_cast<int>(threadIdx.x) * kBinsPT + q;
+        run += c[q];
+      }
       bfound = block_min_i(bfound, rs);
+      binovf = block_or_i(binovf, rs);
       if (bfound == INT_MAX) {
-        // fewer than kKbig elements in the window: keep the window, and all
-        // of the chunk when nothing lies below it
+        // fewer than kKbig logits in the window: keep the window, and all of
+        // the chunk when nothing lies below it
         athr = (static_cast<int>(tot) >= nallow_c) ? INT_MIN : babs_m - (kNB - 1);
       } else {
         athr = babs_m - bfound;
@@ -637,41 +652,35 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     }
     // ---- P3: candidate keys into the workspace ----
     uint64_t* cdst = ws.cands + (static_cast<int64_t>(row) * ws.smax + chunk) * kCapC;
-    for (int gb = warp * 32; gb < ngroups; gb += kCT) {
-      const int g = gb + lane;
-      float v[G];
-      bool anyt = false;
-      if (g < ngroups) {
-        sl.load(g, v);
 #pragma unroll
-        for (int k = 0; k < G; ++k) {
-          const bool t = thr_path ? (v[k] >= tau) : (v[k] > RL_NEG_INF && babs(v[k], rt) >= athr);
-          anyt |= t && (v[k] > RL_NEG_INF);
-        }
+    for (int q = 0; q < kGPT; ++q) {
+      bool take[4];
+      bool anyt = false;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float x = v[q][k];
+        take[k] = x > RL_NEG_INF && (thr_path ? (x >= tau) : (babs(x, rt) >= athr));
+        anyt |= take[k];
       }
       if (!__any_sync(0xffffffffu, anyt)) continue;
 #pragma unroll
-      for (int k = 0; k < G; ++k) {
-        bool take = false;
-        if (anyt) {
-          const float x = v[k];
-          take = x > RL_NEG_INF && (thr_path ? (x >= tau) : (babs(x, rt) >= athr));
-        }
-        const uint32_t bal = __ballot_sync(0xffffffffu, take);
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t bal = __ballot_sync(0xffffffffu, take[k]);
         if (bal) {
           int base = 0;
           if (lane == 0) base = atomicAdd(&ctrl->ncand, __popc(bal));
           base = __shfl_sync(0xffffffffu, base, 0);
-          if (take) {
+          if (take[k]) {
             const int idx = base + __popc(bal & ((1u << lane) - 1u));
-            if (idx < kCapC) cdst[idx] = cand_key(v[k], static_cast<uint32_t>(start + g * G + k));
+            if (idx < kCapC)
+              cdst[idx] = cand_key(v[q][k], static_cast<uint32_t>(start + (static_cast<int>(threadIdx.x) + q * kCT) * 4 + k));
           }
         }
       }
     }
     if (hist_path) {
       uint32_t* gc = ws.hcnt + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
-      unsigned long long* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
+      uint32_t* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
       for (int b = tid; b < kNB; b += kCT) {
         gc[b] = cnt[b];
         gm[b] = mass[b];
@@ -684,7 +693,7 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     s.m = m_c;
     s.argmax = argmax_c;
     s.nallow = nallow_c;
-    s.flags = bad_c | (timed_out ? 2 : 0) | (ctrl->ncand > kCapC ? 4 : 0);
+    s.flags = bad_c | (timed_out ? 2 : 0) | (ctrl->ncand > kCapC ? 4 : 0) | (binovf ? 8 : 0);
     s.z = z_c;
     s.ncand = min(ctrl->ncand, kCapC);
     s.babs_m = babs_m;
@@ -723,12 +732,12 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   __syncthreads();
   float m = RL_NEG_INF;
   int gargmax = INT_MAX, gallow = 0, gflags = 0;
-  int athr_max = INT_MIN;
+  float tau_max = RL_NEG_INF;
   for (int c = 0; c < S; ++c) {
     const ChunkSum& s = sums_s[c];
     gallow += s.nallow;
     gflags |= s.flags;
-    athr_max = max(athr_max, s.athr);
+    if (s.nallow > 0) tau_max = fmaxf(tau_max, s.tau);
     if (s.m > m) {
       m = s.m;
       gargmax = s.argmax;
@@ -739,7 +748,7 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   int row_st = 0;
   if (gflags & 2) row_st = RL_ERR_TIMEOUT;
   else if ((gflags & 1) || gallow == 0 || !(fabsf(T) < RL_POS_INF)) row_st = RL_ERR_NONFINITE;
-  else if (gflags & 4) row_st = RL_ERR_UNSUPPORTED;
+  else if (gflags & 12) row_st = RL_ERR_UNSUPPORTED;
 
   auto finish = [&](int status, int token, float prob) {
     if (tid == 0) {
@@ -773,7 +782,10 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   const float u = a.uniforms[row];
   const int K = (prm.top_k > 0 && prm.top_k < gallow) ? prm.top_k : gallow;
   const bool mass_mode = prm.top_p < 1.0f;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(data);  // the chunk is no longer needed
+  uint64_t* keys = reinterpret_cast<uint64_t*>(data);         // kMergeCap / 2 keys
+  uint64_t* keys2 = keys + kMergeCap / 2;                     // kMergeCap / 2 keys
+  double* gcnt = reinterpret_cast<double*>(keys + kMergeCap);  // kNB (histogram path)
+  double* gmass = gcnt + kNB;                                  // kNB
   if (tid == 0) {
     Walk& w = *wk;
     w.phase = 0;
@@ -790,33 +802,51 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     w.t2 = static_cast<double>(prm.top_p) * Z;
     w.S = 0.0;
     w.t3 = 0.0;
+    ctrl->nsel = 0;
   }
   __syncthreads();
 
   if (thr_path) {
-    // ---- merge the candidate lists, sort, exact top-k / top-p / draw ----
-    int off = 0;
+    // ---- the row's top-k: candidates >= the largest chunk threshold ----
+    // (the row's k-th value >= every chunk's k-th value >= that chunk's tau)
     for (int c = 0; c < S; ++c) {
       const int n = sums_s[c].ncand;
       const uint64_t* srcc = ws.cands + (static_cast<int64_t>(row) * ws.smax + c) * kCapC;
-      for (int i = tid; i < n && off + i < kMergeCap; i += kCT) keys[off + i] = __ldcg(srcc + i);
-      off += n;
+      for (int i = tid; i < n; i += kCT) {
+        const uint64_t key = __ldcg(srcc + i);
+        if (key_val(key) >= tau_max) {
+          const int idx = atomicAdd(&ctrl->nsel, 1);
+          if (idx < kMergeCap / 2) keys[idx] = key;
+        }
+      }
     }
-    if (off > kMergeCap) {
+    __syncthreads();
+    int n = ctrl->nsel;
+    if (n > kMergeCap / 2) {
       finish(RL_ERR_UNSUPPORTED, -1, 0.0f);
       return;
     }
-    const int P = pow2_ceil(off);
-    for (int i = off + tid; i < P; i += kCT) keys[i] = 0ull;
-    __syncthreads();
-    block_sort_desc(keys, P);
-    const int nlist = min(K, off);
+    // tighten once more on the merged keys, then rank-sort the survivors
+    {
+      float tm = RL_NEG_INF;
+      for (int i = tid; i < n; i += kCT) tm = fmaxf(tm, key_val(keys[i]));
+      float t2 = block_kth_lower_bound(tm, K, rs);
+      if (!(t2 > RL_NEG_INF)) t2 = -3.402823466e38f;
+      if (tid == 0) ctrl->nsel = 0;
+      __syncthreads();
+      for (int i = tid; i < n; i += kCT) {
+        const uint64_t key = keys[i];
+        if (key_val(key) >= t2) keys2[atomicAdd(&ctrl->nsel, 1)] = key;
+      }
+      __syncthreads();
+      n = ctrl->nsel;
+    }
+    const int nlist = min(K, n);
+    rank_sort(keys2, n, keys, nlist);  // keys[0..nlist): the top-k, descending
     double cum_at = 0.0;
     const int f = sweep(keys, nlist, *wk, m, rt, 0, rs, &cum_at);
     const int cut = (f == INT_MAX) ? nlist - 1 : f;
     if (f == INT_MAX) {
-      // cumulative mass never reached top_p inside the list (rounding): the
-      // list end is the cutoff; recompute its cumulative mass
       double tot = 0.0;
       for (int c0 = 0; c0 < nlist; c0 += kCT) {
         const int j = c0 + tid;
@@ -848,38 +878,53 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   }
 
   // ---- histogram path: merge the chunk histograms on the row's grid ----
+  // Row bin j holds absolute bin A = Bmax - j. A logit of bin A has mass
+  // e = e_bin * 2^(((A + 1)/cb - m) * log2(e)/T), e_bin its bin-relative mass.
   const int Bmax = babs(m, rt);
-  double* gcnt = reinterpret_cast<double*>(smem + kOffCnt);
-  double* gmass = reinterpret_cast<double*>(smem + kOffMass);
   {
-    double c2[2] = {0.0, 0.0}, m2[2] = {0.0, 0.0};
-    for (int c = 0; c < S; ++c) {
-      const ChunkSum& s = sums_s[c];
-      if (s.nallow == 0) continue;
-      const int shift = Bmax - s.babs_m;
-      const double f = exp2((static_cast<double>(s.m) - static_cast<double>(m)) * (kLog2e / static_cast<double>(T))) /
-                       kMassScale;
-      const uint32_t* gc = ws.hcnt + (static_cast<int64_t>(row) * ws.smax + c) * kNB;
-      const unsigned long long* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + c) * kNB;
+    const double cl = kLog2e / static_cast<double>(T);
+    const double cbd = static_cast<double>(rt.cb);
+    double cq[kBinsPT], mq[kBinsPT];
+    double csum = 0.0, msum = 0.0;
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int i = 2 * tid + q - shift;
-        if (i >= 0 && i < kNB) {
-          c2[q] += static_cast<double>(__ldcg(gc + i));
-          m2[q] += static_cast<double>(__ldcg(gm + i)) * f;
+    for (int q = 0; q < kBinsPT; ++q) {
+      const int j = static_cast<int>(threadIdx.x) * kBinsPT + q;
+      double cc = 0.0, mm = 0.0;
+      if (j < kNB) {
+        const int A = Bmax - j;
+        for (int c = 0; c < S; ++c) {
+          const ChunkSum& s = sums_s[c];
+          if (s.nallow == 0) continue;
+          const int i = s.babs_m - A;
+          if (i >= 0 && i < kNB) {
+            const int64_t base = (static_cast<int64_t>(row) * ws.smax + c) * kNB + i;
+            cc += static_cast<double>(__ldcg(ws.hcnt + base));
+            mm += static_cast<double>(__ldcg(ws.hmass + base));
+          }
         }
+        mm *= exp2(((static_cast<double>(A) + 1.0) / cbd - static_cast<double>(m)) * cl) / static_cast<double>(kMassQ);
       }
+      cq[q] = cc;
+      mq[q] = mm;
+      csum += cc;
+      msum += mm;
     }
     double tc, tm;
-    const double ci = block_scan_d(c2[0] + c2[1], rs, &tc);
-    const double mi = block_scan_d(m2[0] + m2[1], rs, &tm);
-    gcnt[2 * tid] = ci - c2[1];
-    gcnt[2 * tid + 1] = ci;
-    gmass[2 * tid] = mi - m2[1];
-    gmass[2 * tid + 1] = mi;
+    double ci = block_scan_d(csum, rs, &tc) - csum;
+    double mi = block_scan_d(msum, rs, &tm) - msum;
+#pragma unroll
+    for (int q = 0; q < kBinsPT; ++q) {
+      const int j = static_cast<int>(threadIdx.x) * kBinsPT + q;
+      ci += cq[q];
+      mi += mq[q];
+      if (j < kNB) {
+        gcnt[j] = ci;
+        gmass[j] = mi;
+      }
+    }
     __syncthreads();
   }
-  // gcnt / gmass: inclusive cumulative counts / masses per row bin j (absolute bin Bmax - j)
+  // gcnt / gmass: inclusive cumulative counts / masses per row bin
   const bool need_q1 = K < gallow;
   auto first_bin = [&](int kind, double target) -> int {
     // kind 0: count >= target; 1: mass >= target; 2: mass > target
@@ -910,8 +955,9 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
   // ---- bin-by-bin walk ----
   int32_t* hid = reinterpret_cast<int32_t*>(smem + kOffHist);  // finisher history table (sorted)
   float* hval = reinterpret_cast<float*>(smem + kOffPen);
-  uint64_t* bkeys = keys;                                       // keys of one bin (<= kMergeCap)
-  int nh = -1;  // history table built on first re-read
+  uint64_t* bkeys = keys;   // keys of one bin (<= kMergeCap / 2)
+  uint64_t* skeys = keys2;  // the same, sorted
+  int nh = -1;              // history table built on the first re-read
   for (int round = 0; round < kMaxRounds; ++round) {
     if (bin >= kNB) {
       if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;  // beyond the 64-nat window
@@ -931,73 +977,51 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
           const uint64_t key = __ldcg(srcc + i);
           if (babs(key_val(key), rt) == A) {
             const int idx = atomicAdd(&ctrl->nbin, 1);
-            if (idx < kMergeCap) bkeys[idx] = key;
+            if (idx < kMergeCap / 2) bkeys[idx] = key;
           }
         }
       }
     } else {
-      // re-read the row (L2-resident) for the elements of bin A
+      // re-read the row (L2-resident) for the logits of bin A
       if (nh < 0) {
         // sorted, de-duplicated history ids with their penalised values
         int hlr = a.hist ? a.hist_len[row] : 0;
         hlr = max(0, min(hlr, min(a.hist_stride, kHmax)));
-        const int P = pow2_ceil(max(hlr, 1));
-        for (int j = tid; j < P; j += kCT) {
-          uint64_t h = ~0ull;
-          if (j < hlr) {
-            const int hv = a.hist[static_cast<int64_t>(row) * a.hist_stride + j] - a.vocab_offset;
-            if (hv >= 0 && hv < V) h = static_cast<uint64_t>(hv);
-          }
-          bkeys[j] = h;
+        if (tid == 0) ctrl->nsel = 0;
+        __syncthreads();
+        for (int j = tid; j < hlr; j += kCT) {
+          const int hv = a.hist[static_cast<int64_t>(row) * a.hist_stride + j] - a.vocab_offset;
+          if (hv >= 0 && hv < V) bkeys[atomicAdd(&ctrl->nsel, 1)] = (static_cast<uint64_t>(hv) << 32) | j;
         }
         __syncthreads();
-        block_sort_desc(bkeys, P);  // descending; position j ascending is P-1-j
+        const int nrows = ctrl->nsel;
+        rank_sort(bkeys, nrows, skeys, nrows);  // descending (id, position)
         const E* xr0 = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
-        // each thread owns ascending positions tid and tid + kCT (P <= kHmax <= 2 kCT)
-        int fl[2] = {0, 0};
-        uint64_t idv[2] = {~0ull, ~0ull};
-        int cntv[2] = {0, 0};
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int j = tid + q * kCT;
-          if (j < P) {
-            const uint64_t h = bkeys[P - 1 - j];
-            if (h != ~0ull && (j == 0 || bkeys[P - j] != h)) {
-              fl[q] = 1;
-              idv[q] = h;
-              int c = 0;
-              for (int t = j; t < P && bkeys[P - 1 - t] == h; ++t) ++c;
-              cntv[q] = c;
-            }
+        if (tid == 0) ctrl->nsel = 0;
+        __syncthreads();
+        // ascending position p is skeys[nrows - 1 - p]; the first of each id run applies
+        for (int p = tid; p < nrows; p += kCT) {
+          const int id = static_cast<int>(skeys[nrows - 1 - p] >> 32);
+          if (p > 0 && static_cast<int>(skeys[nrows - p] >> 32) == id) continue;
+          int c = 0;
+          for (int q = p; q < nrows && static_cast<int>(skeys[nrows - 1 - q] >> 32) == id; ++q) ++c;
+          float v;
+          if constexpr (sizeof(E) == 4) {
+            v = __ldcg(xr0 + id);
+          } else {
+            v = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr0) + id));
           }
+          const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
+          const float pv = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
+          bkeys[atomicAdd(&ctrl->nsel, 1)] = (static_cast<uint64_t>(static_cast<uint32_t>(id)) << 32) | __float_as_uint(pv);
         }
-        // output positions in ascending order: positions 0..kCT-1, then kCT..P-1
-        {
-          double t0;
-          const double i0 = block_scan_d(static_cast<double>(fl[0]), rs, &t0);
-          double t1;
-          const double i1 = block_scan_d(static_cast<double>(fl[1]), rs, &t1);
-          const int p0 = static_cast<int>(i0) - fl[0];
-          const int p1 = static_cast<int>(t0) + static_cast<int>(i1) - fl[1];
-          auto pen = [&](int id, int c) {
-            float v;
-            if constexpr (sizeof(E) == 4) {
-              v = __ldcg(xr0 + id);
-            } else {
-              v = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr0) + id));
-            }
-            const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
-            return sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
-          };
-          if (fl[0]) {
-            hid[p0] = static_cast<int32_t>(idv[0]);
-            hval[p0] = pen(static_cast<int>(idv[0]), cntv[0]);
-          }
-          if (fl[1]) {
-            hid[p1] = static_cast<int32_t>(idv[1]);
-            hval[p1] = pen(static_cast<int>(idv[1]), cntv[1]);
-          }
-          nh = static_cast<int>(t0 + t1);
+        __syncthreads();
+        nh = ctrl->nsel;
+        rank_sort(bkeys, nh, skeys, nh);  // descending id
+        for (int j = tid; j < nh; j += kCT) {
+          const uint64_t kv = skeys[nh - 1 - j];  // ascending id
+          hid[j] = static_cast<int32_t>(kv >> 32);
+          hval[j] = __uint_as_float(static_cast<uint32_t>(kv & 0xffffffffu));
         }
         if (tid == 0) ctrl->nbin = 0;
         __syncthreads();
@@ -1015,20 +1039,17 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
         if (!(x > RL_NEG_INF)) continue;
         if (babs(x, rt) == A) {
           const int idx = atomicAdd(&ctrl->nbin, 1);
-          if (idx < kMergeCap) bkeys[idx] = cand_key(x, static_cast<uint32_t>(i));
+          if (idx < kMergeCap / 2) bkeys[idx] = cand_key(x, static_cast<uint32_t>(i));
         }
       }
     }
     __syncthreads();
     const int nb = ctrl->nbin;
-    if (nb > kMergeCap) {
+    if (nb > kMergeCap / 2) {
       if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;
       break;
     }
-    const int P = pow2_ceil(max(nb, 1));
-    for (int i = nb + tid; i < P; i += kCT) bkeys[i] = 0ull;
-    __syncthreads();
-    block_sort_desc(bkeys, P);
+    rank_sort(bkeys, nb, skeys, nb);
     if (tid == 0) {
       wk->count_before = bin ? static_cast<long long>(gcnt[bin - 1]) : 0;
       wk->mass_before = bin ? gmass[bin - 1] : 0.0;
@@ -1037,7 +1058,7 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     int next = INT_MAX;
     double cum_at = 0.0;
     if (wk->phase == 0) {
-      const int f = sweep(bkeys, nb, *wk, m, rt, 0, rs, &cum_at);
+      const int f = sweep(skeys, nb, *wk, m, rt, 0, rs, &cum_at);
       if (f != INT_MAX) {
         if (tid == 0) {
           wk->cut_in_seg = 1;
@@ -1058,13 +1079,13 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
         const int b3 = first_bin(2, wk->t3);
         next = (b3 < bin) ? b3 : max(0, bin - 1);
       } else {
-        const int d = sweep(bkeys, nb, *wk, m, rt, 1, rs, &cum_at);
+        const int d = sweep(skeys, nb, *wk, m, rt, 1, rs, &cum_at);
         if (tid == 0) {
           int j = -1;
           if (d != INT_MAX && (!wk->cut_in_seg || d <= wk->cut_idx)) j = d;
           else if (wk->cut_in_seg) j = wk->cut_idx;
           if (j >= 0) {
-            const uint64_t key = bkeys[j];
+            const uint64_t key = skeys[j];
             wk->token = static_cast<int>(key_id(key));
             wk->prob = static_cast<float>(static_cast<double>(exact_e(key_val(key), m, rt)) / wk->S);
             wk->phase = 2;
@@ -1079,7 +1100,7 @@ __global__ void __launch_bounds__(kCT, 2) spec_chunk_kernel(const SpecArgs a) {
     bin = next;
   }
   __syncthreads();
-  if (a.list_len && tid == 0) a.list_len[row] = -1;  // lists are reported on the threshold path only
+  if (a.list_len && tid == 0) a.list_len[row] = -1;  // lists are reported on the threshold path
   const Walk& w = *wk;
   if (w.phase == 2 && w.status == 0) finish(0, w.token, w.prob);
   else finish(w.status ? w.status : RL_ERR_UNSUPPORTED, -1, 0.0f);
@@ -1097,12 +1118,9 @@ static cudaError_t launch_typed(const SpecArgs& a, int S, int smem, cudaStream_t
   return cudaGetLastError();
 }
 
-cudaError_t launch_spec(const SpecArgs& args_in, int dtype, cudaStream_t stream) {
-  SpecArgs a = args_in;
-  const int es = dtype == RL_BF16 ? 2 : 4;
-  a.chunk_elems = kChunkBytes / es;
-  const int S = spec_chunks(a.V, es);
-  const int smem = spec_smem_bytes(es);
+cudaError_t launch_spec(const SpecArgs& a, int dtype, cudaStream_t stream) {
+  const int S = spec_chunks(a.V);
+  const int smem = spec_smem_bytes(dtype == RL_BF16 ? 2 : 4);
   if (dtype == RL_BF16) return launch_typed<uint16_t>(a, S, smem, stream);
   return launch_typed<float>(a, S, smem, stream);
 }

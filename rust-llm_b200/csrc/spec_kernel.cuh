@@ -8,9 +8,10 @@
 
 namespace rl {
 
-constexpr int kCT = 512;             // threads per chunk CTA
+constexpr int kCT = 384;             // threads per chunk CTA (three CTAs per SM)
 constexpr int kCW = kCT / 32;        // warps per chunk CTA
-constexpr int kChunkBytes = 65536;   // logits bytes per chunk (16384 f32 / 32768 bf16)
+constexpr int kCE = 12288;           // logits per chunk (48 KB f32, 24 KB bf16)
+constexpr int kGPT = kCE / kCT / 4;  // groups of 4 logits per thread (8)
 constexpr int kNB = 1024;            // histogram bins per chunk (absolute grid)
 constexpr float kRbin = 16.0f;       // bins per nat of (x - m) / T
 constexpr int kKthr = 128;           // top_k <= kKthr: thread-maximum threshold path
@@ -20,16 +21,16 @@ constexpr int kSmax = 64;            // max chunks per row
 constexpr int kHmax = 1024;          // max history entries per row
 constexpr int kNPiece = 4;           // bulk-copy pieces per chunk
 constexpr int kMaxRounds = 16;       // bin rounds of the finishing walk
-constexpr int kMergeCap = 8192;      // merged keys the finishing CTA holds (64 KB)
-constexpr double kMassScale = 1099511627776.0;  // 2^40 fixed point for bin masses
-constexpr float kMassScaleF = 1099511627776.0f;
+constexpr int kMergeCap = 4096;      // keys the finishing CTA holds (32 KB)
+constexpr float kMassQ = 1048576.0f; // 2^20 fixed point of bin-relative masses (u32)
+constexpr int kBinCntSafe = 3800;    // a bin holding more elements may overflow its u32 mass
 
 // Per-chunk summary written by every chunk CTA.
 struct ChunkSum {
-  float m;       // chunk max over allowed finite (penalised) logits
+  float m;       // chunk max over allowed finite (penalised) logits (-inf: none)
   int argmax;    // lowest row-local id at that max
   int nallow;    // allowed finite logits in the chunk
-  int flags;     // bit0 non-finite input, bit1 copy timeout, bit2 candidate overflow
+  int flags;     // bit0 non-finite, bit1 copy timeout, bit2 candidate overflow, bit3 bin overflow
   double z;      // sum of exp((x - m) / T) over the chunk, relative to m
   int ncand;     // candidate keys written
   int babs_m;    // absolute bin of m
@@ -42,8 +43,8 @@ struct Workspace {
   int32_t* row_done;           // [max_batch] arrival counters, reset by the finisher
   ChunkSum* sums;              // [max_batch * smax]
   uint64_t* cands;             // [max_batch * smax * kCapC]
-  uint32_t* hcnt;              // [max_batch * smax * kNB]
-  unsigned long long* hmass;   // [max_batch * smax * kNB]
+  uint32_t* hcnt;              // [max_batch * smax * kNB] counts per chunk bin
+  uint32_t* hmass;             // [max_batch * smax * kNB] bin-relative masses, 2^20 fixed point
   int smax;
 };
 
@@ -72,12 +73,11 @@ struct SpecArgs {
   int list_cap;
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
   int mode;
-  int chunk_elems;   // elements per chunk
   Workspace ws;
 };
 
 int spec_smem_bytes(int es);
-int spec_chunks(int V, int es);
+int spec_chunks(int V);
 cudaError_t launch_spec(const SpecArgs& args, int dtype, cudaStream_t stream);
 
 }  // namespace rl

@@ -24,7 +24,7 @@ rl_status alloc_workspace(rl_sampler* h) {
             dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
             dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
   // chunked spec kernel workspace: f32 chunks are the smallest (most chunks)
-  const int smax = (h->max_vocab + (kChunkBytes / 4) - 1) / (kChunkBytes / 4);
+  const int smax = (h->max_vocab + kCE - 1) / kCE;
   h->ws.smax = smax;
   const size_t rows_chunks = B * static_cast<size_t>(smax);
   ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, rows_chunks) &&
