@@ -64,6 +64,8 @@ rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max
   if (max_batch <= 0 || max_vocab <= 0 || max_history < 0)
     return fail(RL_ERR_INVALID_ARG, "rl_sampler_create: limits must be positive");
   if (max_batch > 65535) return fail(RL_ERR_SHAPE, "rl_sampler_create: max_batch > 65535");
+  if (max_vocab > (1 << 21) - rl::kCE)
+    return fail(RL_ERR_SHAPE, "rl_sampler_create: max_vocab %d > %d", max_vocab, (1 << 21) - rl::kCE);
   if (max_history > rl::kHmax)
     return fail(RL_ERR_SHAPE, "rl_sampler_create: max_history %d > %d", max_history, rl::kHmax);
   int ndev = 0;
@@ -133,8 +135,6 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: mask_stride %lld < ceil(V/32)", (long long)mask_stride);
   if (list_len && (!list_ids || !list_probs || list_cap <= 0))
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list buffers required");
-  if (rl::spec_chunks(V) > h->ws.smax)
-    return fail(RL_ERR_SHAPE, "rl_sample_batch: V=%d beyond the handle's max_vocab", V);
   DeviceGuard g(h->device);
   if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
   rl::SpecArgs a = {};
@@ -157,9 +157,8 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.list_len = list_len;
   a.list_cap = list_cap;
   a.vocab_offset = vocab_offset;
-  a.mode = rl::kModeSample;
   a.ws = h->ws;
-  cudaError_t e = rl::launch_spec(a, dtype, static_cast<cudaStream_t>(stream));
+  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
   return RL_OK;
 }

@@ -9,24 +9,29 @@
 //   strict '<' draw            Decoder::sample_multinomial   decoder.rs:146-158
 //   empty allowed set -> all   Sampler::sample_with_grammar  decoder.rs:362-364
 //
-// Design (B200, sm_100a). One launch, grid (chunks, rows), three CTAs per SM.
-// Every CTA streams one 48 KB chunk (12288 logits) of one row into shared
-// memory with bulk async copies (cp.async.bulk + mbarrier) -- the only HBM
-// read of those logits -- applies the row's penalties and mask in place, and
-// reduces the chunk to a summary in the handle's workspace. Each pass keeps
-// its 32 values per thread in registers (8 unrolled 16-byte loads):
-//   P1  chunk max, allowed count, non-finite check, per-thread maxima
-//   P2  Z partial: sum of 2^((x - m_c) * log2(e)/T) (split constant, ex2)
-//       histogram rows also bin every logit on an absolute grid (16 bins per
-//       nat) and add its bin-relative mass (u32 fixed point; u32 atomics)
-//   P3  candidate keys (value desc, id asc) of every logit that can be in the
-//       row's top-k: x >= tau, tau from the per-thread maxima (top_k <= 128),
-//       or the chunk's top 512 by the histogram.
-// The last CTA of a row to arrive (arrival counter) finishes the row: global
-// max and Z, the exact top-k list (tightened threshold + rank sort, exact
-// exp), the inclusive top-p cutoff and the draw. Rows without a small top_k
-// walk the merged histogram bin by bin; a bin not covered by the candidate
-// lists is re-read from the row (L2-resident by then).
+// Design (B200, sm_100a). A persistent launch of at most two CTAs per SM; a
+// row is split into segments of 4096-logit chunks and each CTA owns a list of
+// (row, segment) items. A CTA has three roles:
+//   * one copy warp streams the chunks through a ring of kNS shared-memory
+//     stages with bulk async copies (cp.async.bulk + full/empty mbarrier
+//     pairs) -- the only HBM read of the logits;
+//   * one preparation warp builds each item's row data one item ahead:
+//     parameters, the allowed-mask flag and the history table (sorted,
+//     de-duplicated ids with their counts, for the penalties);
+//   * eight consumer warps each own a fixed 512-logit slice of every chunk
+//     and keep their running state in registers, with no block barrier per
+//     chunk: max, allowed count, non-finite check, the softmax sum (per-lane
+//     reference, ex2), the candidate keys of the row's top list (per-warp
+//     buffer compacted by a warp radix select, bound shared across warps)
+//     and, for rows without a small top_k, a windowed histogram of
+//     bin-relative masses (16 bins per nat) for deep top-p cutoffs.
+// At the end of an item the consumers select the item's top-128 keys; the
+// last CTA of a row to finish (the only one when a row is one segment)
+// merges the row and writes its token: exact exp over the sorted list, the
+// inclusive top-p cutoff and the draw. When the cutoff or the draw lies
+// below the list, the merged histogram locates its bin and the row is
+// re-read for that bin's logits; an exact radix walk over re-reads of the
+// row covers what the histogram cannot.
 #include <climits>
 
 #include "common.cuh"
@@ -34,19 +39,17 @@
 
 namespace rl {
 
-constexpr uint16_t kBf16NegInf = 0xff80;
 constexpr double kLog2e = 1.4426950408889634074;
-constexpr int kBinsPT = (kNB + kCT - 1) / kCT;  // histogram bins per thread in scans (3)
 
 // ---------------------------------------------------------------------------
 // Row arithmetic
 // ---------------------------------------------------------------------------
 struct RowT {
-  float T, rT;       // temperature, RN(1/T)
-  bool fast_div;     // Markstein division valid for T
-  float c_hi, c_lo;  // log2(e)/T split in two floats
-  float cb;          // absolute bins per logit unit: kRbin / T
-  float dlt;         // log2(e) / kRbin: log2 width of one bin
+  float T, rT;         // temperature, RN(1/T)
+  int fast_div;        // Markstein division valid for T
+  float c;             // log2(e)/T (bulk sums)
+  float cb_hi, cb_lo;  // kRbin / T split in two floats
+  float dlt;           // log2(e) / kRbin
 };
 
 __device__ __forceinline__ RowT make_rowt(float T) {
@@ -54,10 +57,10 @@ __device__ __forceinline__ RowT make_rowt(float T) {
   r.T = T;
   r.rT = __frcp_rn(T);
   r.fast_div = (T >= 9.5367431640625e-07f) && (T <= 1048576.0f);
-  const double c = kLog2e / static_cast<double>(T);
-  r.c_hi = static_cast<float>(c);
-  r.c_lo = static_cast<float>(c - static_cast<double>(r.c_hi));
-  r.cb = div_rn(kRbin, T);
+  r.c = static_cast<float>(kLog2e / static_cast<double>(T));
+  const double cb = static_cast<double>(kRbin) / static_cast<double>(T);
+  r.cb_hi = static_cast<float>(cb);
+  r.cb_lo = static_cast<float>(cb - static_cast<double>(r.cb_hi));
   r.dlt = static_cast<float>(kLog2e / static_cast<double>(kRbin));
   return r;
 }
@@ -73,1056 +76,1925 @@ __device__ __forceinline__ float ex2_approx(float t) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
   return y;
 }
-// exp((x - m)/T) for bulk sums: split-constant exponent, hardware ex2.
-__device__ __forceinline__ float fast_e(float x, float m, const RowT& r) {
-  const float d = sub_rn(x, m);
-  return ex2_approx(fmaf(d, r.c_lo, d * r.c_hi));
+// Absolute histogram bin of x: floor(x * kRbin / T), as a float.
+__device__ __forceinline__ float bin_of(float x, const RowT& r) { return floorf(__fmul_rn(x, r.cb_hi)); }
+// Mass of x relative to the top edge of its bin af: exp(x/T - (af+1)/kRbin).
+__device__ __forceinline__ float bin_rel_mass(float x, float af, const RowT& r) {
+  const float yh = __fmul_rn(x, r.cb_hi);
+  const float yl = __fmaf_rn(x, r.cb_hi, -yh) + x * r.cb_lo;
+  return ex2_approx(((yh - af) + yl - 1.0f) * r.dlt);
 }
-// Absolute bin of a logit: monotone in x, identical wherever it is computed.
-__device__ __forceinline__ int babs(float x, const RowT& r) { return __float2int_rd(__fmul_rn(x, r.cb)); }
-
-// ---------------------------------------------------------------------------
-// Chunk access: 4 consecutive logits per 16-byte (f32) / 8-byte (bf16) load.
-// ---------------------------------------------------------------------------
-template <typename E>
-__device__ __forceinline__ void load4(const E* data, int g, float (&v)[4]);
-template <>
-__device__ __forceinline__ void load4<float>(const float* data, int g, float (&v)[4]) {
-  const float4 q = reinterpret_cast<const float4*>(data)[g];
-  v[0] = q.x;
-  v[1] = q.y;
-  v[2] = q.z;
-  v[3] = q.w;
-}
-template <>
-__device__ __forceinline__ void load4<uint16_t>(const uint16_t* data, int g, float (&v)[4]) {
-  const uint2 q = reinterpret_cast<const uint2*>(data)[g];
-  v[0] = __uint_as_float(q.x << 16);
-  v[1] = __uint_as_float(q.x & 0xffff0000u);
-  v[2] = __uint_as_float(q.y << 16);
-  v[3] = __uint_as_float(q.y & 0xffff0000u);
-}
-// all kGPT groups of this thread (group g = tid + k * kCT)
-template <typename E>
-__device__ __forceinline__ void load_all(const E* data, float (&v)[kGPT][4]) {
-#pragma unroll
-  for (int k = 0; k < kGPT; ++k) load4<E>(data, threadIdx.x + k * kCT, v[k]);
-}
-
-// ---------------------------------------------------------------------------
-// Block / warp helpers (kCT threads)
-// ---------------------------------------------------------------------------
-struct RedScratch {
-  double d[kCW];
-  float f[kCW];
-  int i[kCW];
-  int j[kCW];
-  double bcast_d;
-  int bcast_i;
-  int pad;
-};
-
-__device__ __forceinline__ double block_sum_d(double v, RedScratch* rs) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  v = warp_sum_d(v);
-  __syncthreads();
-  if (lane == 0) rs->d[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    double t = lane < kCW ? rs->d[lane] : 0.0;
-    t = warp_sum_d(t);
-    if (lane == 0) rs->bcast_d = t;
-  }
-  __syncthreads();
-  return rs->bcast_d;
-}
-
-__device__ __forceinline__ int block_min_i(int v, RedScratch* rs) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
-  __syncthreads();
-  if (lane == 0) rs->i[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int t = lane < kCW ? rs->i[lane] : INT_MAX;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t = min(t, __shfl_xor_sync(0xffffffffu, t, o));
-    if (lane == 0) rs->bcast_i = t;
-  }
-  __syncthreads();
-  return rs->bcast_i;
-}
-
-__device__ __forceinline__ int block_or_i(int v, RedScratch* rs) {
-  v = __any_sync(0xffffffffu, v != 0);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  __syncthreads();
-  if (lane == 0) rs->i[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    int t = lane < kCW ? rs->i[lane] : 0;
-    t = __any_sync(0xffffffffu, t != 0);
-    if (lane == 0) rs->bcast_i = t;
-  }
-  __syncthreads();
-  return rs->bcast_i;
-}
-
-// Inclusive block scan of doubles (one value per thread); *total = block sum.
-__device__ __forceinline__ double block_scan_d(double v, RedScratch* rs, double* total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double n = __shfl_up_sync(0xffffffffu, v, o);
-    if (lane >= o) v += n;
-  }
-  __syncthreads();
-  if (lane == 31) rs->d[warp] = v;
-  __syncthreads();
-  if (warp == 0) {
-    double t = lane < kCW ? rs->d[lane] : 0.0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double n = __shfl_up_sync(0xffffffffu, t, o);
-      if (lane >= o) t += n;
-    }
-    if (lane < kCW) rs->d[lane] = t;
-  }
-  __syncthreads();
-  const double off = warp > 0 ? rs->d[warp - 1] : 0.0;
-  *total = rs->d[kCW - 1];
-  return v + off;
-}
-
-// Descending sort of one float per lane across a warp (bitonic, shuffles).
-__device__ __forceinline__ float warp_sort_desc(float v) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      const float o = __shfl_xor_sync(0xffffffffu, v, j);
-      const bool desc = (lane & k) == 0 || k == 32;
-      const bool lower = (lane & j) == 0;
-      v = (desc == lower) ? fmaxf(v, o) : fminf(v, o);
-    }
-  }
-  return v;
-}
-
-// Lower bound of the k-th largest of the values held one per thread: every
-// warp holds at least ceil(k / kCW) values >= the result, so at least k
-// values are. -inf if some warp holds fewer finite values.
-__device__ __forceinline__ float block_kth_lower_bound(float v, int k, RedScratch* rs) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int j = min((k + kCW - 1) / kCW, 32);
-  const float s = warp_sort_desc(v);
-  const float wj = __shfl_sync(0xffffffffu, s, j - 1);
-  __syncthreads();
-  if (lane == 0) rs->f[warp] = wj;
-  __syncthreads();
-  float t = RL_POS_INF;
-  for (int w = 0; w < kCW; ++w) t = fminf(t, rs->f[w]);
-  return t;
-}
-
-// out[rank] = key for every key of rank < keep (keys unique; rank = number of
-// larger keys): the top `keep` keys in descending order.
-__device__ void rank_sort(const uint64_t* in, int n, uint64_t* out, int keep) {
-  for (int i = threadIdx.x; i < n; i += kCT) {
-    const uint64_t k = in[i];
-    int r = 0;
-    for (int j = 0; j < n; ++j) r += in[j] > k;
-    if (r < keep) out[r] = k;
-  }
-  __syncthreads();
+__device__ __forceinline__ float pen_value(float v, int cnt, float rp, float freq, float pres) {
+  const float x1 = (v < 0.0f) ? mul_rn(v, rp) : div_rn(v, rp);
+  return sub_rn(sub_rn(x1, mul_rn(static_cast<float>(cnt), freq)), pres);
 }
 
 // ---------------------------------------------------------------------------
 // Shared-memory layout
 // ---------------------------------------------------------------------------
-struct Ctrl {
-  int n_local;  // history entries inside the chunk
-  int ncand;    // candidate keys written
+struct ItemMeta {
+  int item, row, seg, c0, c1;
+  int mode;        // 0 greedy, 1 threshold (top_k <= kN), 2 histogram
+  int nkeep;       // candidate keys kept
+  int need_count;  // histogram counts (top_k > kN)
+  int mask_on;     // the row's allowed set is not empty
+  int ntab;        // history table entries
+  int wbins;       // window depth below the anchor top (bins)
+  int top_k;
+  float top_p, u, rp, pres, freq;
+  RowT rt;
+};
+
+struct Ctl {
+  unsigned long long tau_shared;  // item-level candidate bound (max over warps)
+  unsigned long long res_key;
+  long long res_c;
+  double res_d;
+  int abort;
   int is_last;
-  int nsel;     // finisher: keys selected
-  int nbin;     // finisher: keys gathered for the current bin
-  int pad[3];
+  int cnt;
+  int sel_bucket;
+  uint32_t sel_above, sel_cnt;
+  int res_i, res_j;
 };
 
-// Finisher walk state (masses relative to the row max, e-units).
-struct Walk {
-  int phase;       // 0: find the cutoff, 1: find the draw, 2: done
-  int K;           // list length
-  int mass_mode;   // top_p < 1
-  int cut_in_seg;  // the cutoff element is in the current segment
-  int cut_idx;
-  int status;
-  int token;
-  float prob;
-  long long count_before;
-  double mass_before;
-  double Z, t2, S, t3;
+struct Red {
+  double d[kCW];
+  unsigned long long q[kCW];
+  float f[kCW];
+  int i[kCW];
+  uint32_t u[kCW];
 };
 
-constexpr int kOffMbar = 0;
-constexpr int kOffCtrl = 64;
-constexpr int kOffWalk = 128;
+constexpr int kOffBar = 0;                         // 12 mbarriers
+constexpr int kOffCtl = 128;
 constexpr int kOffRed = 256;
-constexpr int kOffCnt = 1024;                  // kNB u32 counts
-constexpr int kOffMass = kOffCnt + kNB * 4;    // kNB u32 masses
-constexpr int kOffHist = kOffMass + kNB * 4;   // kHmax ints (finisher: sorted history ids)
-constexpr int kOffPen = kOffHist + kHmax * 4;  // kHmax floats (finisher: their values)
-constexpr int kOffSums = kOffPen + kHmax * 4;  // kSmax ChunkSum (finisher)
-constexpr int kOffData = ((kOffSums + kSmax * static_cast<int>(sizeof(ChunkSum)) + 127) / 128) * 128;
-constexpr int kDataBytes = kCE * 4;            // f32 chunk; finisher: keys + merged histograms
-static_assert(kMergeCap * 8 + kNB * 16 <= kDataBytes, "finisher region");
-static_assert(sizeof(Walk) <= 128, "walk");
-static_assert(kOffRed + sizeof(RedScratch) <= kOffCnt, "smem header");
+constexpr int kOffWcnt = 512;                      // per-warp candidate counts
+constexpr int kOffMeta = 640;                      // 2 ItemMeta
+constexpr int kOffTopE = 896;                      // kN floats: exact e of the list
+constexpr int kOffTopC = kOffTopE + kN * 4;        // kN doubles: cumulative probabilities
+constexpr int kOffTop = kOffTopC + kN * 8;         // kN keys: the sorted list
+constexpr int kOffSumS = kOffTop + kN * 8;         // kSmax ItemSum (finisher)
+constexpr int kOffSegN = kOffSumS + kSmax * static_cast<int>(sizeof(ItemSum));  // kSmax ints
+constexpr int kOffTab = kOffSegN + kSmax * 4;      // 2 x kHmax u32
+constexpr int kOffHist = kOffTab + 2 * kHmax * 4;  // mass[kNB] + cnt[kNB] u32
+constexpr int kOffRadix = kOffHist + 2 * kNB * 4;  // kCW x 256 u32 radix bins
+constexpr int kOffWbuf = kOffRadix + kCW * 256 * 4;   // kCW x kWcap keys
+constexpr int kOffMask = kOffWbuf + kCW * kWcap * 8;  // kNS x kMaskWords u32
+constexpr int kOffMscr = kOffMask + kNS * kMaskWords * 4;  // row preparation: 2 x kHmax ids + 128 counters
+constexpr int kOffStage = ((kOffMscr + 2 * kHmax * 4 + 128 * 4 + 127) / 128) * 128;
+constexpr int kSmemBytes = kOffStage + kNS * kStageBytes;
+// Finisher reuse: the collect buffer spans the histogram and the radix bins;
+// the merged histogram (two kNB double arrays) the warp buffers.
+static_assert(kOffRadix + kCW * 256 * 4 - kOffHist >= kCollect * 8, "collect buffer");
+static_assert(kCW * kWcap * 8 >= 2 * kNB * 8, "merged histogram");
+static_assert(256 * (4 + 8 + 8) <= kCW * 256 * 4, "radix walk bins");
+static_assert(sizeof(ItemMeta) <= 128 && sizeof(Ctl) <= 128 && sizeof(Red) <= 256, "smem header");
+static_assert(kOffMeta + 2 * 128 <= kOffTopE, "meta");
+static_assert(kOffStage % 128 == 0 && kOffMask % 16 == 0 && kOffSumS % 8 == 0 && kOffHist % 16 == 0, "alignment");
+static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
 
-int spec_smem_bytes(int /*es*/) { return kOffData + kDataBytes; }
-int spec_chunks(int V) { return (V + kCE - 1) / kCE; }
+int spec_smem_bytes() { return kSmemBytes; }
+
+struct Smem {
+  uint64_t* full;    // [kNS]
+  uint64_t* empty;   // [kNS]
+  uint64_t* mfull;   // [2]
+  uint64_t* mempty;  // [2]
+  Ctl* ctl;
+  Red* red;
+  int* wcnt;
+  ItemMeta* meta;
+  float* tope;
+  double* topc;
+  uint64_t* top;
+  ItemSum* sums;
+  int* segn;
+  uint32_t* tab;
+  uint32_t* hmass;
+  uint32_t* hcnt;
+  uint32_t* radix;
+  uint64_t* wbuf;
+  uint32_t* maskst;
+  int* mscr;
+  unsigned char* stage;
+};
+extern __shared__ __align__(128) unsigned char g_smem[];
+__device__ __forceinline__ Smem smem_map() {
+  unsigned char* s = g_smem;
+  Smem m;
+  m.full = reinterpret_cast<uint64_t*>(s + kOffBar);
+  m.empty = m.full + kNS;
+  m.mfull = m.empty + kNS;
+  m.mempty = m.mfull + 2;
+  m.ctl = reinterpret_cast<Ctl*>(s + kOffCtl);
+  m.red = reinterpret_cast<Red*>(s + kOffRed);
+  m.wcnt = reinterpret_cast<int*>(s + kOffWcnt);
+  m.meta = reinterpret_cast<ItemMeta*>(s + kOffMeta);
+  m.tope = reinterpret_cast<float*>(s + kOffTopE);
+  m.topc = reinterpret_cast<double*>(s + kOffTopC);
+  m.top = reinterpret_cast<uint64_t*>(s + kOffTop);
+  m.sums = reinterpret_cast<ItemSum*>(s + kOffSumS);
+  m.segn = reinterpret_cast<int*>(s + kOffSegN);
+  m.tab = reinterpret_cast<uint32_t*>(s + kOffTab);
+  m.hmass = reinterpret_cast<uint32_t*>(s + kOffHist);
+  m.hcnt = m.hmass + kNB;
+  m.radix = reinterpret_cast<uint32_t*>(s + kOffRadix);
+  m.wbuf = reinterpret_cast<uint64_t*>(s + kOffWbuf);
+  m.maskst = reinterpret_cast<uint32_t*>(s + kOffMask);
+  m.mscr = reinterpret_cast<int*>(s + kOffMscr);
+  m.stage = s + kOffStage;
+  return m;
+}
 
 // ---------------------------------------------------------------------------
-// Finisher pieces
+// Small helpers
 // ---------------------------------------------------------------------------
-// Sweep over n sorted keys: first index j whose cumulative mass
-// (w.mass_before + e_0 + ... + e_j, e exact) meets the condition. mode 0:
-// cutoff (list position K-1, or cum >= t2 in mass mode); mode 1: cum > t3.
-__device__ int sweep(const uint64_t* keys, int n, const Walk& w, float m, const RowT& rt, int mode,
-                     RedScratch* rs, double* cum_at) {
-  double run = w.mass_before;
-  for (int c0 = 0; c0 < n; c0 += kCT) {
-    const int j = c0 + threadIdx.x;
-    const bool valid = j < n;
-    float e = 0.0f;
-    if (valid) e = exact_e(key_val(keys[j]), m, rt);
-    double tot;
-    const double cum = run + block_scan_d(static_cast<double>(e), rs, &tot);
-    bool cond = false;
-    if (valid) {
-      if (mode == 0)
-        cond = (w.count_before + j == static_cast<long long>(w.K) - 1) || (w.mass_mode && cum >= w.t2);
-      else
-        cond = cum > w.t3;
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier of the 256 consumer threads (the other two warps never join it).
+__device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+__device__ __forceinline__ uint64_t warp_min_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = t < v ? t : v;
+  }
+  return v;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint64_t t = __shfl_xor_sync(0xffffffffu, v, o);
+    v = t > v ? t : v;
+  }
+  return v;
+}
+// k agrees with prefix on every bit at or above bit s
+__device__ __forceinline__ bool hi_match(uint64_t k, uint64_t prefix, int s) {
+  return s >= 64 || ((k ^ prefix) >> s) == 0;
+}
+template <typename E>
+__device__ __forceinline__ float to_f32(E v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<uint16_t>(uint16_t v) { return bf16_bits_to_f32(v); }
+
+__device__ __forceinline__ float pick16(const float (&v)[4][4], int idx) {
+  float r = 0.0f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (q * 4 + k == idx) r = v[q][k];
+  return r;
+}
+__device__ __forceinline__ void put16(float (&v)[4][4], int idx, float x) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (q * 4 + k == idx) v[q][k] = x;
+}
+
+// Consumer-group reductions: every consumer thread returns the result, and
+// the final combination runs in a fixed order, so all threads agree.
+__device__ __forceinline__ double csum_d(double v, Red* r) {
+  v = warp_sum_d(v);
+  v = __shfl_sync(0xffffffffu, v, 0);
+  if ((threadIdx.x & 31) == 0) r->d[threadIdx.x >> 5] = v;
+  cbar();
+  double t = 0.0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t += r->d[w];
+  cbar();
+  return t;
+}
+__device__ __forceinline__ unsigned long long csum_u64(unsigned long long v, Red* r) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) r->q[threadIdx.x >> 5] = v;
+  cbar();
+  unsigned long long t = 0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t += r->q[w];
+  cbar();
+  return t;
+}
+__device__ __forceinline__ int csum_i(int v, Red* r) {
+  v = warp_sum_i(v);
+  if ((threadIdx.x & 31) == 0) r->i[threadIdx.x >> 5] = v;
+  cbar();
+  int t = 0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t += r->i[w];
+  cbar();
+  return t;
+}
+__device__ __forceinline__ int cmin_i(int v, Red* r) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) r->i[threadIdx.x >> 5] = v;
+  cbar();
+  int t = INT_MAX;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t = min(t, r->i[w]);
+  cbar();
+  return t;
+}
+__device__ __forceinline__ int cor_i(int v, Red* r) {
+  v = __any_sync(0xffffffffu, v) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0) r->i[threadIdx.x >> 5] = v;
+  cbar();
+  int t = 0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t |= r->i[w];
+  cbar();
+  return t;
+}
+__device__ __forceinline__ float cmax_f(float v, Red* r) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) r->f[threadIdx.x >> 5] = v;
+  cbar();
+  float t = RL_NEG_INF;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t = fmaxf(t, r->f[w]);
+  cbar();
+  return t;
+}
+__device__ __forceinline__ uint64_t cmin_u64(uint64_t v, Red* r) {
+  v = warp_min_u64(v);
+  if ((threadIdx.x & 31) == 0) r->q[threadIdx.x >> 5] = v;
+  cbar();
+  uint64_t t = ~0ull;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t = r->q[w] < t ? r->q[w] : t;
+  cbar();
+  return t;
+}
+__device__ __forceinline__ uint64_t cmax_u64(uint64_t v, Red* r) {
+  v = warp_max_u64(v);
+  if ((threadIdx.x & 31) == 0) r->q[threadIdx.x >> 5] = v;
+  cbar();
+  uint64_t t = 0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) t = r->q[w] > t ? r->q[w] : t;
+  cbar();
+  return t;
+}
+// Inclusive scans over consumer threads 0..255 (thread order).
+__device__ __forceinline__ double cscan_d(double v, Red* r, double* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  double s = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  if (lane == 31) r->d[warp] = s;
+  cbar();
+  double before = 0.0, tot = 0.0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) {
+    if (w < warp) before += r->d[w];
+    tot += r->d[w];
+  }
+  cbar();
+  *total = tot;
+  return before + s;
+}
+__device__ __forceinline__ uint32_t cscan_u32(uint32_t v, Red* r) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t s = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  if (lane == 31) r->u[warp] = s;
+  cbar();
+  uint32_t before = 0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w)
+    if (w < warp) before += r->u[w];
+  cbar();
+  return before + s;
+}
+
+// Descending bitonic sort of a[0..n) (n <= P, P a power of two) by the
+// consumer threads; a[n..P) is padded with 0 (the smallest key).
+__device__ void csort_desc(uint64_t* a, int n, int P) {
+  const int tid = threadIdx.x;
+  for (int i = n + tid; i < P; i += kConsumers) a[i] = 0ull;
+  cbar();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < P; i += kConsumers) {
+        const int l = i ^ j;
+        if (l > i) {
+          const uint64_t x = a[i], y = a[l];
+          const bool desc = (i & k) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            a[i] = y;
+            a[l] = x;
+          }
+        }
+      }
+      cbar();
     }
-    const int f = block_min_i(cond ? j : INT_MAX, rs);
-    if (f != INT_MAX) {
-      if (j == f) rs->bcast_d = cum;
-      __syncthreads();
-      *cum_at = rs->bcast_d;
-      __syncthreads();
-      return f;
+  }
+}
+__device__ __forceinline__ int pow2_at_least(int n) {
+  int p = 1;
+  while (p < n) p <<= 1;
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// Radix selection of the need-th largest key (keys are distinct, need >= 1)
+// ---------------------------------------------------------------------------
+// Warp version over a warp's candidates: keys [0, min(n, kWcap)) in shared
+// memory (buf), the rest in its global overflow area (gov); n <= kWcap + kWovf.
+// bins: 256 u32 of this warp.
+__device__ __forceinline__ uint64_t wkey(const uint64_t* buf, const uint64_t* gov, int i) {
+  return i < kWcap ? buf[i] : __ldcg(reinterpret_cast<const unsigned long long*>(gov + (i - kWcap)));
+}
+__device__ __forceinline__ uint64_t warp_select(const uint64_t* buf, const uint64_t* gov, int n, int need,
+                                                uint32_t* bins) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  uint64_t kmin = ~0ull, kmax = 0ull;
+  for (int i = lane; i < n; i += 32) {
+    const uint64_t k = wkey(buf, gov, i);
+    kmin = k < kmin ? k : kmin;
+    kmax = k > kmax ? k : kmax;
+  }
+  kmin = warp_min_u64(kmin);
+  kmax = warp_max_u64(kmax);
+  if (kmin == kmax) return kmax;
+  const int lead = __clzll(static_cast<long long>(kmin ^ kmax));
+  int shift = 64 - (lead & ~7);
+  uint64_t prefix = shift >= 64 ? 0ull : ((kmax >> shift) << shift);
+  for (int pass = 0; pass < 8; ++pass) {
+    shift -= 8;
+    for (int b = lane; b < 256; b += 32) bins[b] = 0u;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+      const uint64_t k = wkey(buf, gov, i);
+      if (hi_match(k, prefix, shift + 8)) atomicAdd(&bins[static_cast<int>((k >> shift) & 255u)], 1u);
+    }
+    __syncwarp();
+    // lane L owns buckets 255 - 8L - j, j = 0..7 (descending)
+    uint32_t c[8];
+    uint32_t ls = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = bins[255 - 8 * lane - j];
+      ls += c[j];
+    }
+    uint32_t inc = ls;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    const uint32_t exc = inc - ls;
+    const bool hit = exc < static_cast<uint32_t>(need) && inc >= static_cast<uint32_t>(need);
+    const int hl = __ffs(__ballot_sync(0xffffffffu, hit)) - 1;
+    int bucket = 0;
+    uint32_t above = 0, cntb = 0;
+    if (lane == hl) {
+      uint32_t run = exc;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (cntb == 0 && run + c[j] >= static_cast<uint32_t>(need)) {
+          bucket = 255 - 8 * lane - j;
+          above = run;
+          cntb = c[j];
+        }
+        run += c[j];
+      }
+    }
+    bucket = __shfl_sync(0xffffffffu, bucket, hl);
+    above = __shfl_sync(0xffffffffu, above, hl);
+    cntb = __shfl_sync(0xffffffffu, cntb, hl);
+    __syncwarp();
+    prefix |= static_cast<uint64_t>(bucket) << shift;
+    need -= static_cast<int>(above);
+    if (shift == 0) return prefix;
+    if (cntb == 1u || static_cast<uint32_t>(need) == cntb) {
+      uint64_t mn = ~0ull;
+      for (int i = lane; i < n; i += 32) {
+        const uint64_t k = wkey(buf, gov, i);
+        if (hi_match(k, prefix, shift) && k < mn) mn = k;
+      }
+      return warp_min_u64(mn);
+    }
+  }
+  return prefix;
+}
+
+// Keeps the top `keep` keys of a warp's candidates (n > keep) in buf[0, keep);
+// returns the bound (the keep-th largest key). The kept keys are written in
+// 32-key windows after the window has been read, so the in-place move is safe.
+__device__ __forceinline__ uint64_t warp_compact(uint64_t* buf, const uint64_t* gov, int n, int keep,
+                                                 uint32_t* bins) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t T = warp_select(buf, gov, n, keep, bins);
+  int pos = 0;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t k = i < n ? wkey(buf, gov, i) : 0ull;
+    const bool kf = i < n && k >= T;
+    const unsigned b = __ballot_sync(0xffffffffu, kf);
+    __syncwarp();
+    if (kf) buf[pos + __popc(b & ((1u << lane) - 1u))] = k;
+    pos += __popc(b);
+  }
+  __syncwarp();
+  return T;
+}
+
+// Consumer-group version over segments of keys: segment s holds cnts[s]
+// valid keys at base[s * seg_size ...]. G: the keys are in global memory
+// written by other CTAs (read through L2).
+template <bool G>
+__device__ __forceinline__ uint64_t ldkey(const uint64_t* p) {
+  if constexpr (G) {
+    return __ldcg(reinterpret_cast<const unsigned long long*>(p));
+  } else {
+    return *p;
+  }
+}
+template <bool G>
+__device__ uint64_t block_select(const uint64_t* base, int nsegs, int seg_size, const int* cnts, int need,
+                                 uint32_t* bins, Red* rs, Ctl* ctl) {
+  const int tid = threadIdx.x;
+  const int slots = nsegs * seg_size;
+  uint64_t kmin = ~0ull, kmax = 0ull;
+  for (int f = tid; f < slots; f += kConsumers) {
+    const int s = f / seg_size;
+    if (f - s * seg_size < cnts[s]) {
+      const uint64_t k = ldkey<G>(base + f);
+      kmin = k < kmin ? k : kmin;
+      kmax = k > kmax ? k : kmax;
+    }
+  }
+  kmin = cmin_u64(kmin, rs);
+  kmax = cmax_u64(kmax, rs);
+  if (kmin == kmax) return kmax;
+  const int lead = __clzll(static_cast<long long>(kmin ^ kmax));
+  int shift = 64 - (lead & ~7);
+  uint64_t prefix = shift >= 64 ? 0ull : ((kmax >> shift) << shift);
+  for (int pass = 0; pass < 8; ++pass) {
+    shift -= 8;
+    bins[tid] = 0u;
+    cbar();
+    for (int f = tid; f < slots; f += kConsumers) {
+      const int s = f / seg_size;
+      if (f - s * seg_size < cnts[s]) {
+        const uint64_t k = ldkey<G>(base + f);
+        if (hi_match(k, prefix, shift + 8)) atomicAdd(&bins[static_cast<int>((k >> shift) & 255u)], 1u);
+      }
+    }
+    cbar();
+    const uint32_t c = bins[255 - tid];
+    const uint32_t inc = cscan_u32(c, rs);
+    const uint32_t exc = inc - c;
+    if (exc < static_cast<uint32_t>(need) && inc >= static_cast<uint32_t>(need)) {
+      ctl->sel_bucket = 255 - tid;
+      ctl->sel_above = exc;
+      ctl->sel_cnt = c;
+    }
+    cbar();
+    const int bucket = ctl->sel_bucket;
+    const uint32_t above = ctl->sel_above, cntb = ctl->sel_cnt;
+    cbar();
+    prefix |= static_cast<uint64_t>(bucket) << shift;
+    need -= static_cast<int>(above);
+    if (shift == 0) return prefix;
+    if (cntb == 1u || static_cast<uint32_t>(need) == cntb) {
+      uint64_t mn = ~0ull;
+      for (int f = tid; f < slots; f += kConsumers) {
+        const int s = f / seg_size;
+        if (f - s * seg_size < cnts[s]) {
+          const uint64_t k = ldkey<G>(base + f);
+          if (hi_match(k, prefix, shift) && k < mn) mn = k;
+        }
+      }
+      return cmin_u64(mn, rs);
+    }
+  }
+  return prefix;
+}
+
+// Gathers the keys >= T of the segments into out (<= kN) and sorts them.
+template <bool G>
+__device__ int gather_sorted(const uint64_t* base, int nsegs, int seg_size, const int* cnts, uint64_t T,
+                             uint64_t* out, Ctl* ctl) {
+  const int tid = threadIdx.x;
+  if (tid == 0) ctl->cnt = 0;
+  cbar();
+  const int slots = nsegs * seg_size;
+  for (int f = tid; f < slots; f += kConsumers) {
+    const int s = f / seg_size;
+    if (f - s * seg_size < cnts[s]) {
+      const uint64_t k = ldkey<G>(base + f);
+      if (k >= T) {
+        const int i = atomicAdd(&ctl->cnt, 1);
+        if (i < kN) out[i] = k;
+      }
+    }
+  }
+  cbar();
+  const int n = min(ctl->cnt, kN);
+  cbar();
+  csort_desc(out, n, kN);
+  return n;
+}
+
+// ---------------------------------------------------------------------------
+// Chunk geometry shared by the copy warp and the consumers
+// ---------------------------------------------------------------------------
+template <typename E>
+__device__ __forceinline__ uint32_t chunk_bytes(const SpecArgs& a, int row, int start, int len) {
+  const E* src = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start;
+  if (reinterpret_cast<uintptr_t>(src) & 15u) return 0u;
+  return static_cast<uint32_t>(len * static_cast<int>(sizeof(E))) & ~15u;
+}
+__device__ __forceinline__ uint32_t mask_bytes(const SpecArgs& a, int row, int start, int len) {
+  if (!a.mask) return 0u;
+  const uint32_t* src = a.mask + static_cast<int64_t>(row) * a.mask_stride + (start >> 5);
+  if (reinterpret_cast<uintptr_t>(src) & 15u) return 0u;
+  return (static_cast<uint32_t>((len + 31) >> 5) * 4u) & ~15u;
+}
+
+// ---------------------------------------------------------------------------
+// Copy warp
+// ---------------------------------------------------------------------------
+template <typename E>
+__device__ __noinline__ void producer_loop(const SpecArgs& a) {
+  if ((threadIdx.x & 31) != 0) return;
+  const Smem sm = smem_map();
+  const int S = spec_chunks(a.V);
+  int seq = 0;
+  bool ok = true;
+  for (int item = blockIdx.x; item < a.nitems && ok; item += gridDim.x) {
+    const int row = item / a.nseg;
+    const int seg = item - row * a.nseg;
+    const int c0 = seg * a.cps, c1 = min(S, c0 + a.cps);
+    for (int c = c0; c < c1; ++c, ++seq) {
+      const int s = seq % kNS;
+      const uint32_t ph = static_cast<uint32_t>((seq / kNS) & 1);
+      if (!mbar_wait(&sm.empty[s], ph ^ 1u, kWaitBudget) || *reinterpret_cast<volatile int*>(&sm.ctl->abort)) {
+        atomicExch(&sm.ctl->abort, 1);
+        ok = false;
+        break;
+      }
+      const int start = c * kCE;
+      const int len = min(kCE, a.V - start);
+      const uint32_t db = chunk_bytes<E>(a, row, start, len);
+      const uint32_t mb = mask_bytes(a, row, start, len);
+      mbar_expect_tx(&sm.full[s], db + mb);
+      if (db)
+        bulk_g2s(sm.stage + s * kStageBytes,
+                 reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start, db, &sm.full[s]);
+      if (mb)
+        bulk_g2s(sm.maskst + s * kMaskWords, a.mask + static_cast<int64_t>(row) * a.mask_stride + (start >> 5), mb,
+                 &sm.full[s]);
+    }
+  }
+  if (!ok) {
+    // never leave with a copy still landing in this CTA's shared memory
+    for (int i = max(0, seq - kNS); i < seq; ++i)
+      mbar_wait(&sm.full[i % kNS], static_cast<uint32_t>((i / kNS) & 1), kWaitBudget);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Row-preparation warp
+// ---------------------------------------------------------------------------
+// The row's history ids in [0, V), sorted ascending by a one-warp LSD radix
+// sort (three 7-bit digits; ids < 2^21), packed as (id << 11) | count: the
+// first copy of an id carries its count, later copies count 0 (skipped).
+// scr: 2 * kHmax ints + 128 counters of this warp. Returns the entry count.
+__device__ __noinline__ int build_table(const SpecArgs& a, int row, int hl, uint32_t* tab, int* scr) {
+  const int lane = threadIdx.x & 31;
+  int* bufA = scr;
+  int* bufB = scr + kHmax;
+  int* cnt = scr + 2 * kHmax;
+  const int32_t* h = a.hist + static_cast<int64_t>(row) * a.hist_stride;
+  // valid ids, compacted in history order (loads issued 8 windows at a time)
+  int n = 0;
+  for (int g0 = 0; g0 < hl; g0 += 256) {
+    int ids[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = g0 + r * 32 + lane;
+      ids[r] = i < hl ? __ldg(h + i) : -1;
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = g0 + r * 32 + lane;
+      const int id = ids[r] - a.vocab_offset;
+      const bool ok = i < hl && id >= 0 && id < a.V;
+      const unsigned b = __ballot_sync(0xffffffffu, ok);
+      if (ok) bufA[n + __popc(b & ((1u << lane) - 1u))] = id;
+      n += __popc(b);
+    }
+  }
+  __syncwarp();
+  int* src = bufA;
+  int* dst = bufB;
+  for (int shift = 0; shift < 21; shift += 7) {
+    for (int d = lane; d < 128; d += 32) cnt[d] = 0;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) atomicAdd(&cnt[(src[i] >> shift) & 127], 1);
+    __syncwarp();
+    // exclusive scan of the 128 counters (4 per lane)
+    int c4[4], tot = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      c4[j] = cnt[lane * 4 + j];
+      tot += c4[j];
+    }
+    int inc = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    int run = inc - tot;
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      cnt[lane * 4 + j] = run;
+      run += c4[j];
+    }
+    __syncwarp();
+    // stable scatter, 32 ids at a time
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lane;
+      const bool ok = i < n;
+      const int key = ok ? src[i] : 0;
+      const int d = ok ? ((key >> shift) & 127) : (128 + lane);
+      const unsigned peers = __match_any_sync(0xffffffffu, d);
+      const int rank = __popc(peers & ((1u << lane) - 1u));
+      const int base = ok ? cnt[d] : 0;
+      __syncwarp();
+      if (ok) {
+        dst[base + rank] = key;
+        if (rank == 0) cnt[d] = base + __popc(peers);
+      }
+      __syncwarp();
+    }
+    int* t = src;
+    src = dst;
+    dst = t;
+  }
+  // src: sorted ids; one entry per position, the first of each run counts it
+  for (int p = lane; p < n; p += 32) {
+    const int id = src[p];
+    uint32_t c = 0u;
+    if (p == 0 || src[p - 1] != id) {
+      int q = p + 1;
+      while (q < n && src[q] == id) ++q;
+      c = static_cast<uint32_t>(min(q - p, 2047));
+    }
+    tab[p] = (static_cast<uint32_t>(id) << 11) | c;
+  }
+  __syncwarp();
+  return n;
+}
+
+template <typename E>
+__device__ __noinline__ void meta_loop(const SpecArgs& a) {
+  const Smem sm = smem_map();
+  const int lane = threadIdx.x & 31;
+  const int S = spec_chunks(a.V);
+  int mseq = 0;
+  for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
+    const int slot = mseq & 1;
+    if (!mbar_wait(&sm.mempty[slot], static_cast<uint32_t>(((mseq >> 1) & 1) ^ 1), kWaitBudget) ||
+        *reinterpret_cast<volatile int*>(&sm.ctl->abort)) {
+      if (lane == 0) atomicExch(&sm.ctl->abort, 1);
+      return;
+    }
+    ItemMeta& mt = sm.meta[slot];
+    uint32_t* tab = sm.tab + slot * kHmax;
+    const int row = item / a.nseg;
+    const int seg = item - row * a.nseg;
+    // every global read of the row issued up front
+    const rl_row_params prm = a.params[row];
+    const float u = a.uniforms[row];
+    const int hl_raw = a.hist ? a.hist_len[row] : 0;
+    const float T = prm.temperature;
+    int mode;
+    if (!(fabsf(T) < RL_POS_INF) || !(T > 0.0f)) mode = 0;  // greedy; a non-finite T is reported at the end
+    else if (prm.top_k > 0 && prm.top_k <= kN) mode = 1;
+    else mode = 2;
+    // allowed-mask flag: an empty allowed set means every id is allowed
+    int mask_on = 0;
+    if (a.mask) {
+      const uint32_t* mrow = a.mask + static_cast<int64_t>(row) * a.mask_stride;
+      const int nw = (a.V + 31) >> 5;
+      uint32_t any = 0u;
+      for (int w = lane; w < nw; w += 32) {
+        uint32_t bits = __ldg(mrow + w);
+        const int rem = a.V - w * 32;
+        if (rem < 32) bits &= (1u << rem) - 1u;
+        any |= bits;
+      }
+      mask_on = __any_sync(0xffffffffu, any != 0u) ? 1 : 0;
+    }
+    // history table (only when the penalties are not the identity)
+    const bool pen = !(prm.repeat_penalty == 1.0f && prm.frequency_penalty == 0.0f && prm.presence_penalty == 0.0f);
+    int ntab = 0;
+    if (a.hist && pen) {
+      const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
+      if (hl > 0) ntab = build_table(a, row, hl, tab, sm.mscr);
+    }
+    // Histogram window depth W (nats below the anchor): the mass below it is
+    // at most V e^-W of the row max, kept under a quarter of the smallest
+    // tail mass that the cutoff or the draw can reach.
+    int wbins = kNB - 1;
+    if (mode == 2 && prm.top_k <= 0) {
+      const double p = static_cast<double>(prm.top_p);
+      double tail = 1.0;
+      if (p < 1.0) tail = fmin(tail, 1.0 - p);
+      tail = fmin(tail, (1.0 - static_cast<double>(u)) * fmin(p, 1.0));
+      if (tail > 0.0 && p > 0.0) {
+        const double W = log(4.0 * static_cast<double>(a.V) / tail) + 1.0;
+        wbins = min(wbins, kHead + max(64, static_cast<int>(ceil(W * kRbin))));
+      }
+    }
+    if (lane == 0) {
+      mt.item = item;
+      mt.row = row;
+      mt.seg = seg;
+      mt.c0 = seg * a.cps;
+      mt.c1 = min(S, mt.c0 + a.cps);
+      mt.mode = mode;
+      mt.nkeep = mode == 1 ? prm.top_k : kN;
+      mt.need_count = (mode == 2 && prm.top_k > 0) ? 1 : 0;
+      mt.mask_on = mask_on;
+      mt.ntab = ntab;
+      mt.wbins = wbins;
+      mt.top_k = prm.top_k;
+      mt.top_p = prm.top_p;
+      mt.u = u;
+      mt.rp = prm.repeat_penalty;
+      mt.pres = prm.presence_penalty;
+      mt.freq = prm.frequency_penalty;
+      mt.rt = make_rowt(mode == 0 ? 1.0f : T);
+      mt.rt.T = T;  // the raw temperature (greedy rows check it at the end)
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.mfull[slot]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Consumer side: penalties and row re-reads
+// ---------------------------------------------------------------------------
+// Penalties of the table entries in [lo, hi) applied to the registers of the
+// slice that starts at lo (logit lo + (q*32+lane)*4 + k is v[q][k]); hp is
+// the warp's cursor in the table.
+__device__ __forceinline__ void pen_regs(float (&v)[4][4], int lo, int hi, const uint32_t* tab, int ntab, int& hp,
+                                         const ItemMeta& mt) {
+  const int lane = threadIdx.x & 31;
+  while (true) {
+    const int j = hp + lane;
+    const uint32_t ent = j < ntab ? tab[j] : 0xffffffffu;
+    const int id = static_cast<int>(ent >> 11);
+    const bool below = j < ntab && id < hi;
+    const bool mine = below && id >= lo && (ent & 2047u) != 0u;
+    unsigned mb = __ballot_sync(0xffffffffu, mine);
+    while (mb) {
+      const int src = __ffs(mb) - 1;
+      mb &= mb - 1u;
+      const int e = __shfl_sync(0xffffffffu, id, src) - lo;
+      const int cn = __shfl_sync(0xffffffffu, static_cast<int>(ent & 2047u), src);
+      if (((e >> 2) & 31) == lane) {
+        const int idx = ((e >> 7) << 2) | (e & 3);
+        put16(v, idx, pen_value(pick16(v, idx), cn, mt.rp, mt.freq, mt.pres));
+      }
+    }
+    const int adv = __popc(__ballot_sync(0xffffffffu, below));
+    hp += adv;
+    if (adv < 32) break;
+  }
+}
+// Cursor start: the number of table entries with id < lo.
+__device__ __forceinline__ int tab_lower_bound(const uint32_t* tab, int ntab, int lo) {
+  const int lane = threadIdx.x & 31;
+  int c = 0;
+  for (int j0 = 0; j0 < ntab; j0 += 32) {
+    const int j = j0 + lane;
+    const bool lt = j < ntab && static_cast<int>(tab[j] >> 11) < lo;
+    c += __popc(__ballot_sync(0xffffffffu, lt));
+  }
+  return c;
+}
+// Row re-read: the warp's slice of chunk `start` from global memory,
+// penalised and masked (-inf outside the row or disallowed).
+template <typename E>
+__device__ __forceinline__ void load_slice_global(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int& hp,
+                                                  int start, int base, float (&v)[4][4]) {
+  const int lane = threadIdx.x & 31;
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
+  const int len = min(kCE, a.V - start);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int el = base + (q * 32 + lane) * 4 + k;
+      v[q][k] = el < len ? to_f32<E>(__ldcg(rowp + start + el)) : RL_NEG_INF;
+    }
+  if (mt.ntab > 0) pen_regs(v, start + base, start + base + kSlice, tab, mt.ntab, hp, mt);
+  if (mt.mask_on) {
+    const uint32_t* mrow = a.mask + static_cast<int64_t>(mt.row) * a.mask_stride;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e0 = base + (q * 32 + lane) * 4;
+      const uint32_t word = e0 < len ? __ldcg(mrow + ((start + e0) >> 5)) : 0u;
+      const uint32_t bits = (word >> ((start + e0) & 31)) & 15u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (!((bits >> k) & 1u)) v[q][k] = RL_NEG_INF;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Finisher
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status, int token, float prob) {
+  const bool ok = status == 0;
+  a.out_tok[row] = ok ? token + a.vocab_offset : -1;
+  if (a.out_prob) a.out_prob[row] = ok ? prob : 0.0f;
+  if (a.row_status) a.row_status[row] = status;
+}
+
+// Keys of the allowed logits of absolute bin A, gathered from a re-read of
+// the row into buf; returns the count (> kCollect: too many).
+template <typename E>
+__device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, uint64_t* buf,
+                           Ctl* ctl) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = spec_chunks(a.V);
+  if (threadIdx.x == 0) ctl->cnt = 0;
+  cbar();
+  int hp = 0;
+  for (int c = 0; c < S; ++c) {
+    const int start = c * kCE;
+    float v[4][4];
+    load_slice_global<E>(a, mt, tab, hp, start, warp * kSlice, v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float x = v[q][k];
+        if (x > RL_NEG_INF && bin_of(x, mt.rt) == A) {
+          const int i = atomicAdd(&ctl->cnt, 1);
+          if (i < kCollect)
+            buf[i] = cand_key(x, static_cast<uint32_t>(start + warp * kSlice + (q * 32 + lane) * 4 + k));
+        }
+      }
+  }
+  cbar();
+  const int n = ctl->cnt;
+  cbar();
+  return n;
+}
+
+// Exact radix walk over re-reads of the row: the first logit in list order
+// at which the running count reaches cnt_target (kind 0) or the running
+// mass (e units, relative to M) reaches target (kind 1: >=, kind 2: >).
+// Returns its key and its exclusive cumulative count and mass; when the
+// target is never reached, *cnt_before = -1 and *mass_before = the total.
+template <typename E>
+__device__ __noinline__ uint64_t radix_walk(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float M, int kind,
+                               long long cnt_target, double target, long long* cnt_before, double* mass_before) {
+  const Smem sm = smem_map();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
+  const int S = spec_chunks(a.V);
+  uint32_t* bcnt = sm.radix;
+  double* bmass = reinterpret_cast<double*>(sm.radix + 256);
+  unsigned long long* bmax = reinterpret_cast<unsigned long long*>(bmass + 256);
+  uint64_t prefix = 0ull;
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    bcnt[tid] = 0u;
+    bmass[tid] = 0.0;
+    bmax[tid] = 0ull;
+    cbar();
+    long long my_c = 0;
+    double my_m = 0.0;
+    int hp = 0;
+    for (int c = 0; c < S; ++c) {
+      const int start = c * kCE;
+      float v[4][4];
+      load_slice_global<E>(a, mt, tab, hp, start, warp * kSlice, v);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float x = v[q][k];
+          if (!(x > RL_NEG_INF)) continue;
+          const uint64_t key = cand_key(x, static_cast<uint32_t>(start + warp * kSlice + (q * 32 + lane) * 4 + k));
+          const double e = static_cast<double>(exact_e(x, M, mt.rt));
+          if (hi_match(key, prefix, shift + 8)) {
+            const int b = static_cast<int>((key >> shift) & 255u);
+            atomicAdd(&bcnt[b], 1u);
+            atomicAdd(&bmass[b], e);
+            atomicMax(&bmax[b], static_cast<unsigned long long>(key));
+          } else if (key > prefix) {
+            my_c += 1;
+            my_m += e;
+          }
+        }
+    }
+    cbar();
+    // logits above the current prefix range
+    const long long ca = static_cast<long long>(csum_u64(static_cast<unsigned long long>(my_c), sm.red));
+    const double ma = csum_d(my_m, sm.red);
+    // thread t owns bucket 255 - t; inclusive scans from the top bucket
+    const int b = 255 - tid;
+    double mtot;
+    const uint32_t nb = bcnt[b];
+    const double mbk = bmass[b];
+    const uint32_t cinc = cscan_u32(nb, sm.red);
+    const double minc = cscan_d(mbk, sm.red, &mtot);
+    bool hit = false;
+    if (nb > 0u) {
+      if (kind == 0) hit = ca + static_cast<long long>(cinc) >= cnt_target;
+      else if (kind == 1) hit = ma + minc >= target;
+      else hit = ma + minc > target;
+    }
+    const int first = cmin_i(hit ? tid : INT_MAX, sm.red);
+    if (first == INT_MAX) {
+      *cnt_before = -1;
+      *mass_before = ma + mtot;
+      return 0ull;
+    }
+    if (tid == first) {
+      sm.ctl->res_i = static_cast<int>(nb);
+      sm.ctl->res_j = b;
+      sm.ctl->res_key = bmax[b];
+      sm.ctl->res_c = ca + static_cast<long long>(cinc - nb);
+      sm.ctl->res_d = ma + (minc - mbk);
+    }
+    cbar();
+    const int cnt_b = sm.ctl->res_i;
+    const int bsel = sm.ctl->res_j;
+    const uint64_t kmaxb = sm.ctl->res_key;
+    const long long ce = sm.ctl->res_c;
+    const double me = sm.ctl->res_d;
+    cbar();
+    prefix |= static_cast<uint64_t>(bsel) << shift;
+    if (cnt_b == 1 || shift == 0) {
+      *cnt_before = ce;
+      *mass_before = me;
+      return cnt_b == 1 ? kmaxb : prefix;
+    }
+  }
+  *cnt_before = -1;
+  *mass_before = 0.0;
+  return 0ull;
+}
+
+// First index j in [0, n) of sorted keys (exact e, probability units,
+// starting at `run`) where cond(j, cum_j) holds; INT_MAX if none. *cum_at
+// gets the inclusive cumulative there, *run_end the total.
+template <typename F>
+__device__ int sweep_sorted(const uint64_t* keys, int n, float M, double Z, const RowT& rt, double run, F cond,
+                            Red* rs, Ctl* ctl, double* cum_at, double* run_end) {
+  const int tid = threadIdx.x;
+  for (int c0 = 0; c0 < n; c0 += kConsumers) {
+    const int j = c0 + tid;
+    double pj = 0.0;
+    if (j < n) pj = static_cast<double>(exact_e(key_val(keys[j]), M, rt)) / Z;
+    double tot;
+    const double cum = run + cscan_d(pj, rs, &tot);
+    const int g = cmin_i((j < n && cond(j, cum)) ? j : INT_MAX, rs);
+    if (g != INT_MAX) {
+      if (j == g) ctl->res_d = cum;
+      cbar();
+      *cum_at = ctl->res_d;
+      cbar();
+      *run_end = run + tot;
+      return g;
     }
     run += tot;
   }
+  *run_end = run;
   return INT_MAX;
 }
 
-// Penalised value of id from the finisher's sorted history table, or x.
-__device__ __forceinline__ float hist_value(float x, int id, const int32_t* hid, const float* hval, int nh) {
-  int lo = 0, hi = nh - 1;
-  while (lo <= hi) {
-    const int mid = (lo + hi) >> 1;
-    const int v = hid[mid];
-    if (v == id) return hval[mid];
-    if (v < id) lo = mid + 1;
-    else hi = mid - 1;
+// The finisher of a row (consumer threads). On entry sm.sums[0..nseg) hold
+// the segment summaries; for a one-segment row sm.top holds the sorted list
+// and the histogram is in shared memory.
+template <typename E>
+__device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int first_item) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  const int row = mt.row;
+  const int nseg = a.nseg;
+  Ctl* ctl = sm.ctl;
+  Red* rs = sm.red;
+  // ---- row summary ----
+  float M = RL_NEG_INF;
+  int argmax = INT_MAX, nallow = 0, flags = 0;
+  for (int s = 0; s < nseg; ++s) {
+    const ItemSum& q = sm.sums[s];
+    nallow += q.nallow;
+    flags |= q.flags;
+    if (q.m > M) {
+      M = q.m;
+      argmax = q.argmax;
+    } else if (q.m == M) {
+      argmax = min(argmax, q.argmax);
+    }
   }
-  return x;
+  const float T = mt.rt.T;
+  int status = 0;
+  if (flags & kFlagTimeout) status = RL_ERR_TIMEOUT;
+  else if ((flags & kFlagBad) || nallow == 0 || !(fabsf(T) < RL_POS_INF)) status = RL_ERR_NONFINITE;
+  const bool want_list = a.list_len != nullptr;
+  if (status != 0 || mt.mode == 0) {
+    if (tid == 0) {
+      write_row(a, row, status, argmax, 1.0f);
+      if (want_list) {
+        const bool ok = status == 0 && a.list_cap > 0;
+        a.list_len[row] = ok ? 1 : 0;
+        if (ok) {
+          a.list_ids[static_cast<int64_t>(row) * a.list_cap] = argmax + a.vocab_offset;
+          a.list_probs[static_cast<int64_t>(row) * a.list_cap] = 1.0f;
+        }
+      }
+    }
+    return;
+  }
+  const RowT& rt = mt.rt;
+  const double cd = kLog2e / static_cast<double>(T);
+  double Z = 0.0;
+  for (int s = 0; s < nseg; ++s) {
+    const ItemSum& q = sm.sums[s];
+    if (q.nallow > 0 && q.m > RL_NEG_INF) Z += q.z * exp2((static_cast<double>(q.m) - static_cast<double>(M)) * cd);
+  }
+  // ---- the row's sorted list ----
+  int nt = 0;
+  if (nseg == 1) {
+    nt = sm.sums[0].ncand;
+  } else {
+    int total = 0;
+    for (int s = 0; s < nseg; ++s) total += sm.sums[s].ncand;
+    for (int s = tid; s < nseg; s += kConsumers) sm.segn[s] = sm.sums[s].ncand;
+    cbar();
+    const uint64_t* base = a.ws.cands + static_cast<int64_t>(first_item) * kN;
+    const int need = min(total, mt.nkeep);
+    if (need > 0) {
+      // a segment holding nkeep keys bounds the row's nkeep-th key by its last
+      // one (lists are sorted); the keys above the bound go to shared memory
+      uint64_t b0 = 0ull;
+      if (tid < nseg && sm.segn[tid] >= mt.nkeep)
+        b0 = __ldcg(reinterpret_cast<const unsigned long long*>(base + static_cast<int64_t>(tid) * kN + mt.nkeep - 1));
+      const uint64_t bound = cmax_u64(b0, rs);
+      uint64_t* buf = reinterpret_cast<uint64_t*>(sm.hmass);  // collect area (the histogram is in global)
+      if (tid == 0) ctl->cnt = 0;
+      cbar();
+      const int slots = nseg * kN;
+      for (int f0 = 0; f0 < slots; f0 += 4 * kConsumers) {
+        uint64_t k4[4];
+        bool ok4[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int f = f0 + r * kConsumers + tid;
+          const int sg = f / kN;
+          ok4[r] = f < slots && (f - sg * kN) < sm.segn[sg];
+          k4[r] = ok4[r] ? __ldcg(reinterpret_cast<const unsigned long long*>(base + f)) : 0ull;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+          if (ok4[r] && k4[r] >= bound) {
+            const int i = atomicAdd(&ctl->cnt, 1);
+            if (i < kCollect) buf[i] = k4[r];
+          }
+      }
+      cbar();
+      const int ncol = ctl->cnt;
+      cbar();
+      if (ncol <= kCollect) {
+        if (tid == 0) ctl->res_j = ncol;
+        cbar();
+        const int* cn = &ctl->res_j;
+        // (the collect area spans the radix bins: count in the warp-buffer area)
+        const uint64_t Tk = block_select<false>(buf, 1, ncol, cn, need, reinterpret_cast<uint32_t*>(sm.wbuf), rs, ctl);
+        nt = gather_sorted<false>(buf, 1, ncol, cn, Tk, sm.top, ctl);
+      } else {
+        const uint64_t Tk = block_select<true>(base, nseg, kN, sm.segn, need, sm.radix, rs, ctl);
+        nt = gather_sorted<true>(base, nseg, kN, sm.segn, Tk, sm.top, ctl);
+      }
+    }
+  }
+  const int K = (mt.top_k > 0 && mt.top_k < nallow) ? mt.top_k : nallow;
+  const bool mass_mode = mt.top_p < 1.0f;
+  const bool count_mode = K < nallow;
+  const double pd = static_cast<double>(mt.top_p);
+  const double ud = static_cast<double>(mt.u);
+  // exact e and cumulative probabilities of the list
+  {
+    float e = 0.0f;
+    double pr = 0.0;
+    if (tid < nt) {
+      e = exact_e(key_val(sm.top[tid]), M, rt);
+      pr = static_cast<double>(e) / Z;
+    }
+    double tot;
+    const double cum = cscan_d(pr, rs, &tot);
+    if (tid < nt) {
+      sm.tope[tid] = e;
+      sm.topc[tid] = cum;
+    }
+    cbar();
+  }
+  // complete prefix: list entries whose whole bin is in the list
+  int complete = nt;
+  float amin = 0.0f;
+  if (mt.mode == 2 && nt < nallow && nt > 0) {
+    amin = bin_of(key_val(sm.top[nt - 1]), rt);
+    complete = cmin_i((tid < nt && bin_of(key_val(sm.top[tid]), rt) == amin) ? tid : INT_MAX, rs);
+  }
+  if (want_list) {
+    const bool listed = K <= nt;
+    const int nl = listed ? min(K, a.list_cap) : 0;
+    if (tid == 0) a.list_len[row] = listed ? nl : -1;
+    for (int i = tid; i < nl; i += kConsumers) {
+      a.list_ids[static_cast<int64_t>(row) * a.list_cap + i] = static_cast<int>(key_id(sm.top[i])) + a.vocab_offset;
+      a.list_probs[static_cast<int64_t>(row) * a.list_cap + i] =
+          static_cast<float>(static_cast<double>(sm.tope[i]) / Z);
+    }
+  }
+  int token = -1, st = 0;
+  float prob = 0.0f;
+  bool done = false;
+  // cutoff inside the complete prefix
+  const int cut = cmin_i(
+      (tid < complete && (tid == K - 1 || (mass_mode && sm.topc[tid] >= pd))) ? tid : INT_MAX, rs);
+  if (cut != INT_MAX) {
+    const double Sx = sm.topc[cut];
+    const double tgt = ud * Sx;
+    int d = cmin_i((tid <= cut && sm.topc[tid] > tgt) ? tid : INT_MAX, rs);
+    if (d == INT_MAX) d = cut;
+    token = static_cast<int>(key_id(sm.top[d]));
+    prob = static_cast<float>((static_cast<double>(sm.tope[d]) / Z) / Sx);
+    done = true;
+  } else if (!mass_mode && !count_mode) {
+    // the list is every allowed id: S is the whole mass (1)
+    const int d = cmin_i((tid < complete && sm.topc[tid] > ud) ? tid : INT_MAX, rs);
+    if (d != INT_MAX) {
+      token = static_cast<int>(key_id(sm.top[d]));
+      prob = static_cast<float>(static_cast<double>(sm.tope[d]) / Z);
+      done = true;
+    }
+  }
+
+  if (!done) {
+    // ---- below the list: the merged histogram, then the exact radix walk ----
+    const double base_m = complete > 0 ? sm.topc[complete - 1] : 0.0;  // probability units
+    const long long base_c = complete;
+    bool hist_ok = mt.mode == 2 && nt > 0;
+    int A_hi = 0, A_lo = INT_MIN;
+    if (hist_ok) {
+      A_hi = static_cast<int>(amin);
+      int atop_min = INT_MAX;
+      for (int s = 0; s < nseg; ++s) {
+        const ItemSum& q = sm.sums[s];
+        if (q.nallow == 0) continue;
+        if (q.atop == kNoAnchor || (q.flags & kFlagHistBad)) hist_ok = false;
+        A_lo = max(A_lo, q.wlo);
+        atop_min = min(atop_min, q.atop);
+      }
+      if (A_hi > atop_min || A_hi < A_lo || A_hi - A_lo >= kNB) hist_ok = false;
+    }
+    bool resolved = false;
+    if (hist_ok) {
+      // merged bins i = A_hi - A in probability units: inclusive prefix sums
+      double* cm = reinterpret_cast<double*>(sm.wbuf);
+      double* cc = cm + kNB;
+      const int nb = A_hi - A_lo + 1;
+      constexpr int BPT = kNB / kConsumers;
+      {
+        double lm[BPT], lc[BPT];
+        double sm_ = 0.0, sc_ = 0.0;
+#pragma unroll
+        for (int r = 0; r < BPT; ++r) {
+          const int i = tid * BPT + r;
+          double mq = 0.0, cq = 0.0;
+          if (i < nb) {
+            const int A = A_hi - i;
+            for (int s = 0; s < nseg; ++s) {
+              const ItemSum& q = sm.sums[s];
+              if (q.nallow == 0) continue;
+              const int off = q.atop - A;
+              if (off < 0 || off >= kNB) continue;
+              if (nseg == 1) {
+                mq += static_cast<double>(sm.hmass[off]);
+                cq += static_cast<double>(sm.hcnt[off]);
+              } else {
+                const int64_t gb = static_cast<int64_t>(first_item + s) * kNB + off;
+                mq += static_cast<double>(__ldcg(a.ws.hmass + gb));
+                if (mt.need_count) cq += static_cast<double>(__ldcg(a.ws.hcnt + gb));
+              }
+            }
+            mq *= exp2(((static_cast<double>(A) + 1.0) / static_cast<double>(kRbin) -
+                        static_cast<double>(M) / static_cast<double>(T)) * kLog2e) /
+                  (static_cast<double>(kMassQ) * Z);
+          }
+          lm[r] = mq;
+          lc[r] = cq;
+          sm_ += mq;
+          sc_ += cq;
+        }
+        double tm, tc;
+        double im = cscan_d(sm_, rs, &tm) - sm_;
+        double ic = cscan_d(sc_, rs, &tc) - sc_;
+#pragma unroll
+        for (int r = 0; r < BPT; ++r) {
+          const int i = tid * BPT + r;
+          im += lm[r];
+          ic += lc[r];
+          if (i < nb) {
+            cm[i] = im;
+            cc[i] = ic;
+          }
+        }
+        cbar();
+      }
+      uint64_t* buf = reinterpret_cast<uint64_t*>(sm.hmass);  // collect buffer (the histogram is merged)
+      int held = -1;  // bin whose sorted keys are in buf
+      int nheld = 0;
+      double corr = 0.0;  // exact minus histogram mass of the bins passed so far
+      long long ccorr = 0;
+      // -- the cutoff bin --
+      int i_c = nb, cut_pos = -1;
+      double Sx = 0.0, bm_cut = 0.0;
+      bool cut_ok = false;
+      int i0 = 0;
+      for (int guard = 0; guard < nb && !cut_ok && (mass_mode || count_mode); ++guard) {
+        int best = INT_MAX;
+#pragma unroll
+        for (int r = 0; r < BPT; ++r) {
+          const int i = tid * BPT + r;
+          if (i >= i0 && i < nb) {
+            const bool hc = count_mode && base_c + ccorr + static_cast<long long>(cc[i]) >= K;
+            const bool hm = mass_mode && base_m + corr + cm[i] >= pd;
+            if ((hc || hm) && i < best) best = i;
+          }
+        }
+        const int f = cmin_i(best, rs);
+        if (f == INT_MAX) break;
+        const double mb = base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
+        const long long cb = base_c + ccorr + (f > 0 ? static_cast<long long>(cc[f - 1]) : 0);
+        nheld = collect_bin<E>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
+        if (nheld > kCollect) break;
+        csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
+        held = f;
+        double cum_at = 0.0, run_end = 0.0;
+        const int g = sweep_sorted(
+            buf, nheld, M, Z, rt, mb,
+            [&](int j, double cum) {
+              return (count_mode && cb + j == static_cast<long long>(K) - 1) || (mass_mode && cum >= pd);
+            },
+            rs, ctl, &cum_at, &run_end);
+        if (g != INT_MAX) {
+          i_c = f;
+          cut_pos = g;
+          Sx = cum_at;
+          bm_cut = mb;
+          cut_ok = true;
+        } else {
+          // the histogram overstated this bin: continue with its exact mass
+          corr += (run_end - mb) - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
+          ccorr += static_cast<long long>(nheld) - static_cast<long long>(cc[f] - (f > 0 ? cc[f - 1] : 0.0));
+          i0 = f + 1;
+        }
+      }
+      if (!cut_ok && !mass_mode && !count_mode) {
+        cut_ok = true;  // no cutoff: S is the whole mass
+        Sx = 1.0;
+      }
+      if (cut_ok) {
+        const double tgt = ud * Sx;
+        if (complete > 0 && tgt < base_m) {
+          int d = cmin_i((tid < complete && sm.topc[tid] > tgt) ? tid : INT_MAX, rs);
+          if (d == INT_MAX) d = complete - 1;
+          token = static_cast<int>(key_id(sm.top[d]));
+          prob = static_cast<float>((static_cast<double>(sm.tope[d]) / Z) / Sx);
+          resolved = true;
+        } else {
+          // the draw bin: the first bin whose end exceeds the target, at or
+          // above the cutoff bin
+          int i_d = 0;
+          for (int guard = 0; guard < nb && !resolved; ++guard) {
+            int best = INT_MAX;
+#pragma unroll
+            for (int r = 0; r < BPT; ++r) {
+              const int i = tid * BPT + r;
+              if (i >= i_d && i < nb && base_m + corr + cm[i] > tgt && i < best) best = i;
+            }
+            int f = cmin_i(best, rs);
+            if (cut_pos >= 0 && (f == INT_MAX || f > i_c)) f = i_c;
+            if (f == INT_MAX) break;
+            if (held != f) {
+              nheld = collect_bin<E>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
+              if (nheld > kCollect) break;
+              csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
+              held = f;
+            }
+            const bool at_cut = cut_pos >= 0 && f == i_c;
+            const double mb = at_cut ? bm_cut : base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
+            const int lim = at_cut ? cut_pos + 1 : nheld;
+            double cum_at = 0.0, run_end = 0.0;
+            int g = sweep_sorted(
+                buf, lim, M, Z, rt, mb, [&](int, double cum) { return cum > tgt; }, rs, ctl, &cum_at, &run_end);
+            if (g == INT_MAX && at_cut) g = cut_pos;
+            if (g != INT_MAX) {
+              const uint64_t key = buf[g];
+              token = static_cast<int>(key_id(key));
+              prob = static_cast<float>((static_cast<double>(exact_e(key_val(key), M, rt)) / Z) / Sx);
+              resolved = true;
+            } else {
+              i_d = f + 1;
+            }
+          }
+        }
+      }
+    }
+    if (!resolved) {
+      // ---- exact radix walk over re-reads of the row ----
+      long long cb1 = -1, cb2 = -1;
+      double mb1 = 0.0, mb2 = 0.0;
+      uint64_t kc = 0ull;
+      double Sx_e = 0.0;
+      bool have_cut = false;
+      if (count_mode) {
+        const uint64_t kk = radix_walk<E>(a, mt, tab, M, 0, K, 0.0, &cb1, &mb1);
+        if (cb1 >= 0) {
+          kc = kk;
+          Sx_e = mb1 + static_cast<double>(exact_e(key_val(kk), M, rt));
+          have_cut = true;
+        }
+      }
+      if (mass_mode) {
+        const uint64_t kp = radix_walk<E>(a, mt, tab, M, 1, 0, pd * Z, &cb2, &mb2);
+        if (cb2 >= 0 && (!have_cut || kp > kc)) {
+          kc = kp;
+          Sx_e = mb2 + static_cast<double>(exact_e(key_val(kp), M, rt));
+          have_cut = true;
+        }
+      }
+      if (!have_cut) {
+        long long cbt;
+        double tot;
+        radix_walk<E>(a, mt, tab, M, 0, LLONG_MAX, 0.0, &cbt, &tot);
+        Sx_e = tot;
+      }
+      long long cbd;
+      double mbd;
+      uint64_t kd = radix_walk<E>(a, mt, tab, M, 2, 0, ud * Sx_e, &cbd, &mbd);
+      if (cbd < 0 || (have_cut && kd < kc)) kd = kc;
+      if (kd == 0ull || !(Sx_e > 0.0)) {
+        st = RL_ERR_UNSUPPORTED;
+      } else {
+        token = static_cast<int>(key_id(kd));
+        prob = static_cast<float>(static_cast<double>(exact_e(key_val(kd), M, rt)) / Sx_e);
+      }
+    }
+  }
+  if (tid == 0) write_row(a, row, st, token, prob);
+}
+
+// Per-thread accumulators of an item, handed to its end.
+struct ItemAcc {
+  float m_run;
+  int arg_run;
+  int nal, bad, tmo;
+  float zref, zs;
+  unsigned long long qs;
+  int wcnt;
+  int atop;
+  int hist_on;
+  int cseq;
+};
+
+// End of an item (consumer threads): the item's summary and top list, then
+// the row's finisher when this CTA is the last of the row to arrive.
+template <typename E>
+__device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, ItemAcc acc) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ItemMeta& mt = sm.meta[slot];
+  const uint32_t* tab = sm.tab + slot * kHmax;
+  const int mode = mt.mode;
+  const int row = mt.row;
+  const int nkeep = mt.nkeep;
+  const RowT& rt = mt.rt;
+  uint32_t* bins_w = sm.radix + warp * 256;
+  uint64_t* wbuf = sm.wbuf + warp * kWcap;
+  const uint64_t* gov = a.ws.wovf + (static_cast<int64_t>(blockIdx.x) * kCW + warp) * kWovf;
+  const float m_run = acc.m_run;
+  const int arg_run = acc.arg_run;
+  const int nal = acc.nal, bad = acc.bad, tmo = acc.tmo;
+  const float zref = acc.zref, zs = acc.zs;
+  const unsigned long long qs = acc.qs;
+  int wcnt = acc.wcnt;
+  const int atop = acc.atop;
+  const bool hist_on = acc.hist_on != 0;
+  if (wcnt > kWcap) {
+    warp_compact(wbuf, gov, wcnt, nkeep, bins_w);
+    wcnt = nkeep;
+  }
+  if (lane == 0) sm.wcnt[warp] = wcnt;
+  cbar();
+  const float m_item = cmax_f(m_run, sm.red);
+  const int nallow = csum_i(nal, sm.red);
+  const int badf = cor_i(bad, sm.red);
+  const int tmof = cor_i(tmo, sm.red);
+  int argmax = INT_MAX;
+  double z_item = 0.0;
+  if (mode == 0) {
+    argmax = cmin_i((m_run == m_item && m_item > RL_NEG_INF) ? arg_run : INT_MAX, sm.red);
+  } else {
+    double zl = 0.0;
+    if (zref > RL_NEG_INF && m_item > RL_NEG_INF)
+      zl = static_cast<double>(zs) *
+           exp2((static_cast<double>(zref) - static_cast<double>(m_item)) * (kLog2e / static_cast<double>(rt.T)));
+    z_item = csum_d(zl, sm.red);
+  }
+  int hflags = 0;
+  if (mode == 2) {
+    // every fixed-point mass added must still be in the bins (no u32 wrap)
+    unsigned long long bsum = 0ull;
+    for (int i = tid; i < kNB; i += kConsumers) bsum += sm.hmass[i];
+    const unsigned long long tb = csum_u64(bsum, sm.red);
+    const unsigned long long tq = csum_u64(qs, sm.red);
+    if (tb != tq || !hist_on) hflags = kFlagHistBad;
+  }
+  int ncand = 0;
+  if (mode != 0) {
+    int total = 0;
+    for (int w = 0; w < kCW; ++w) total += sm.wcnt[w];
+    const int need = min(total, nkeep);
+    if (need > 0) {
+      const uint64_t Tk = block_select<false>(sm.wbuf, kCW, kWcap, sm.wcnt, need, sm.radix, sm.red, sm.ctl);
+      ncand = gather_sorted<false>(sm.wbuf, kCW, kWcap, sm.wcnt, Tk, sm.top, sm.ctl);
+    }
+  }
+  ItemSum is;
+  is.m = m_item;
+  is.argmax = argmax;
+  is.nallow = nallow;
+  is.flags = (badf ? kFlagBad : 0) | (tmof ? kFlagTimeout : 0) | hflags;
+  is.z = z_item;
+  is.ncand = ncand;
+  is.atop = (mode == 2) ? atop : kNoAnchor;
+  is.wlo = (mode == 2 && atop != kNoAnchor) ? atop - mt.wbins : 0;
+  is.pad = 0;
+  is.qsum = qs;
+  const int first_item = row * a.nseg;
+  bool run_finisher;
+  if (a.nseg == 1) {
+    if (tid == 0) sm.sums[0] = is;
+    cbar();
+    run_finisher = true;
+  } else {
+    if (tid == 0) a.ws.sums[item] = is;
+    uint64_t* gc = a.ws.cands + static_cast<int64_t>(item) * kN;
+    for (int i = tid; i < ncand; i += kConsumers) gc[i] = sm.top[i];
+    if (mode == 2) {
+      uint32_t* gm = a.ws.hmass + static_cast<int64_t>(item) * kNB;
+      uint32_t* gk = a.ws.hcnt + static_cast<int64_t>(item) * kNB;
+      for (int i = tid; i < kNB; i += kConsumers) {
+        gm[i] = sm.hmass[i];
+        if (mt.need_count) gk[i] = sm.hcnt[i];
+      }
+    }
+    __threadfence();
+    cbar();
+    if (tid == 0) {
+      const int prev = atomicAdd(&a.ws.row_done[row], 1);
+      sm.ctl->is_last = (prev == a.nseg - 1) ? 1 : 0;
+    }
+    cbar();
+    run_finisher = sm.ctl->is_last != 0;
+    if (run_finisher) {
+      __threadfence();
+      for (int s2 = tid; s2 < a.nseg; s2 += kConsumers) {
+        const ItemSum* src = a.ws.sums + first_item + s2;
+        ItemSum t;
+        t.m = __ldcg(&src->m);
+        t.argmax = __ldcg(&src->argmax);
+        t.nallow = __ldcg(&src->nallow);
+        t.flags = __ldcg(&src->flags);
+        t.z = __ldcg(&src->z);
+        t.ncand = __ldcg(&src->ncand);
+        t.atop = __ldcg(&src->atop);
+        t.wlo = __ldcg(&src->wlo);
+        t.pad = 0;
+        t.qsum = __ldcg(&src->qsum);
+        sm.sums[s2] = t;
+      }
+      cbar();
+    }
+  }
+  if (run_finisher) {
+    finish_row<E>(a, mt, tab, first_item);
+    if (a.nseg > 1 && tid == 0) a.ws.row_done[row] = 0;  // ready for the next launch
+  }
+  cbar();
+}
+
+// ---------------------------------------------------------------------------
+// Consumer warps
+// ---------------------------------------------------------------------------
+// The chunks of one item (consumer threads), specialised per row mode so
+// that each mode keeps only the state it needs in registers.
+template <typename E, int MODE>
+__device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int es = static_cast<int>(sizeof(E));
+  const int V = a.V;
+  const int base = warp * kSlice;
+  uint32_t* bins_w = sm.radix + warp * 256;
+  uint64_t* wbuf = sm.wbuf + warp * kWcap;
+  uint64_t* gov = a.ws.wovf + (static_cast<int64_t>(blockIdx.x) * kCW + warp) * kWovf;
+  const ItemMeta& mt = sm.meta[slot];
+  const uint32_t* tab = sm.tab + slot * kHmax;
+  constexpr int mode = MODE;
+  const int row = mt.row;
+  const RowT rt = mt.rt;
+  const int nkeep = mt.nkeep;
+  const int ntab = mt.ntab;
+  const bool mask_on = mt.mask_on != 0;
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
+  const uint32_t* mrow = a.mask ? a.mask + static_cast<int64_t>(row) * a.mask_stride : nullptr;
+  // running state
+  float m_run = RL_NEG_INF;
+  int arg_run = INT_MAX;
+  int nal = 0, bad = 0, tmo = 0;
+  float zref = RL_NEG_INF, zs = 0.0f;
+  unsigned long long qs = 0ull;
+  int wcnt = 0;
+  uint64_t tau = 0ull;
+  float tau_v = RL_NEG_INF;
+  int atop = kNoAnchor;
+  float atop_f = 0.0f, x_lo = RL_POS_INF;
+  const float wb_f = static_cast<float>(mt.wbins);
+  bool hist_on = MODE == 2;
+  int hp = ntab > 0 ? tab_lower_bound(tab, ntab, mt.c0 * kCE) : 0;
+  if (mode == 2)
+    for (int i = tid; i < kNB; i += kConsumers) {
+      sm.hmass[i] = 0u;
+      sm.hcnt[i] = 0u;
+    }
+  if (tid == 0) sm.ctl->tau_shared = 0ull;
+  cbar();
+
+  for (int c = mt.c0; c < mt.c1; ++c, ++cseq) {
+    if (wcnt > kWcompact) {
+      // room for a whole slice of appends (the only call in the loop; no
+      // logits are live here)
+      tau = warp_compact(wbuf, gov, wcnt, nkeep, bins_w);
+      tau_v = key_val(tau);
+      wcnt = nkeep;
+      if (lane == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
+    }
+    const int s = cseq % kNS;
+    const uint32_t ph = static_cast<uint32_t>((cseq / kNS) & 1);
+    if (!mbar_wait(&sm.full[s], ph, kWaitBudget)) tmo = 1;
+    const int start = c * kCE;
+    const int len = min(kCE, V - start);
+    const int nfast = static_cast<int>(chunk_bytes<E>(a, row, start, len)) / es;
+    const int mfast = static_cast<int>(mask_bytes(a, row, start, len)) / 4;
+    E* stg = reinterpret_cast<E*>(sm.stage + s * kStageBytes);
+    const uint32_t* mst = sm.maskst + s * kMaskWords;
+    const int lo = start + base, hi = lo + kSlice;
+    float v[4][4];
+    // penalties patched into the stage (f32 slices entirely in the stage)
+    const bool patch = (es == 4) && (base + kSlice <= nfast);
+    bool patched = false;
+    if (ntab > 0 && patch) {
+      float* f = reinterpret_cast<float*>(stg);
+      while (true) {
+        const int j = hp + lane;
+        const uint32_t ent = j < ntab ? tab[j] : 0xffffffffu;
+        const int id = static_cast<int>(ent >> 11);
+        const bool below = j < ntab && id < hi;
+        const bool mine = below && id >= lo && (ent & 2047u) != 0u;
+        if (mine) f[id - start] = pen_value(f[id - start], static_cast<int>(ent & 2047u), mt.rp, mt.freq, mt.pres);
+        patched |= __any_sync(0xffffffffu, mine);
+        const int adv = __popc(__ballot_sync(0xffffffffu, below));
+        hp += adv;
+        if (adv < 32) break;
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int el0 = base + (q * 32 + lane) * 4;
+      if (el0 < nfast) {
+        if constexpr (es == 4) {
+          const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(stg) + el0);
+          v[q][0] = f.x;
+          v[q][1] = f.y;
+          v[q][2] = f.z;
+          v[q][3] = f.w;
+        } else {
+          const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(stg) + el0);
+          v[q][0] = __uint_as_float(h.x << 16);
+          v[q][1] = __uint_as_float(h.x & 0xffff0000u);
+          v[q][2] = __uint_as_float(h.y << 16);
+          v[q][3] = __uint_as_float(h.y & 0xffff0000u);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int el = el0 + k;
+          v[q][k] = el < len ? to_f32<E>(__ldcg(rowp + start + el)) : RL_NEG_INF;
+        }
+      }
+    }
+    uint32_t mbits[4] = {15u, 15u, 15u, 15u};
+    if (mask_on) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int el0 = base + (q * 32 + lane) * 4;
+        const int wi = el0 >> 5;
+        uint32_t word = 0u;
+        if (wi < mfast) word = mst[wi];
+        else if (el0 < len) word = __ldcg(mrow + (start >> 5) + wi);
+        mbits[q] = (word >> ((lane & 7) * 4)) & 15u;
+      }
+    }
+    // the stage is released: generic writes ordered before the next bulk copy
+    if (patched) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[s]);
+    // penalties in registers (bf16, or slices partly outside the stage)
+    if (ntab > 0 && !patch) pen_regs(v, lo, hi, tab, ntab, hp, mt);
+
+    // ---- per-slice statistics ----
+    float lm = RL_NEG_INF;
+    if (mask_on) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int el = base + (q * 32 + lane) * 4 + k;
+          const bool allowed = el < len && ((mbits[q] >> k) & 1u);
+          float x = allowed ? v[q][k] : RL_NEG_INF;
+          if (allowed) {
+            bad |= (x != x) || (x == RL_POS_INF);
+            nal += (x > RL_NEG_INF) ? 1 : 0;
+          }
+          if (x != x) x = RL_NEG_INF;
+          v[q][k] = x;
+          lm = fmaxf(lm, x);
+        }
+    } else {
+      float fin = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          lm = fmaxf(lm, v[q][k]);
+          fin = __fmaf_rn(v[q][k], 0.0f, fin);
+        }
+      if (fin == 0.0f) {
+        nal += 16;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int el = base + (q * 32 + lane) * 4 + k;
+            float x = v[q][k];
+            if (el < len) {
+              bad |= (x != x) || (x == RL_POS_INF);
+              nal += (x > RL_NEG_INF) ? 1 : 0;
+            }
+            if (x != x) x = RL_NEG_INF;
+            v[q][k] = x;
+          }
+      }
+    }
+    if (mode == 0) {
+      int la = INT_MAX;
+#pragma unroll
+      for (int q = 3; q >= 0; --q)
+#pragma unroll
+        for (int k = 3; k >= 0; --k)
+          if (v[q][k] == lm) la = start + base + (q * 32 + lane) * 4 + k;
+      if (lm > m_run) {
+        m_run = lm;
+        arg_run = la;
+      }
+      continue;
+    }
+    m_run = fmaxf(m_run, lm);
+    // ---- softmax sum (per-lane reference) ----
+    if (lm > RL_NEG_INF) {
+      if (zref == RL_NEG_INF) {
+        zref = lm;
+      } else if ((lm - zref) * rt.c > 8.0f) {
+        zs *= ex2_approx((zref - lm) * rt.c);
+        zref = lm;
+      }
+      float z4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) z4[k] += ex2_approx((v[q][k] - zref) * rt.c);
+      zs += (z4[0] + z4[1]) + (z4[2] + z4[3]);
+    }
+    // ---- candidates ----
+    {
+      const uint64_t ts = *reinterpret_cast<volatile unsigned long long*>(&sm.ctl->tau_shared);
+      if (ts > tau) {
+        tau = ts;
+        tau_v = key_val(ts);
+      }
+      if (__any_sync(0xffffffffu, lm > RL_NEG_INF && lm >= tau_v)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float x = v[q][k];
+            const uint32_t id = static_cast<uint32_t>(start + base + (q * 32 + lane) * 4 + k);
+            const bool take = x > RL_NEG_INF && x >= tau_v && (x > tau_v || cand_key(x, id) >= tau);
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            if (take) {
+              const int idx = wcnt + __popc(bal & ((1u << lane) - 1u));
+              const uint64_t key = cand_key(x, id);
+              if (idx < kWcap) wbuf[idx] = key;
+              else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
+            }
+            wcnt += __popc(bal);
+          }
+      }
+    }
+    // ---- windowed histogram ----
+    if (hist_on) {
+      if (atop == kNoAnchor) {
+        // anchor on the first chunk with an allowed finite logit
+        const float bm = cmax_f(lm, sm.red);
+        if (bm > RL_NEG_INF) {
+          const float af = bin_of(bm, rt);
+          if (fabsf(af) < 4194304.0f) {
+            atop = static_cast<int>(af) + kHead;
+            atop_f = static_cast<float>(atop);
+            x_lo = (atop_f - wb_f - 2.0f) / rt.cb_hi;  // logits below are outside the window
+          } else {
+            hist_on = false;
+          }
+        }
+      }
+      if (atop != kNoAnchor && __any_sync(0xffffffffu, lm >= x_lo)) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float x = v[q][k];
+            if (x >= x_lo) {
+              const float af = bin_of(x, rt);
+              const float rf = atop_f - af;
+              if (rf >= 0.0f && rf <= wb_f) {
+                const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
+                const int r = static_cast<int>(rf);
+                atomicAdd(&sm.hmass[r], qm);
+                if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
+                qs += qm;
+              }
+            }
+          }
+      }
+    }
+  }
+
+  ItemAcc acc;
+  acc.m_run = m_run;
+  acc.arg_run = arg_run;
+  acc.nal = nal;
+  acc.bad = bad;
+  acc.tmo = tmo;
+  acc.zref = zref;
+  acc.zs = zs;
+  acc.qs = qs;
+  acc.wcnt = wcnt;
+  acc.atop = atop;
+  acc.hist_on = hist_on ? 1 : 0;
+  acc.cseq = cseq;
+  return acc;
+}
+
+template <typename E>
+__device__ __noinline__ void consumer_loop(const SpecArgs& a) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  int cseq = 0, mseq = 0;
+  for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
+    const int slot = mseq & 1;
+    const bool timeout = !mbar_wait(&sm.mfull[slot], static_cast<uint32_t>((mseq >> 1) & 1), kWaitBudget);
+    if (cor_i(timeout || *reinterpret_cast<volatile int*>(&sm.ctl->abort), sm.red)) {
+      if (tid == 0) {
+        atomicExch(&sm.ctl->abort, 1);
+        // rows of this CTA that will not be finished
+        for (int it = item; it < a.nitems; it += gridDim.x)
+          if ((it % a.nseg) == 0) write_row(a, it / a.nseg, RL_ERR_TIMEOUT, -1, 0.0f);
+      }
+      return;
+    }
+    const int mode = sm.meta[slot].mode;
+    ItemAcc acc;
+    if (mode == 0) acc = run_item<E, 0>(a, slot, cseq);
+    else if (mode == 1) acc = run_item<E, 1>(a, slot, cseq);
+    else acc = run_item<E, 2>(a, slot, cseq);
+    cseq = acc.cseq;
+    item_end<E>(a, item, slot, acc);
+    // the row data of this slot may be rebuilt
+    if ((tid & 31) == 0) mbar_arrive(&sm.mempty[slot]);
+  }
 }
 
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
 template <typename E>
-__global__ void __launch_bounds__(kCT, 3) spec_chunk_kernel(const SpecArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  const int chunk = blockIdx.x;
-  const int row = blockIdx.y;
-  const int S = gridDim.x;
-  const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + kOffMbar);
-  Ctrl* ctrl = reinterpret_cast<Ctrl*>(smem + kOffCtrl);
-  Walk* wk = reinterpret_cast<Walk*>(smem + kOffWalk);
-  RedScratch* rs = reinterpret_cast<RedScratch*>(smem + kOffRed);
-  uint32_t* cnt = reinterpret_cast<uint32_t*>(smem + kOffCnt);
-  uint32_t* mass = reinterpret_cast<uint32_t*>(smem + kOffMass);
-  int32_t* hist_local = reinterpret_cast<int32_t*>(smem + kOffHist);
-  float* pen_val = reinterpret_cast<float*>(smem + kOffPen);
-  ChunkSum* sums_s = reinterpret_cast<ChunkSum*>(smem + kOffSums);
-  E* data = reinterpret_cast<E*>(smem + kOffData);
-
-  const int V = a.V;
-  const int start = chunk * kCE;
-  const int len = max(0, min(kCE, V - start));
-  constexpr int es = static_cast<int>(sizeof(E));
-  const Workspace& ws = a.ws;
-
-  const rl_row_params prm = a.params[row];
-  const float T = prm.temperature;
-  const bool greedy = !(T > 0.0f);  // NaN is reported as non-finite by the finisher
-  const bool thr_path = prm.top_k > 0 && prm.top_k <= kKthr;
-  const bool hist_path = !greedy && !thr_path;
-
-  // ---- prologue: mbarriers, bulk copy ----
-  const E* src = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start;
-  const uint32_t bulk_bytes = static_cast<uint32_t>(len * es) & ~15u;
-  const bool use_bulk = ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) && bulk_bytes > 0;
-  if (tid == 0) {
-    for (int p = 0; p < kNPiece; ++p) mbar_init(&mbar[p], 1);
+__global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_constant__ SpecArgs a) {
+  const Smem sm = smem_map();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNS; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kCW);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.mfull[s], 1);
+      mbar_init(&sm.mempty[s], kCW);
+    }
+    sm.ctl->abort = 0;
     fence_mbar_init();
-    ctrl->n_local = 0;
-    ctrl->ncand = 0;
-  }
-  if (hist_path)
-    for (int b = tid; b < kNB; b += kCT) {
-      cnt[b] = 0u;
-      mass[b] = 0u;
-    }
-  __syncthreads();
-  if (tid == 0 && use_bulk) {
-    const uint32_t piece = ((bulk_bytes / kNPiece) + 15u) & ~15u;
-    uint32_t off = 0;
-    for (int p = 0; p < kNPiece; ++p) {
-      const uint32_t nb = off < bulk_bytes ? min(piece, bulk_bytes - off) : 0u;
-      mbar_expect_tx(&mbar[p], nb);
-      if (nb > 0)
-        bulk_g2s(reinterpret_cast<unsigned char*>(data) + off,
-                 reinterpret_cast<const unsigned char*>(src) + off, nb, &mbar[p]);
-      off += nb;
-    }
-  }
-
-  // history ids inside this chunk, overlapping the copy
-  const int vstart = a.vocab_offset + start;
-  int hl = a.hist ? a.hist_len[row] : 0;
-  hl = max(0, min(hl, min(a.hist_stride, kHmax)));
-  for (int j = tid; j < hl; j += kCT) {
-    const int h = a.hist[static_cast<int64_t>(row) * a.hist_stride + j];
-    const int loc = h - vstart;
-    if (h >= a.vocab_offset && loc >= 0 && loc < len) hist_local[atomicAdd(&ctrl->n_local, 1)] = loc;
-  }
-  // does the row's mask allow anything? (an all-zero mask allows every id)
-  const uint32_t* mrow = a.mask ? a.mask + static_cast<int64_t>(row) * a.mask_stride : nullptr;
-  int mask_on = 0;
-  if (mrow) {
-    const int nw = (V + 31) >> 5;
-    int any = 0;
-    for (int w0 = 0; w0 < nw && !any; w0 += kCT) {
-      const int w = w0 + tid;
-      uint32_t bits = 0u;
-      if (w < nw) {
-        bits = mrow[w];
-        const int rem = V - w * 32;
-        if (rem < 32) bits &= (1u << rem) - 1u;
-      }
-      any = block_or_i(bits != 0u, rs);
-    }
-    mask_on = any;
-  }
-
-  // ---- wait for the chunk, unaligned remainder, tail padding ----
-  int timed_out = 0;
-  if (use_bulk) {
-    bool ok = true;
-    for (int p = 0; p < kNPiece; ++p) ok &= mbar_wait(&mbar[p], 0, kWaitBudget);
-    timed_out = !ok;
-  }
-  {
-    const int first_plain = use_bulk ? static_cast<int>(bulk_bytes / es) : 0;
-    for (int i = first_plain + tid; i < len; i += kCT) data[i] = src[i];
-    E neg;
-    if constexpr (sizeof(E) == 4) {
-      neg = RL_NEG_INF;
-    } else {
-      neg = kBf16NegInf;
-    }
-    for (int i = len + tid; i < kCE; i += kCT) data[i] = neg;
   }
   __syncthreads();
-
-  // ---- penalties: one warp per history entry (count + first occurrence) ----
-  const int n_local = min(ctrl->n_local, kHmax);
-  for (int t = warp; t < n_local; t += kCW) {
-    const int h = hist_local[t];
-    int c = 0;
-    bool first = true;
-    for (int j0 = 0; j0 < n_local; j0 += 32) {
-      const int j = j0 + lane;
-      const bool eq = j < n_local && hist_local[j] == h;
-      const uint32_t bal = __ballot_sync(0xffffffffu, eq);
-      c += __popc(bal);
-      if (eq && j < t) first = false;
-    }
-    first = __all_sync(0xffffffffu, first);
-    if (lane == 0) {
-      if (first) {
-        float v;
-        if constexpr (sizeof(E) == 4) {
-          v = data[h];
-        } else {
-          v = bf16_bits_to_f32(data[h]);
-        }
-        const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
-        pen_val[t] = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
-      } else {
-        pen_val[t] = __int_as_float(0x7fffffff);  // duplicate entry: no-op
-      }
-    }
-  }
-  __syncthreads();
-  const bool dup_free = true;
-  (void)dup_free;
-  // f32: write the penalised values in place; bf16 chunks cannot hold them,
-  // so they are patched into the registers after every load (few slots).
-  if constexpr (sizeof(E) == 4) {
-    for (int t = tid; t < n_local; t += kCT)
-      if (!(pen_val[t] != pen_val[t])) data[hist_local[t]] = pen_val[t];
-    __syncthreads();
-  }
-  // masked ids -> -inf in place
-  if (mask_on) {
-    for (int g = tid; g < kCE / 4; g += kCT) {
-      const int id0 = start + g * 4;
-      const uint32_t bits = id0 < V ? (mrow[id0 >> 5] >> (id0 & 31)) : 0u;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        if (!((bits >> k) & 1u)) {
-          if constexpr (sizeof(E) == 4) {
-            data[g * 4 + k] = RL_NEG_INF;
-          } else {
-            data[g * 4 + k] = kBf16NegInf;
-          }
-        }
-      }
-    }
-    __syncthreads();
-  }
-  // bf16: patch the penalised slots this thread owns (masked slots stay -inf)
-  auto patch = [&](float (&v)[kGPT][4]) {
-    if constexpr (sizeof(E) == 2) {
-      for (int t = 0; t < n_local; ++t) {
-        const float pv = pen_val[t];
-        if (pv != pv) continue;  // duplicate entry
-        const int h = hist_local[t];
-        const int g = h >> 2;
-        if ((g % kCT) != static_cast<int>(threadIdx.x)) continue;
-        const int q0 = g / kCT;
-#pragma unroll
-        for (int q = 0; q < kGPT; ++q)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (q == q0 && k == (h & 3) && v[q][k] > RL_NEG_INF) v[q][k] = pv;
-      }
-    }
-  };
-
-  // ---- P1: chunk max / allowed count / non-finite; per-thread max ----
-  float mx = RL_NEG_INF;
-  int nallow = 0;
-  int bad = 0;
-  int amx = INT_MAX;
-  {
-    float v[kGPT][4];
-    load_all<E>(data, v);
-    patch(v);
-#pragma unroll
-    for (int q = 0; q < kGPT; ++q) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float x = v[q][k];
-        nallow += (x > RL_NEG_INF) ? 1 : 0;
-        bad |= (x != x) || (x == RL_POS_INF);
-        mx = fmaxf(mx, x);
-      }
-    }
-    if (greedy) {
-#pragma unroll
-      for (int q = 0; q < kGPT; ++q)
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (v[q][k] == mx) amx = min(amx, (static_cast<int>(threadIdx.x) + q * kCT) * 4 + k);
-    }
-  }
-  float m_c;
-  int argmax_c, nallow_c, bad_c;
-  {
-    const float wm = warp_max(mx);
-    int wa = (mx == wm) ? amx : INT_MAX;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) wa = min(wa, __shfl_xor_sync(0xffffffffu, wa, o));
-    const int wn = warp_sum_i(nallow);
-    const int wb = __any_sync(0xffffffffu, bad);
-    __syncthreads();
-    if (lane == 0) {
-      rs->f[warp] = wm;
-      rs->i[warp] = wa;
-      rs->j[warp] = wn | (wb << 30);
-    }
-    __syncthreads();
-    float bm = RL_NEG_INF;
-    int ba = INT_MAX, bn = 0, bb = 0;
-    for (int w = 0; w < kCW; ++w) {
-      bn += rs->j[w] & 0x3fffffff;
-      bb |= rs->j[w] >> 30;
-      if (rs->f[w] > bm) {
-        bm = rs->f[w];
-        ba = rs->i[w];
-      } else if (rs->f[w] == bm) {
-        ba = min(ba, rs->i[w]);
-      }
-    }
-    m_c = bm;
-    argmax_c = ba == INT_MAX ? INT_MAX : ba + start;
-    nallow_c = bn;
-    bad_c = bb ? 1 : 0;
-  }
-
-  double z_c = 0.0;
-  int babs_m = 0;
-  int athr = INT_MIN;
-  float tau = RL_NEG_INF;
-  int binovf = 0;
-  const RowT rt = make_rowt(greedy ? 1.0f : T);
-  if (!greedy && nallow_c > 0 && !bad_c) {
-    babs_m = babs(m_c, rt);
-    float v[kGPT][4];
-    load_all<E>(data, v);
-    patch(v);
-    // ---- P2: Z partial (+ histograms) ----
-    float z4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int q = 0; q < kGPT; ++q) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float x = v[q][k];
-        z4[k] += fast_e(x, m_c, rt);  // -inf contributes 0
-        if (hist_path && x > RL_NEG_INF) {
-          const float y = __fmul_rn(x, rt.cb);
-          const float af = floorf(y);
-          const int b = babs_m - static_cast<int>(af);
-          if (b < kNB) {
-            const float eb = ex2_approx((y - af - 1.0f) * rt.dlt);  // mass relative to the bin top
-            atomicAdd(&cnt[b], 1u);
-            atomicAdd(&mass[b], __float2uint_rn(eb * kMassQ));
-          }
-        }
-      }
-    }
-    z_c = block_sum_d(static_cast<double>((z4[0] + z4[1]) + (z4[2] + z4[3])), rs);
-    // ---- collection threshold ----
-    if (thr_path) {
-      tau = block_kth_lower_bound(mx, prm.top_k, rs);
-      if (!(tau > RL_NEG_INF)) tau = -3.402823466e38f;  // too few values: keep all
-    } else {
-      // first bin whose cumulative count reaches kKbig
-      uint32_t c[kBinsPT];
-      uint32_t csum = 0;
-#pragma unroll
-      for (int q = 0; q < kBinsPT; ++q) {
-        const int b = static_cast<int>(threadIdx.x) * kBinsPT + q;
-        c[q] = b < kNB ? cnt[b] : 0u;
-        csum += c[q];
-        if (c[q] > static_cast<uint32_t>(kBinCntSafe)) binovf = 1;
-      }
-      double tot;
-      const double incl = block_scan_d(static_cast<double>(csum), rs, &tot);
-      double run = incl - static_cast<double>(csum);
-      int bfound = INT_MAX;
-#pragma unroll
-      for (int q = 0; q < kBinsPT; ++q) {
-        if (run < kKbig && run + c[q] >= kKbig && bfound == INT_MAX)
-          bfound = static_cast<int>(threadIdx.x) * kBinsPT + q;
-        run += c[q];
-      }
-      bfound = block_min_i(bfound, rs);
-      binovf = block_or_i(binovf, rs);
-      if (bfound == INT_MAX) {
-        // fewer than kKbig logits in the window: keep the window, and all of
-        // the chunk when nothing lies below it
-        athr = (static_cast<int>(tot) >= nallow_c) ? INT_MIN : babs_m - (kNB - 1);
-      } else {
-        athr = babs_m - bfound;
-      }
-    }
-    // ---- P3: candidate keys into the workspace ----
-    uint64_t* cdst = ws.cands + (static_cast<int64_t>(row) * ws.smax + chunk) * kCapC;
-#pragma unroll
-    for (int q = 0; q < kGPT; ++q) {
-      bool take[4];
-      bool anyt = false;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float x = v[q][k];
-        take[k] = x > RL_NEG_INF && (thr_path ? (x >= tau) : (babs(x, rt) >= athr));
-        anyt |= take[k];
-      }
-      if (!__any_sync(0xffffffffu, anyt)) continue;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t bal = __ballot_sync(0xffffffffu, take[k]);
-        if (bal) {
-          int base = 0;
-          if (lane == 0) base = atomicAdd(&ctrl->ncand, __popc(bal));
-          base = __shfl_sync(0xffffffffu, base, 0);
-          if (take[k]) {
-            const int idx = base + __popc(bal & ((1u << lane) - 1u));
-            if (idx < kCapC)
-              cdst[idx] = cand_key(v[q][k], static_cast<uint32_t>(start + (static_cast<int>(threadIdx.x) + q * kCT) * 4 + k));
-          }
-        }
-      }
-    }
-    if (hist_path) {
-      uint32_t* gc = ws.hcnt + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
-      uint32_t* gm = ws.hmass + (static_cast<int64_t>(row) * ws.smax + chunk) * kNB;
-      for (int b = tid; b < kNB; b += kCT) {
-        gc[b] = cnt[b];
-        gm[b] = mass[b];
-      }
-    }
-  }
-  __syncthreads();
-  if (tid == 0) {
-    ChunkSum s;
-    s.m = m_c;
-    s.argmax = argmax_c;
-    s.nallow = nallow_c;
-    s.flags = bad_c | (timed_out ? 2 : 0) | (ctrl->ncand > kCapC ? 4 : 0) | (binovf ? 8 : 0);
-    s.z = z_c;
-    s.ncand = min(ctrl->ncand, kCapC);
-    s.babs_m = babs_m;
-    s.athr = athr;
-    s.tau = tau;
-    ws.sums[static_cast<int64_t>(row) * ws.smax + chunk] = s;
-    __threadfence();
-    const int prev = atomicAdd(&ws.row_done[row], 1);
-    ctrl->is_last = prev == S - 1;
-  }
-  __syncthreads();
-  if (timed_out) {
-    // never leave with a copy still landing in this CTA's shared memory
-    for (int p = 0; p < kNPiece; ++p) mbar_wait(&mbar[p], 0, kWaitBudget);
-  }
-  if (!ctrl->is_last) return;
-
-  // =====================================================================
-  // Finisher: the last CTA of the row
-  // =====================================================================
-  __threadfence();
-  if (tid < S) {
-    const ChunkSum* src_s = ws.sums + static_cast<int64_t>(row) * ws.smax + tid;
-    ChunkSum s;
-    s.m = __ldcg(&src_s->m);
-    s.argmax = __ldcg(&src_s->argmax);
-    s.nallow = __ldcg(&src_s->nallow);
-    s.flags = __ldcg(&src_s->flags);
-    s.z = __ldcg(&src_s->z);
-    s.ncand = __ldcg(&src_s->ncand);
-    s.babs_m = __ldcg(&src_s->babs_m);
-    s.athr = __ldcg(&src_s->athr);
-    s.tau = __ldcg(&src_s->tau);
-    sums_s[tid] = s;
-  }
-  __syncthreads();
-  float m = RL_NEG_INF;
-  int gargmax = INT_MAX, gallow = 0, gflags = 0;
-  float tau_max = RL_NEG_INF;
-  for (int c = 0; c < S; ++c) {
-    const ChunkSum& s = sums_s[c];
-    gallow += s.nallow;
-    gflags |= s.flags;
-    if (s.nallow > 0) tau_max = fmaxf(tau_max, s.tau);
-    if (s.m > m) {
-      m = s.m;
-      gargmax = s.argmax;
-    } else if (s.m == m) {
-      gargmax = min(gargmax, s.argmax);
-    }
-  }
-  int row_st = 0;
-  if (gflags & 2) row_st = RL_ERR_TIMEOUT;
-  else if ((gflags & 1) || gallow == 0 || !(fabsf(T) < RL_POS_INF)) row_st = RL_ERR_NONFINITE;
-  else if (gflags & 12) row_st = RL_ERR_UNSUPPORTED;
-
-  auto finish = [&](int status, int token, float prob) {
-    if (tid == 0) {
-      const bool ok = status == 0;
-      a.out_tok[row] = ok ? token + a.vocab_offset : -1;
-      if (a.out_prob) a.out_prob[row] = ok ? prob : 0.0f;
-      if (a.row_status) a.row_status[row] = status;
-      ws.row_done[row] = 0;  // ready for the next launch
-    }
-  };
-
-  if (row_st != 0 || greedy) {
-    finish(row_st, gargmax, 1.0f);
-    if (a.list_len && tid == 0) {
-      const bool ok = row_st == 0;
-      a.list_len[row] = (ok && a.list_cap > 0) ? 1 : 0;
-      if (ok && a.list_cap > 0) {
-        a.list_ids[static_cast<int64_t>(row) * a.list_cap] = gargmax + a.vocab_offset;
-        a.list_probs[static_cast<int64_t>(row) * a.list_cap] = 1.0f;
-      }
-    }
-    return;
-  }
-
-  // Z = sum_c z_c * 2^((m_c - m) log2(e) / T)
-  double zpart = 0.0;
-  if (tid < S && sums_s[tid].nallow > 0)
-    zpart = sums_s[tid].z * exp2((static_cast<double>(sums_s[tid].m) - static_cast<double>(m)) *
-                                 (kLog2e / static_cast<double>(T)));
-  const double Z = block_sum_d(zpart, rs);
-  const float u = a.uniforms[row];
-  const int K = (prm.top_k > 0 && prm.top_k < gallow) ? prm.top_k : gallow;
-  const bool mass_mode = prm.top_p < 1.0f;
-  uint64_t* keys = reinterpret_cast<uint64_t*>(data);         // kMergeCap / 2 keys
-  uint64_t* keys2 = keys + kMergeCap / 2;                     // kMergeCap / 2 keys
-  double* gcnt = reinterpret_cast<double*>(keys + kMergeCap);  // kNB (histogram path)
-  double* gmass = gcnt + kNB;                                  // kNB
-  if (tid == 0) {
-    Walk& w = *wk;
-    w.phase = 0;
-    w.K = K;
-    w.mass_mode = mass_mode;
-    w.cut_in_seg = 0;
-    w.cut_idx = -1;
-    w.status = 0;
-    w.token = -1;
-    w.prob = 0.0f;
-    w.count_before = 0;
-    w.mass_before = 0.0;
-    w.Z = Z;
-    w.t2 = static_cast<double>(prm.top_p) * Z;
-    w.S = 0.0;
-    w.t3 = 0.0;
-    ctrl->nsel = 0;
-  }
-  __syncthreads();
-
-  if (thr_path) {
-    // ---- the row's top-k: candidates >= the largest chunk threshold ----
-    // (the row's k-th value >= every chunk's k-th value >= that chunk's tau)
-    for (int c = 0; c < S; ++c) {
-      const int n = sums_s[c].ncand;
-      const uint64_t* srcc = ws.cands + (static_cast<int64_t>(row) * ws.smax + c) * kCapC;
-      for (int i = tid; i < n; i += kCT) {
-        const uint64_t key = __ldcg(srcc + i);
-        if (key_val(key) >= tau_max) {
-          const int idx = atomicAdd(&ctrl->nsel, 1);
-          if (idx < kMergeCap / 2) keys[idx] = key;
-        }
-      }
-    }
-    __syncthreads();
-    int n = ctrl->nsel;
-    if (n > kMergeCap / 2) {
-      finish(RL_ERR_UNSUPPORTED, -1, 0.0f);
-      return;
-    }
-    // tighten once more on the merged keys, then rank-sort the survivors
-    {
-      float tm = RL_NEG_INF;
-      for (int i = tid; i < n; i += kCT) tm = fmaxf(tm, key_val(keys[i]));
-      float t2 = block_kth_lower_bound(tm, K, rs);
-      if (!(t2 > RL_NEG_INF)) t2 = -3.402823466e38f;
-      if (tid == 0) ctrl->nsel = 0;
-      __syncthreads();
-      for (int i = tid; i < n; i += kCT) {
-        const uint64_t key = keys[i];
-        if (key_val(key) >= t2) keys2[atomicAdd(&ctrl->nsel, 1)] = key;
-      }
-      __syncthreads();
-      n = ctrl->nsel;
-    }
-    const int nlist = min(K, n);
-    rank_sort(keys2, n, keys, nlist);  // keys[0..nlist): the top-k, descending
-    double cum_at = 0.0;
-    const int f = sweep(keys, nlist, *wk, m, rt, 0, rs, &cum_at);
-    const int cut = (f == INT_MAX) ? nlist - 1 : f;
-    if (f == INT_MAX) {
-      double tot = 0.0;
-      for (int c0 = 0; c0 < nlist; c0 += kCT) {
-        const int j = c0 + tid;
-        double t;
-        block_scan_d(j < nlist ? static_cast<double>(exact_e(key_val(keys[j]), m, rt)) : 0.0, rs, &t);
-        tot += t;
-      }
-      cum_at = tot;
-    }
-    if (tid == 0) {
-      wk->S = cum_at;
-      wk->t3 = static_cast<double>(u) * cum_at;
-    }
-    __syncthreads();
-    const int d = sweep(keys, cut + 1, *wk, m, rt, 1, rs, &cum_at);
-    const int j = (d == INT_MAX) ? cut : d;
-    if (a.list_len) {
-      const int nl = min(nlist, a.list_cap);
-      for (int i = tid; i < nl; i += kCT) {
-        a.list_ids[static_cast<int64_t>(row) * a.list_cap + i] = static_cast<int>(key_id(keys[i])) + a.vocab_offset;
-        a.list_probs[static_cast<int64_t>(row) * a.list_cap + i] =
-            static_cast<float>(static_cast<double>(exact_e(key_val(keys[i]), m, rt)) / Z);
-      }
-      if (tid == 0) a.list_len[row] = nl;
-    }
-    const float ej = exact_e(key_val(keys[j]), m, rt);
-    finish(0, static_cast<int>(key_id(keys[j])), static_cast<float>(static_cast<double>(ej) / wk->S));
-    return;
-  }
-
-  // ---- histogram path: merge the chunk histograms on the row's grid ----
-  // Row bin j holds absolute bin A = Bmax - j. A logit of bin A has mass
-  // e = e_bin * 2^(((A + 1)/cb - m) * log2(e)/T), e_bin its bin-relative mass.
-  const int Bmax = babs(m, rt);
-  {
-    const double cl = kLog2e / static_cast<double>(T);
-    const double cbd = static_cast<double>(rt.cb);
-    double cq[kBinsPT], mq[kBinsPT];
-    double csum = 0.0, msum = 0.0;
-#pragma unroll
-    for (int q = 0; q < kBinsPT; ++q) {
-      const int j = static_cast<int>(threadIdx.x) * kBinsPT + q;
-      double cc = 0.0, mm = 0.0;
-      if (j < kNB) {
-        const int A = Bmax - j;
-        for (int c = 0; c < S; ++c) {
-          const ChunkSum& s = sums_s[c];
-          if (s.nallow == 0) continue;
-          const int i = s.babs_m - A;
-          if (i >= 0 && i < kNB) {
-            const int64_t base = (static_cast<int64_t>(row) * ws.smax + c) * kNB + i;
-            cc += static_cast<double>(__ldcg(ws.hcnt + base));
-            mm += static_cast<double>(__ldcg(ws.hmass + base));
-          }
-        }
-        mm *= exp2(((static_cast<double>(A) + 1.0) / cbd - static_cast<double>(m)) * cl) / static_cast<double>(kMassQ);
-      }
-      cq[q] = cc;
-      mq[q] = mm;
-      csum += cc;
-      msum += mm;
-    }
-    double tc, tm;
-    double ci = block_scan_d(csum, rs, &tc) - csum;
-    double mi = block_scan_d(msum, rs, &tm) - msum;
-#pragma unroll
-    for (int q = 0; q < kBinsPT; ++q) {
-      const int j = static_cast<int>(threadIdx.x) * kBinsPT + q;
-      ci += cq[q];
-      mi += mq[q];
-      if (j < kNB) {
-        gcnt[j] = ci;
-        gmass[j] = mi;
-      }
-    }
-    __syncthreads();
-  }
-  // gcnt / gmass: inclusive cumulative counts / masses per row bin
-  const bool need_q1 = K < gallow;
-  auto first_bin = [&](int kind, double target) -> int {
-    // kind 0: count >= target; 1: mass >= target; 2: mass > target
-    int b = INT_MAX;
-    for (int j = tid; j < kNB; j += kCT) {
-      const double cur = kind == 0 ? gcnt[j] : gmass[j];
-      const double prev = j ? (kind == 0 ? gcnt[j - 1] : gmass[j - 1]) : 0.0;
-      const bool hit = kind == 2 ? (cur > target && !(prev > target)) : (cur >= target && !(prev >= target));
-      if (hit) b = j;
-    }
-    return block_min_i(b, rs);
-  };
-  int bin;
-  if (!need_q1 && !mass_mode) {
-    // the list is every allowed id: cutoff at its end, S = Z
-    if (tid == 0) {
-      wk->phase = 1;
-      wk->S = Z;
-      wk->t3 = static_cast<double>(u) * Z;
-    }
-    __syncthreads();
-    bin = first_bin(2, wk->t3);
-  } else {
-    const int b1 = need_q1 ? first_bin(0, static_cast<double>(K)) : INT_MAX;
-    const int b2 = mass_mode ? first_bin(1, wk->t2) : INT_MAX;
-    bin = min(b1, b2);
-  }
-  // ---- bin-by-bin walk ----
-  int32_t* hid = reinterpret_cast<int32_t*>(smem + kOffHist);  // finisher history table (sorted)
-  float* hval = reinterpret_cast<float*>(smem + kOffPen);
-  uint64_t* bkeys = keys;   // keys of one bin (<= kMergeCap / 2)
-  uint64_t* skeys = keys2;  // the same, sorted
-  int nh = -1;              // history table built on the first re-read
-  for (int round = 0; round < kMaxRounds; ++round) {
-    if (bin >= kNB) {
-      if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;  // beyond the 64-nat window
-      break;
-    }
-    const int A = Bmax - bin;
-    bool covered = true;
-    for (int c = 0; c < S; ++c)
-      if (sums_s[c].nallow > 0 && sums_s[c].athr > A) covered = false;
-    if (tid == 0) ctrl->nbin = 0;
-    __syncthreads();
-    if (covered) {
-      for (int c = 0; c < S; ++c) {
-        const int n = sums_s[c].ncand;
-        const uint64_t* srcc = ws.cands + (static_cast<int64_t>(row) * ws.smax + c) * kCapC;
-        for (int i = tid; i < n; i += kCT) {
-          const uint64_t key = __ldcg(srcc + i);
-          if (babs(key_val(key), rt) == A) {
-            const int idx = atomicAdd(&ctrl->nbin, 1);
-            if (idx < kMergeCap / 2) bkeys[idx] = key;
-          }
-        }
-      }
-    } else {
-      // re-read the row (L2-resident) for the logits of bin A
-      if (nh < 0) {
-        // sorted, de-duplicated history ids with their penalised values
-        int hlr = a.hist ? a.hist_len[row] : 0;
-        hlr = max(0, min(hlr, min(a.hist_stride, kHmax)));
-        if (tid == 0) ctrl->nsel = 0;
-        __syncthreads();
-        for (int j = tid; j < hlr; j += kCT) {
-          const int hv = a.hist[static_cast<int64_t>(row) * a.hist_stride + j] - a.vocab_offset;
-          if (hv >= 0 && hv < V) bkeys[atomicAdd(&ctrl->nsel, 1)] = (static_cast<uint64_t>(hv) << 32) | j;
-        }
-        __syncthreads();
-        const int nrows = ctrl->nsel;
-        rank_sort(bkeys, nrows, skeys, nrows);  // descending (id, position)
-        const E* xr0 = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
-        if (tid == 0) ctrl->nsel = 0;
-        __syncthreads();
-        // ascending position p is skeys[nrows - 1 - p]; the first of each id run applies
-        for (int p = tid; p < nrows; p += kCT) {
-          const int id = static_cast<int>(skeys[nrows - 1 - p] >> 32);
-          if (p > 0 && static_cast<int>(skeys[nrows - p] >> 32) == id) continue;
-          int c = 0;
-          for (int q = p; q < nrows && static_cast<int>(skeys[nrows - 1 - q] >> 32) == id; ++q) ++c;
-          float v;
-          if constexpr (sizeof(E) == 4) {
-            v = __ldcg(xr0 + id);
-          } else {
-            v = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr0) + id));
-          }
-          const float x1 = (v < 0.0f) ? mul_rn(v, prm.repeat_penalty) : div_rn(v, prm.repeat_penalty);
-          const float pv = sub_rn(sub_rn(x1, mul_rn(static_cast<float>(c), prm.frequency_penalty)), prm.presence_penalty);
-          bkeys[atomicAdd(&ctrl->nsel, 1)] = (static_cast<uint64_t>(static_cast<uint32_t>(id)) << 32) | __float_as_uint(pv);
-        }
-        __syncthreads();
-        nh = ctrl->nsel;
-        rank_sort(bkeys, nh, skeys, nh);  // descending id
-        for (int j = tid; j < nh; j += kCT) {
-          const uint64_t kv = skeys[nh - 1 - j];  // ascending id
-          hid[j] = static_cast<int32_t>(kv >> 32);
-          hval[j] = __uint_as_float(static_cast<uint32_t>(kv & 0xffffffffu));
-        }
-        if (tid == 0) ctrl->nbin = 0;
-        __syncthreads();
-      }
-      const E* xr = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
-      for (int i = tid; i < V; i += kCT) {
-        float x;
-        if constexpr (sizeof(E) == 4) {
-          x = __ldcg(xr + i);
-        } else {
-          x = bf16_bits_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(xr) + i));
-        }
-        if (nh > 0) x = hist_value(x, i, hid, hval, nh);
-        if (mask_on && !((mrow[i >> 5] >> (i & 31)) & 1u)) continue;
-        if (!(x > RL_NEG_INF)) continue;
-        if (babs(x, rt) == A) {
-          const int idx = atomicAdd(&ctrl->nbin, 1);
-          if (idx < kMergeCap / 2) bkeys[idx] = cand_key(x, static_cast<uint32_t>(i));
-        }
-      }
-    }
-    __syncthreads();
-    const int nb = ctrl->nbin;
-    if (nb > kMergeCap / 2) {
-      if (tid == 0) wk->status = RL_ERR_UNSUPPORTED;
-      break;
-    }
-    rank_sort(bkeys, nb, skeys, nb);
-    if (tid == 0) {
-      wk->count_before = bin ? static_cast<long long>(gcnt[bin - 1]) : 0;
-      wk->mass_before = bin ? gmass[bin - 1] : 0.0;
-    }
-    __syncthreads();
-    int next = INT_MAX;
-    double cum_at = 0.0;
-    if (wk->phase == 0) {
-      const int f = sweep(skeys, nb, *wk, m, rt, 0, rs, &cum_at);
-      if (f != INT_MAX) {
-        if (tid == 0) {
-          wk->cut_in_seg = 1;
-          wk->cut_idx = f;
-          wk->S = cum_at;
-          wk->t3 = static_cast<double>(u) * cum_at;
-          wk->phase = 1;
-        }
-      } else {
-        next = bin + 1;
-      }
-    } else if (tid == 0) {
-      wk->cut_in_seg = 0;
-    }
-    __syncthreads();
-    if (wk->phase == 1 && next == INT_MAX) {
-      if (wk->t3 < wk->mass_before) {
-        const int b3 = first_bin(2, wk->t3);
-        next = (b3 < bin) ? b3 : max(0, bin - 1);
-      } else {
-        const int d = sweep(skeys, nb, *wk, m, rt, 1, rs, &cum_at);
-        if (tid == 0) {
-          int j = -1;
-          if (d != INT_MAX && (!wk->cut_in_seg || d <= wk->cut_idx)) j = d;
-          else if (wk->cut_in_seg) j = wk->cut_idx;
-          if (j >= 0) {
-            const uint64_t key = skeys[j];
-            wk->token = static_cast<int>(key_id(key));
-            wk->prob = static_cast<float>(static_cast<double>(exact_e(key_val(key), m, rt)) / wk->S);
-            wk->phase = 2;
-          }
-        }
-        __syncthreads();
-        if (wk->phase != 2) next = bin + 1;
-      }
-    }
-    __syncthreads();
-    if (wk->phase == 2) break;
-    bin = next;
-  }
-  __syncthreads();
-  if (a.list_len && tid == 0) a.list_len[row] = -1;  // lists are reported on the threshold path
-  const Walk& w = *wk;
-  if (w.phase == 2 && w.status == 0) finish(0, w.token, w.prob);
-  else finish(w.status ? w.status : RL_ERR_UNSUPPORTED, -1, 0.0f);
+  const int warp = threadIdx.x >> 5;
+  if (warp == kProdWarp) producer_loop<E>(a);
+  else if (warp == kMetaWarp) meta_loop<E>(a);
+  else consumer_loop<E>(a);
 }
 
 // ---------------------------------------------------------------------------
-// Host launcher
+// Host side
 // ---------------------------------------------------------------------------
+void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas) {
+  const int slots = 2 * num_sms;
+  const int S = spec_chunks(V);
+  int ns = 1;
+  if (B > 0 && B < slots) ns = max(1, min(min(S, kSmax), slots / B));
+  const int c = (S + ns - 1) / ns;
+  ns = (S + c - 1) / c;
+  *nseg = ns;
+  *cps = c;
+  *nctas = max(1, min(B * ns, slots));
+}
+
+int spec_max_ws_items(int num_sms) { return 2 * (2 * num_sms); }
+
 template <typename E>
-static cudaError_t launch_typed(const SpecArgs& a, int S, int smem, cudaStream_t stream) {
-  auto k = spec_chunk_kernel<E>;
-  cudaError_t err = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (err != cudaSuccess) return err;
-  k<<<dim3(S, a.B, 1), dim3(kCT, 1, 1), smem, stream>>>(a);
+static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t stream) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(spec_pipe_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) configured[dev] = 1;
+  }
+  spec_pipe_kernel<E><<<nctas, kThreads, kSmemBytes, stream>>>(a);
   return cudaGetLastError();
 }
 
-cudaError_t launch_spec(const SpecArgs& a, int dtype, cudaStream_t stream) {
-  const int S = spec_chunks(a.V);
-  const int smem = spec_smem_bytes(dtype == RL_BF16 ? 2 : 4);
-  if (dtype == RL_BF16) return launch_typed<uint16_t>(a, S, smem, stream);
-  return launch_typed<float>(a, S, smem, stream);
+cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream) {
+  if (args.B == 0) return cudaSuccess;
+  SpecArgs a = args;
+  int nctas = 0;
+  spec_plan(a.B, a.V, num_sms, &a.nseg, &a.cps, &nctas);
+  a.nitems = a.B * a.nseg;
+  if (a.nseg > 1 && a.nitems > a.ws.max_items) return cudaErrorInvalidValue;
+  return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
 }
 
 }  // namespace rl

@@ -1,55 +1,65 @@
-// Launch interface of the chunked spec sampling kernel.
+// Launch interface of the streaming spec sampling kernel.
 #pragma once
 
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <climits>
+
 #include "rl_sampler.h"
 
 namespace rl {
 
-constexpr int kCT = 384;             // threads per chunk CTA (three CTAs per SM)
-constexpr int kCW = kCT / 32;        // warps per chunk CTA
-constexpr int kCE = 12288;           // logits per chunk (48 KB f32, 24 KB bf16)
-constexpr int kGPT = kCE / kCT / 4;  // groups of 4 logits per thread (8)
-constexpr int kNB = 1024;            // histogram bins per chunk (absolute grid)
-constexpr float kRbin = 16.0f;       // bins per nat of (x - m) / T
-constexpr int kKthr = 128;           // top_k <= kKthr: thread-maximum threshold path
-constexpr int kKbig = 512;           // histogram path: each chunk keeps its top kKbig
-constexpr int kCapC = 1024;          // candidate keys per chunk in the workspace
-constexpr int kSmax = 64;            // max chunks per row
-constexpr int kHmax = 1024;          // max history entries per row
-constexpr int kNPiece = 4;           // bulk-copy pieces per chunk
-constexpr int kMaxRounds = 16;       // bin rounds of the finishing walk
-constexpr int kMergeCap = 4096;      // keys the finishing CTA holds (32 KB)
-constexpr float kMassQ = 1048576.0f; // 2^20 fixed point of bin-relative masses (u32)
-constexpr int kBinCntSafe = 3800;    // a bin holding more elements may overflow its u32 mass
+constexpr int kCW = 8;                     // consumer warps per CTA
+constexpr int kConsumers = kCW * 32;       // consumer threads (named barrier 1)
+constexpr int kThreads = kConsumers + 64;  // + the copy-issuing warp + the row-preparation warp
+constexpr int kProdWarp = kCW;
+constexpr int kMetaWarp = kCW + 1;
+constexpr int kCE = 4096;                  // logits per chunk
+constexpr int kSlice = kCE / kCW;          // logits of one consumer warp per chunk (512)
+constexpr int kNS = 3;                     // chunk stages in flight per CTA
+constexpr int kStageBytes = kCE * 4;       // one stage (f32 chunk; bf16 uses half)
+constexpr int kMaskWords = kCE / 32;       // allowed-token mask words per chunk (128)
+constexpr int kN = 128;                    // candidate keys kept per (row, segment)
+constexpr int kWcap = 256;                 // per-warp candidate buffer (shared memory)
+constexpr int kWovf = 512;                 // per-warp overflow (global): one chunk slice of appends
+constexpr int kWcompact = 192;             // a warp compacts before a chunk when it holds more keys
+constexpr int kNB = 1024;                  // histogram bins (window)
+constexpr float kRbin = 16.0f;             // bins per nat of x / T
+constexpr int kHead = 128;                 // window bins above the anchoring max (8 nats)
+constexpr int kHmax = 1024;                // history entries per row
+constexpr int kCollect = 2048;             // finisher: keys of one bin being resolved
+constexpr float kMassQ = 1048576.0f;       // 2^20 fixed point of bin-relative masses
+constexpr int kSmax = 64;                  // segments per row
 
-// Per-chunk summary written by every chunk CTA.
-struct ChunkSum {
-  float m;       // chunk max over allowed finite (penalised) logits (-inf: none)
-  int argmax;    // lowest row-local id at that max
-  int nallow;    // allowed finite logits in the chunk
-  int flags;     // bit0 non-finite, bit1 copy timeout, bit2 candidate overflow, bit3 bin overflow
-  double z;      // sum of exp((x - m) / T) over the chunk, relative to m
-  int ncand;     // candidate keys written
-  int babs_m;    // absolute bin of m
-  int athr;      // histogram path: every element with absolute bin >= athr was kept
-  float tau;     // threshold path: every element >= tau was kept
+constexpr int kFlagBad = 1;       // NaN / +inf among the allowed logits
+constexpr int kFlagTimeout = 2;   // a wait ran out of its budget
+constexpr int kFlagHistBad = 4;   // histogram unusable (overflow, no anchor)
+constexpr int kNoAnchor = INT_MIN;
+
+// Summary of one (row, segment) item.
+struct ItemSum {
+  float m;        // max over allowed finite (penalised) logits, -inf if none
+  int argmax;     // lowest row-local id at m
+  int nallow;     // allowed finite logits
+  int flags;      // kFlag*
+  double z;       // sum of exp((x - m) / T) over the item
+  int ncand;      // sorted candidate keys written (<= kN)
+  int atop;       // histogram window top (absolute bin), kNoAnchor if none
+  int wlo;        // lowest absolute bin in the window
+  int pad;
+  unsigned long long qsum;  // sum of the fixed-point masses added
 };
 
 // Device workspace owned by the handle (allocated at create).
 struct Workspace {
-  int32_t* row_done;           // [max_batch] arrival counters, reset by the finisher
-  ChunkSum* sums;              // [max_batch * smax]
-  uint64_t* cands;             // [max_batch * smax * kCapC]
-  uint32_t* hcnt;              // [max_batch * smax * kNB] counts per chunk bin
-  uint32_t* hmass;             // [max_batch * smax * kNB] bin-relative masses, 2^20 fixed point
-  int smax;
-};
-
-enum SpecMode : int {
-  kModeSample = 0,  // draw one token per row
+  int32_t* row_done;  // [max_batch] arrival counters, reset by the finisher
+  ItemSum* sums;      // [max_items]
+  uint64_t* cands;    // [max_items * kN]
+  uint32_t* hmass;    // [max_items * kNB]
+  uint32_t* hcnt;     // [max_items * kNB]
+  uint64_t* wovf;     // [max_ctas * kCW * kWovf] per-warp candidate overflow
+  int max_items;      // items of a launch with more than one segment per row
 };
 
 struct SpecArgs {
@@ -72,12 +82,20 @@ struct SpecArgs {
   int32_t* list_len;
   int list_cap;
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
-  int mode;
+  int nseg;          // segments per row
+  int cps;           // chunks per segment
+  int nitems;        // B * nseg
   Workspace ws;
 };
 
-int spec_smem_bytes(int es);
-int spec_chunks(int V);
-cudaError_t launch_spec(const SpecArgs& args, int dtype, cudaStream_t stream);
+int spec_smem_bytes();
+__host__ __device__ inline int spec_chunks(int V) { return (V + kCE - 1) / kCE; }
+// Segments per row, chunks per segment and CTAs for a batch (host side).
+void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas);
+// Items of the largest launch that uses the workspace (more than one segment).
+int spec_max_ws_items(int num_sms);
+// CTAs of the largest launch (the per-warp overflow areas).
+inline int spec_max_ctas(int num_sms) { return 2 * num_sms; }
+cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream);
 
 }  // namespace rl

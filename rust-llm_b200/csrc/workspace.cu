@@ -23,16 +23,14 @@ rl_status alloc_workspace(rl_sampler* h) {
             dalloc(&h->stage_hist_len, B) && dalloc(&h->stage_mask, B * h->mask_words) &&
             dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
             dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
-  // chunked spec kernel workspace: f32 chunks are the smallest (most chunks)
-  const int smax = (h->max_vocab + kCE - 1) / kCE;
-  h->ws.smax = smax;
-  const size_t rows_chunks = B * static_cast<size_t>(smax);
-  ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, rows_chunks) &&
-       dalloc(&h->ws.cands, rows_chunks * kCapC) && dalloc(&h->ws.hcnt, rows_chunks * kNB) &&
-       dalloc(&h->ws.hmass, rows_chunks * kNB);
-  if (ok && smax > kSmax) {
-    return set_error(RL_ERR_SHAPE, "rl_sampler_create: max_vocab needs more chunks per row than supported");
-  }
+  // spec kernel workspace: per-item summaries, candidate lists and
+  // histograms of launches that split rows into segments (at most
+  // spec_max_ws_items items; one-segment rows stay in shared memory)
+  const size_t items = static_cast<size_t>(spec_max_ws_items(h->num_sms));
+  h->ws.max_items = static_cast<int>(items);
+  ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, items) && dalloc(&h->ws.cands, items * kN) &&
+       dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&
+       dalloc(&h->ws.wovf, static_cast<size_t>(spec_max_ctas(h->num_sms)) * kCW * kWovf);
   if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
                cudaDeviceSynchronize() == cudaSuccess;
   if (!ok) {
@@ -57,6 +55,7 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->ws.cands);
   cudaFree(h->ws.hcnt);
   cudaFree(h->ws.hmass);
+  cudaFree(h->ws.wovf);
   h->ws = {};
   if (h->stream) cudaStreamDestroy(h->stream);
   h->stage_logits = nullptr;
