@@ -141,8 +141,7 @@ constexpr int kOffHist = kOffTab + 2 * kHmax * 4;  // mass[kNB] + cnt[kNB] u32
 constexpr int kOffRadix = kOffHist + 2 * kNB * 4;  // kCW x 256 u32 radix bins
 constexpr int kOffWbuf = kOffRadix + kCW * 256 * 4;   // kCW x kWcap keys
 constexpr int kOffMask = kOffWbuf + kCW * kWcap * 8;  // kNS x kMaskWords u32
-constexpr int kOffMscr = kOffMask + kNS * kMaskWords * 4;  // row preparation: 2 x kHmax ids + 128 counters
-constexpr int kOffStage = ((kOffMscr + 2 * kHmax * 4 + 128 * 4 + 127) / 128) * 128;
+constexpr int kOffStage = ((kOffMask + kNS * kMaskWords * 4 + 127) / 128) * 128;
 constexpr int kSmemBytes = kOffStage + kNS * kStageBytes;
 // Finisher reuse: the collect buffer spans the histogram and the radix bins;
 // the merged histogram (two kNB double arrays) the warp buffers.
@@ -176,7 +175,6 @@ struct Smem {
   uint32_t* radix;
   uint64_t* wbuf;
   uint32_t* maskst;
-  int* mscr;
   unsigned char* stage;
 };
 extern __shared__ __align__(128) unsigned char g_smem[];
@@ -202,7 +200,6 @@ __device__ __forceinline__ Smem smem_map() {
   m.radix = reinterpret_cast<uint32_t*>(s + kOffRadix);
   m.wbuf = reinterpret_cast<uint64_t*>(s + kOffWbuf);
   m.maskst = reinterpret_cast<uint32_t*>(s + kOffMask);
-  m.mscr = reinterpret_cast<int*>(s + kOffMscr);
   m.stage = s + kOffStage;
   return m;
 }
@@ -421,11 +418,15 @@ __device__ __forceinline__ int pow2_at_least(int n) {
 __device__ __forceinline__ uint64_t wkey(const uint64_t* buf, const uint64_t* gov, int i) {
   return i < kWcap ? buf[i] : __ldcg(reinterpret_cast<const unsigned long long*>(gov + (i - kWcap)));
 }
+// With min_shift > 0 the walk stops once the bits above min_shift are
+// fixed and returns the lowest key of that bucket: a lower bound that keeps
+// at least need keys (the bucket's other keys too).
 __device__ __forceinline__ uint64_t warp_select(const uint64_t* buf, const uint64_t* gov, int n, int need,
-                                                uint32_t* bins) {
+                                                uint32_t* bins, int min_shift = 0) {
   const int lane = threadIdx.x & 31;
   __syncwarp();
   uint64_t kmin = ~0ull, kmax = 0ull;
+#pragma unroll 1
   for (int i = lane; i < n; i += 32) {
     const uint64_t k = wkey(buf, gov, i);
     kmin = k < kmin ? k : kmin;
@@ -437,11 +438,13 @@ __device__ __forceinline__ uint64_t warp_select(const uint64_t* buf, const uint6
   const int lead = __clzll(static_cast<long long>(kmin ^ kmax));
   int shift = 64 - (lead & ~7);
   uint64_t prefix = shift >= 64 ? 0ull : ((kmax >> shift) << shift);
+#pragma unroll 1
   for (int pass = 0; pass < 8; ++pass) {
     shift -= 8;
     for (int b = lane; b < 256; b += 32) bins[b] = 0u;
     __syncwarp();
-    for (int i = lane; i < n; i += 32) {
+  #pragma unroll 1
+  for (int i = lane; i < n; i += 32) {
       const uint64_t k = wkey(buf, gov, i);
       if (hi_match(k, prefix, shift + 8)) atomicAdd(&bins[static_cast<int>((k >> shift) & 255u)], 1u);
     }
@@ -483,9 +486,10 @@ __device__ __forceinline__ uint64_t warp_select(const uint64_t* buf, const uint6
     __syncwarp();
     prefix |= static_cast<uint64_t>(bucket) << shift;
     need -= static_cast<int>(above);
-    if (shift == 0) return prefix;
+    if (shift <= min_shift) return prefix;
     if (cntb == 1u || static_cast<uint32_t>(need) == cntb) {
       uint64_t mn = ~0ull;
+#pragma unroll 1
       for (int i = lane; i < n; i += 32) {
         const uint64_t k = wkey(buf, gov, i);
         if (hi_match(k, prefix, shift) && k < mn) mn = k;
@@ -496,14 +500,253 @@ __device__ __forceinline__ uint64_t warp_select(const uint64_t* buf, const uint6
   return prefix;
 }
 
+// The need-th largest value among the 512 f32 logits of a warp's slice in
+// shared memory (NaN and -inf ignored; -inf when fewer than need remain),
+// by a radix select on the ordered bits; bins: 256 u32 of this warp.
+__device__ __noinline__ float warp_kth_stage(const float* slice, int need, uint32_t* bins) {
+  const int lane = threadIdx.x & 31;
+  float v[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float x = slice[(q * 4 + k) * 32 + lane];
+      v[q][k] = (x != x) ? RL_NEG_INF : x;
+    }
+  int cnt = 0;
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      if (v[q][k] > RL_NEG_INF) {
+        const uint32_t u = ord_key(v[q][k]);
+        ++cnt;
+        kmin = min(kmin, u);
+        kmax = max(kmax, u);
+      }
+  if (warp_sum_i(cnt) < need) return RL_NEG_INF;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+  }
+  if (kmin == kmax) return ord_key_inv(kmax);
+  const int lead = __clz(static_cast<int>(kmin ^ kmax));
+  int shift = 32 - (lead & ~7);
+  uint32_t prefix = shift >= 32 ? 0u : ((kmax >> shift) << shift);
+  for (int pass = 0; pass < 4; ++pass) {
+    shift -= 8;
+    for (int b = lane; b < 256; b += 32) bins[b] = 0u;
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (v[q][k] > RL_NEG_INF) {
+          const uint32_t u = ord_key(v[q][k]);
+          if (shift + 8 >= 32 || ((u ^ prefix) >> (shift + 8)) == 0u) atomicAdd(&bins[(u >> shift) & 255u], 1u);
+        }
+    __syncwarp();
+    uint32_t c[8];
+    uint32_t ls = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c[j] = bins[255 - 8 * lane - j];
+      ls += c[j];
+    }
+    uint32_t inc = ls;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    const uint32_t exc = inc - ls;
+    const bool hit = exc < static_cast<uint32_t>(need) && inc >= static_cast<uint32_t>(need);
+    const int hl = __ffs(__ballot_sync(0xffffffffu, hit)) - 1;
+    int bucket = 0;
+    uint32_t above = 0, cntb = 0;
+    if (lane == hl) {
+      uint32_t run = exc;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (cntb == 0 && run + c[j] >= static_cast<uint32_t>(need)) {
+          bucket = 255 - 8 * lane - j;
+          above = run;
+          cntb = c[j];
+        }
+        run += c[j];
+      }
+    }
+    bucket = __shfl_sync(0xffffffffu, bucket, hl);
+    above = __shfl_sync(0xffffffffu, above, hl);
+    cntb = __shfl_sync(0xffffffffu, cntb, hl);
+    __syncwarp();
+    prefix |= static_cast<uint32_t>(bucket) << shift;
+    need -= static_cast<int>(above);
+    if (shift == 0) return ord_key_inv(prefix);
+    if (static_cast<uint32_t>(need) == cntb) {
+      uint32_t mn = 0xffffffffu;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (v[q][k] > RL_NEG_INF) {
+            const uint32_t u = ord_key(v[q][k]);
+            if (((u ^ prefix) >> shift) == 0u) mn = min(mn, u);
+          }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mn = min(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+      return ord_key_inv(mn);
+    }
+  }
+  return ord_key_inv(prefix);
+}
+
+// Keeps the keys >= T of a warp's buffer buf[0..n) (n <= kWcap), in order,
+// compacted to the front; returns their count.
+__device__ __forceinline__ int warp_filter(uint64_t* buf, int n, uint64_t T) {
+  const int lane = threadIdx.x & 31;
+  int pos = 0;
+#pragma unroll 1
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t k = i < n ? buf[i] : 0ull;
+    const bool kf = i < n && k >= T;
+    const unsigned b = __ballot_sync(0xffffffffu, kf);
+    __syncwarp();
+    if (kf) buf[pos + __popc(b & ((1u << lane) - 1u))] = k;
+    pos += __popc(b);
+  }
+  __syncwarp();
+  return pos;
+}
+
+// Keys >= T among a warp's n candidates (shared buffer and overflow).
+__device__ __forceinline__ int warp_count_ge(const uint64_t* buf, const uint64_t* gov, int n, uint64_t T) {
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  int c = 0;
+#pragma unroll 1
+  for (int i = lane; i < n; i += 32) c += wkey(buf, gov, i) >= T ? 1 : 0;
+  return warp_sum_i(c);
+}
+// Moves the keys >= T of a warp's n candidates to buf[0..), in order; the
+// caller has checked that they fit in buf.
+__device__ __forceinline__ void warp_keep_ge(uint64_t* buf, const uint64_t* gov, int n, uint64_t T) {
+  const int lane = threadIdx.x & 31;
+  int pos = 0;
+#pragma unroll 1
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t k = i < n ? wkey(buf, gov, i) : 0ull;
+    const bool kf = i < n && k >= T;
+    const unsigned b = __ballot_sync(0xffffffffu, kf);
+    __syncwarp();
+    if (kf) buf[pos + __popc(b & ((1u << lane) - 1u))] = k;
+    pos += __popc(b);
+  }
+  __syncwarp();
+}
+
+// Descending bitonic sort of a warp's buffer buf[0..n) (n <= kN) in place;
+// positions n..pow2 are padded with 0 and not read back.
+__device__ __forceinline__ void warp_sort_desc(uint64_t* buf, int n) {
+  const int lane = threadIdx.x & 31;
+  int P = 1;
+  while (P < n) P <<= 1;
+  for (int i = n + lane; i < P; i += 32) buf[i] = 0ull;
+  __syncwarp();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = lane; i < P; i += 32) {
+        const int l = i ^ j;
+        if (l > i) {
+          const uint64_t x = buf[i], y = buf[l];
+          const bool desc = (i & k) == 0;
+          if (desc ? (x < y) : (x > y)) {
+            buf[i] = y;
+            buf[l] = x;
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// The need-th largest value among the kCE f32 logits of a stage (NaN and
+// -inf ignored; -inf when fewer than need remain), by the consumer threads:
+// a radix select on the ordered bits; bins: 256 u32.
+__device__ __noinline__ float block_kth_stage(const float* stg, int need, uint32_t* bins, Red* rs, Ctl* ctl) {
+  const int tid = threadIdx.x;
+  constexpr int R = kCE / kConsumers;
+  uint32_t u[R];
+  int cnt = 0;
+  uint32_t kmin = 0xffffffffu, kmax = 0u;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float x = stg[r * kConsumers + tid];
+    const bool ok = x > RL_NEG_INF;  // false for NaN
+    u[r] = ok ? ord_key(x) : 0u;
+    if (ok) {
+      ++cnt;
+      kmin = min(kmin, u[r]);
+      kmax = max(kmax, u[r]);
+    }
+  }
+  if (csum_i(cnt, rs) < need) return RL_NEG_INF;
+  kmin = static_cast<uint32_t>(cmin_u64(kmin, rs));
+  kmax = static_cast<uint32_t>(cmax_u64(kmax, rs));
+  if (kmin == kmax) return ord_key_inv(kmax);
+  const int lead = __clz(static_cast<int>(kmin ^ kmax));
+  int shift = 32 - (lead & ~7);
+  uint32_t prefix = shift >= 32 ? 0u : ((kmax >> shift) << shift);
+#pragma unroll 1
+  for (int pass = 0; pass < 4; ++pass) {
+    shift -= 8;
+    bins[tid] = 0u;
+    cbar();
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (u[r] != 0u && (shift + 8 >= 32 || ((u[r] ^ prefix) >> (shift + 8)) == 0u))
+        atomicAdd(&bins[(u[r] >> shift) & 255u], 1u);
+    cbar();
+    const uint32_t c = bins[255 - tid];
+    const uint32_t inc = cscan_u32(c, rs);
+    const uint32_t exc = inc - c;
+    if (exc < static_cast<uint32_t>(need) && inc >= static_cast<uint32_t>(need)) {
+      ctl->sel_bucket = 255 - tid;
+      ctl->sel_above = exc;
+      ctl->sel_cnt = c;
+    }
+    cbar();
+    const int bucket = ctl->sel_bucket;
+    const uint32_t above = ctl->sel_above, cntb = ctl->sel_cnt;
+    cbar();
+    prefix |= static_cast<uint32_t>(bucket) << shift;
+    need -= static_cast<int>(above);
+    if (shift == 0) return ord_key_inv(prefix);
+    if (static_cast<uint32_t>(need) == cntb) {
+      uint32_t mn = 0xffffffffu;
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+        if (u[r] != 0u && ((u[r] ^ prefix) >> shift) == 0u) mn = min(mn, u[r]);
+      return ord_key_inv(static_cast<uint32_t>(cmin_u64(mn, rs)));
+    }
+  }
+  return ord_key_inv(prefix);
+}
+
 // Keeps the top `keep` keys of a warp's candidates (n > keep) in buf[0, keep);
 // returns the bound (the keep-th largest key). The kept keys are written in
 // 32-key windows after the window has been read, so the in-place move is safe.
 __device__ __forceinline__ uint64_t warp_compact(uint64_t* buf, const uint64_t* gov, int n, int keep,
-                                                 uint32_t* bins) {
+                                                 uint32_t* bins, int min_shift = 0) {
   const int lane = threadIdx.x & 31;
-  const uint64_t T = warp_select(buf, gov, n, keep, bins);
+  const uint64_t T = warp_select(buf, gov, n, keep, bins, min_shift);
   int pos = 0;
+#pragma unroll 1
   for (int i0 = 0; i0 < n; i0 += 32) {
     const int i = i0 + lane;
     const uint64_t k = i < n ? wkey(buf, gov, i) : 0ull;
@@ -676,17 +919,11 @@ __device__ __noinline__ void producer_loop(const SpecArgs& a) {
 // ---------------------------------------------------------------------------
 // Row-preparation warp
 // ---------------------------------------------------------------------------
-// The row's history ids in [0, V), sorted ascending by a one-warp LSD radix
-// sort (three 7-bit digits; ids < 2^21), packed as (id << 11) | count: the
-// first copy of an id carries its count, later copies count 0 (skipped).
-// scr: 2 * kHmax ints + 128 counters of this warp. Returns the entry count.
-__device__ __noinline__ int build_table(const SpecArgs& a, int row, int hl, uint32_t* tab, int* scr) {
+// The row's history ids in [0, V), in history order, into tab (the
+// consumers sort them when the item starts). Returns the count.
+__device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, uint32_t* tab) {
   const int lane = threadIdx.x & 31;
-  int* bufA = scr;
-  int* bufB = scr + kHmax;
-  int* cnt = scr + 2 * kHmax;
   const int32_t* h = a.hist + static_cast<int64_t>(row) * a.hist_stride;
-  // valid ids, compacted in history order (loads issued 8 windows at a time)
   int n = 0;
   for (int g0 = 0; g0 < hl; g0 += 256) {
     int ids[8];
@@ -701,72 +938,62 @@ __device__ __noinline__ int build_table(const SpecArgs& a, int row, int hl, uint
       const int id = ids[r] - a.vocab_offset;
       const bool ok = i < hl && id >= 0 && id < a.V;
       const unsigned b = __ballot_sync(0xffffffffu, ok);
-      if (ok) bufA[n + __popc(b & ((1u << lane) - 1u))] = id;
+      if (ok) tab[n + __popc(b & ((1u << lane) - 1u))] = static_cast<uint32_t>(id);
       n += __popc(b);
     }
   }
   __syncwarp();
-  int* src = bufA;
-  int* dst = bufB;
-  for (int shift = 0; shift < 21; shift += 7) {
-    for (int d = lane; d < 128; d += 32) cnt[d] = 0;
-    __syncwarp();
-    for (int i = lane; i < n; i += 32) atomicAdd(&cnt[(src[i] >> shift) & 127], 1);
-    __syncwarp();
-    // exclusive scan of the 128 counters (4 per lane)
-    int c4[4], tot = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      c4[j] = cnt[lane * 4 + j];
-      tot += c4[j];
-    }
-    int inc = tot;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int t = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += t;
-    }
-    int run = inc - tot;
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      cnt[lane * 4 + j] = run;
-      run += c4[j];
-    }
-    __syncwarp();
-    // stable scatter, 32 ids at a time
-    for (int i0 = 0; i0 < n; i0 += 32) {
-      const int i = i0 + lane;
-      const bool ok = i < n;
-      const int key = ok ? src[i] : 0;
-      const int d = ok ? ((key >> shift) & 127) : (128 + lane);
-      const unsigned peers = __match_any_sync(0xffffffffu, d);
-      const int rank = __popc(peers & ((1u << lane) - 1u));
-      const int base = ok ? cnt[d] : 0;
-      __syncwarp();
-      if (ok) {
-        dst[base + rank] = key;
-        if (rank == 0) cnt[d] = base + __popc(peers);
-      }
-      __syncwarp();
-    }
-    int* t = src;
-    src = dst;
-    dst = t;
-  }
-  // src: sorted ids; one entry per position, the first of each run counts it
-  for (int p = lane; p < n; p += 32) {
-    const int id = src[p];
-    uint32_t c = 0u;
-    if (p == 0 || src[p - 1] != id) {
-      int q = p + 1;
-      while (q < n && src[q] == id) ++q;
-      c = static_cast<uint32_t>(min(q - p, 2047));
-    }
-    tab[p] = (static_cast<uint32_t>(id) << 11) | c;
-  }
-  __syncwarp();
   return n;
+}
+
+// Consumers: sorts the slot's raw history ids and packs them as
+// (id << 11) | count -- the first copy of an id carries its count, later
+// copies count 0 (skipped).
+__device__ __noinline__ void sort_table(uint32_t* tab, int n) {
+  const int tid = threadIdx.x;
+  int P = 1;
+  while (P < n) P <<= 1;
+  for (int i = n + tid; i < P; i += kConsumers) tab[i] = 0x7fffffffu;
+  cbar();
+  for (int k = 2; k <= P; k <<= 1) {
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = tid; i < P; i += kConsumers) {
+        const int l = i ^ j;
+        if (l > i) {
+          const uint32_t x = tab[i], y = tab[l];
+          const bool up = (i & k) == 0;
+          if (up ? (x > y) : (x < y)) {
+            tab[i] = y;
+            tab[l] = x;
+          }
+        }
+      }
+      cbar();
+    }
+  }
+  uint32_t packed[kHmax / kConsumers];
+#pragma unroll
+  for (int r = 0; r < kHmax / kConsumers; ++r) {
+    const int p = tid + r * kConsumers;
+    packed[r] = 0u;
+    if (p < n) {
+      const uint32_t id = tab[p];
+      uint32_t c = 0u;
+      if (p == 0 || tab[p - 1] != id) {
+        int q = p + 1;
+        while (q < n && tab[q] == id) ++q;
+        c = static_cast<uint32_t>(min(q - p, 2047));
+      }
+      packed[r] = (id << 11) | c;
+    }
+  }
+  cbar();
+#pragma unroll
+  for (int r = 0; r < kHmax / kConsumers; ++r) {
+    const int p = tid + r * kConsumers;
+    if (p < n) tab[p] = packed[r];
+  }
+  cbar();
 }
 
 template <typename E>
@@ -814,7 +1041,7 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
     int ntab = 0;
     if (a.hist && pen) {
       const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
-      if (hl > 0) ntab = build_table(a, row, hl, tab, sm.mscr);
+      if (hl > 0) ntab = gather_history(a, row, hl, tab);
     }
     // Histogram window depth W (nats below the anchor): the mass below it is
     // at most V e^-W of the row max, kept under a quarter of the smallest
@@ -1187,12 +1414,10 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       const int ncol = ctl->cnt;
       cbar();
       if (ncol <= kCollect) {
-        if (tid == 0) ctl->res_j = ncol;
+        csort_desc(buf, ncol, pow2_at_least(max(ncol, 1)));
+        for (int i = tid; i < need; i += kConsumers) sm.top[i] = buf[i];
         cbar();
-        const int* cn = &ctl->res_j;
-        // (the collect area spans the radix bins: count in the warp-buffer area)
-        const uint64_t Tk = block_select<false>(buf, 1, ncol, cn, need, reinterpret_cast<uint32_t*>(sm.wbuf), rs, ctl);
-        nt = gather_sorted<false>(buf, 1, ncol, cn, Tk, sm.top, ctl);
+        nt = need;
       } else {
         const uint64_t Tk = block_select<true>(base, nseg, kN, sm.segn, need, sm.radix, rs, ctl);
         nt = gather_sorted<true>(base, nseg, kN, sm.segn, Tk, sm.top, ctl);
@@ -1513,9 +1738,22 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
   int wcnt = acc.wcnt;
   const int atop = acc.atop;
   const bool hist_on = acc.hist_on != 0;
-  if (wcnt > kWcap) {
-    warp_compact(wbuf, gov, wcnt, nkeep, bins_w);
-    wcnt = nkeep;
+  if (mode != 0) {
+    // each warp: drop the keys below the item's shared bound; a warp still
+    // holding more than nkeep keeps its exact top-nkeep and shares its bound
+    unsigned long long* tsh = &sm.ctl->tau_shared;
+    if (wcnt <= kWcap) wcnt = warp_filter(wbuf, wcnt, *reinterpret_cast<volatile unsigned long long*>(tsh));
+    if (wcnt > nkeep) {
+      const uint64_t T = warp_compact(wbuf, gov, wcnt, nkeep, bins_w);
+      wcnt = nkeep;
+      if (lane == 0) atomicMax(tsh, static_cast<unsigned long long>(T));
+    }
+  }
+  cbar();
+  if (mode != 0) {
+    // every bound is in: short sorted lists
+    wcnt = warp_filter(wbuf, wcnt, sm.ctl->tau_shared);
+    warp_sort_desc(wbuf, wcnt);
   }
   if (lane == 0) sm.wcnt[warp] = wcnt;
   cbar();
@@ -1549,8 +1787,30 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
     for (int w = 0; w < kCW; ++w) total += sm.wcnt[w];
     const int need = min(total, nkeep);
     if (need > 0) {
-      const uint64_t Tk = block_select<false>(sm.wbuf, kCW, kWcap, sm.wcnt, need, sm.radix, sm.red, sm.ctl);
-      ncand = gather_sorted<false>(sm.wbuf, kCW, kWcap, sm.wcnt, Tk, sm.top, sm.ctl);
+      // rank of each key among the eight sorted lists; the first need go to
+      // sm.top in order
+      for (int f = tid; f < kCW * kN; f += kConsumers) {
+        const int w = f / kN, i = f - w * kN;
+        if (i >= sm.wcnt[w]) continue;
+        const uint64_t key = sm.wbuf[w * kWcap + i];
+        int rank = i;
+#pragma unroll
+        for (int w2 = 0; w2 < kCW; ++w2) {
+          if (w2 == w) continue;
+          // keys of list w2 greater than key (list sorted descending)
+          const uint64_t* l2 = sm.wbuf + w2 * kWcap;
+          int lo = 0, hi = sm.wcnt[w2];
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (l2[mid] > key) lo = mid + 1;
+            else hi = mid;
+          }
+          rank += lo;
+        }
+        if (rank < need) sm.top[rank] = key;
+      }
+      cbar();
+      ncand = need;
     }
   }
   ItemSum is;
@@ -1642,6 +1902,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   const bool mask_on = mt.mask_on != 0;
   const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld;
   const uint32_t* mrow = a.mask ? a.mask + static_cast<int64_t>(row) * a.mask_stride : nullptr;
+  // every chunk of the row shares the row's 16-byte alignment (chunks are
+  // multiples of 16 bytes), so the copy warp's byte counts follow from it
+  const bool row_al = (reinterpret_cast<uintptr_t>(rowp) & 15u) == 0;
+  const bool mrow_al = mrow && (reinterpret_cast<uintptr_t>(mrow) & 15u) == 0;
   // running state
   float m_run = RL_NEG_INF;
   int arg_run = INT_MAX;
@@ -1663,14 +1927,59 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     }
   if (tid == 0) sm.ctl->tau_shared = 0ull;
   cbar();
+  bool pre_patched = false;
+  if constexpr (MODE != 0 && es == 4) {
+    // bound from the item's first chunk (f32, whole in the stage, no mask):
+    // its nkeep-th largest penalised value over all kCE logits, so that the
+    // item appends about nkeep ln(n / kCE) keys in all (the loop below has
+    // no calls)
+    const int start = mt.c0 * kCE;
+    const int len = min(kCE, V - start);
+    const int nfast = row_al ? ((len * es) & ~15) / es : 0;
+    if (!mask_on && nfast == kCE) {
+      const int s = cseq % kNS;
+      float* f = reinterpret_cast<float*>(sm.stage + s * kStageBytes);
+      if (mbar_wait(&sm.full[s], static_cast<uint32_t>((cseq / kNS) & 1), kWaitBudget)) {
+        const int lo = start + base, hi = lo + kSlice;
+        while (ntab > 0) {
+          const int j = hp + lane;
+          const uint32_t ent = j < ntab ? tab[j] : 0xffffffffu;
+          const int id = static_cast<int>(ent >> 11);
+          const bool below = j < ntab && id < hi;
+          const bool mine = below && id >= lo && (ent & 2047u) != 0u;
+          if (mine) f[id - start] = pen_value(f[id - start], static_cast<int>(ent & 2047u), mt.rp, mt.freq, mt.pres);
+          pre_patched |= __any_sync(0xffffffffu, mine);
+          const int adv = __popc(__ballot_sync(0xffffffffu, below));
+          hp += adv;
+          if (adv < 32) break;
+        }
+      }
+      __syncwarp();
+      cbar();  // every warp's penalties are in the stage
+      const float t0 = block_kth_stage(f, nkeep, sm.radix, sm.red, sm.ctl);
+      if (t0 > tau_v) {
+        tau_v = t0;
+        tau = static_cast<uint64_t>(ord_key(t0)) << 32;  // every logit equal to t0 is kept
+        if (tid == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
+      }
+    }
+  }
 
   for (int c = mt.c0; c < mt.c1; ++c, ++cseq) {
     if (wcnt > kWcompact) {
       // room for a whole slice of appends (the only call in the loop; no
       // logits are live here)
-      tau = warp_compact(wbuf, gov, wcnt, nkeep, bins_w);
+      // a bound from the top 16 value bits (two radix passes) keeps nkeep
+      // keys and the rest of their bucket; exact only when that is too many
+      tau = warp_select(wbuf, gov, wcnt, nkeep, bins_w, 48);
+      int kept = warp_count_ge(wbuf, gov, wcnt, tau);
+      if (kept > kWcompact - 64) {
+        tau = warp_select(wbuf, gov, wcnt, nkeep, bins_w);
+        kept = nkeep;
+      }
+      warp_keep_ge(wbuf, gov, wcnt, tau);
+      wcnt = kept;
       tau_v = key_val(tau);
-      wcnt = nkeep;
       if (lane == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
     }
     const int s = cseq % kNS;
@@ -1678,8 +1987,8 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     if (!mbar_wait(&sm.full[s], ph, kWaitBudget)) tmo = 1;
     const int start = c * kCE;
     const int len = min(kCE, V - start);
-    const int nfast = static_cast<int>(chunk_bytes<E>(a, row, start, len)) / es;
-    const int mfast = static_cast<int>(mask_bytes(a, row, start, len)) / 4;
+    const int nfast = row_al ? ((len * es) & ~15) / es : 0;
+    const int mfast = mrow_al ? ((((len + 31) >> 5) * 4) & ~15) / 4 : 0;
     E* stg = reinterpret_cast<E*>(sm.stage + s * kStageBytes);
     const uint32_t* mst = sm.maskst + s * kMaskWords;
     const int lo = start + base, hi = lo + kSlice;
@@ -1703,6 +2012,26 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       }
       __syncwarp();
     }
+    if (nfast == kCE) {
+      // a whole aligned chunk: straight shared-memory loads
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int el0 = base + (q * 32 + lane) * 4;
+        if constexpr (es == 4) {
+          const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(stg) + el0);
+          v[q][0] = f.x;
+          v[q][1] = f.y;
+          v[q][2] = f.z;
+          v[q][3] = f.w;
+        } else {
+          const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(stg) + el0);
+          v[q][0] = __uint_as_float(h.x << 16);
+          v[q][1] = __uint_as_float(h.x & 0xffff0000u);
+          v[q][2] = __uint_as_float(h.y << 16);
+          v[q][3] = __uint_as_float(h.y & 0xffff0000u);
+        }
+      }
+    } else {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int el0 = base + (q * 32 + lane) * 4;
@@ -1728,6 +2057,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         }
       }
     }
+    }
     uint32_t mbits[4] = {15u, 15u, 15u, 15u};
     if (mask_on) {
 #pragma unroll
@@ -1741,7 +2071,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       }
     }
     // the stage is released: generic writes ordered before the next bulk copy
-    if (patched) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (patched || (c == mt.c0 && pre_patched)) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
     // penalties in registers (bf16, or slices partly outside the stage)
@@ -1829,22 +2159,33 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         tau_v = key_val(ts);
       }
       if (__any_sync(0xffffffffu, lm > RL_NEG_INF && lm >= tau_v)) {
+        // slots where some lane may take a logit
+        unsigned m16 = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float x = v[q][k];
-            const uint32_t id = static_cast<uint32_t>(start + base + (q * 32 + lane) * 4 + k);
-            const bool take = x > RL_NEG_INF && x >= tau_v && (x > tau_v || cand_key(x, id) >= tau);
-            const unsigned bal = __ballot_sync(0xffffffffu, take);
-            if (take) {
-              const int idx = wcnt + __popc(bal & ((1u << lane) - 1u));
-              const uint64_t key = cand_key(x, id);
-              if (idx < kWcap) wbuf[idx] = key;
-              else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
-            }
-            wcnt += __popc(bal);
+          for (int k = 0; k < 4; ++k)
+            m16 |= (v[q][k] > RL_NEG_INF && v[q][k] >= tau_v) ? (1u << (q * 4 + k)) : 0u;
+        unsigned wm = m16;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wm |= __shfl_xor_sync(0xffffffffu, wm, o);
+        // a compact (not unrolled) loop over the slots where some lane takes
+#pragma unroll 1
+        while (wm) {
+          const int sl = __ffs(wm) - 1;
+          wm &= wm - 1u;
+          const float x = pick16(v, sl);
+          const uint32_t id = static_cast<uint32_t>(start + base + ((sl >> 2) * 32 + lane) * 4 + (sl & 3));
+          const bool take = ((m16 >> sl) & 1u) && (x > tau_v || cand_key(x, id) >= tau);
+          const unsigned bal = __ballot_sync(0xffffffffu, take);
+          if (take) {
+            const int idx = wcnt + __popc(bal & ((1u << lane) - 1u));
+            const uint64_t key = cand_key(x, id);
+            if (idx < kWcap) wbuf[idx] = key;
+            else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
           }
+          wcnt += __popc(bal);
+        }
       }
     }
     // ---- windowed histogram ----
@@ -1863,24 +2204,28 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
           }
         }
       }
-      if (atop != kNoAnchor && __any_sync(0xffffffffu, lm >= x_lo)) {
+      if (atop != kNoAnchor && lm >= x_lo) {
+        unsigned hm = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float x = v[q][k];
-            if (x >= x_lo) {
-              const float af = bin_of(x, rt);
-              const float rf = atop_f - af;
-              if (rf >= 0.0f && rf <= wb_f) {
-                const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
-                const int r = static_cast<int>(rf);
-                atomicAdd(&sm.hmass[r], qm);
-                if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
-                qs += qm;
-              }
-            }
+          for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= x_lo) ? (1u << (q * 4 + k)) : 0u;
+        // per-lane compact loop over the logits that may fall in the window
+#pragma unroll 1
+        while (hm) {
+          const int sl = __ffs(hm) - 1;
+          hm &= hm - 1u;
+          const float x = pick16(v, sl);
+          const float af = bin_of(x, rt);
+          const float rf = atop_f - af;
+          if (rf >= 0.0f && rf <= wb_f) {
+            const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
+            const int r = static_cast<int>(rf);
+            atomicAdd(&sm.hmass[r], qm);
+            if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
+            qs += qm;
           }
+        }
       }
     }
   }
@@ -1919,6 +2264,7 @@ __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
       return;
     }
     const int mode = sm.meta[slot].mode;
+    if (sm.meta[slot].ntab > 0) sort_table(sm.tab + slot * kHmax, sm.meta[slot].ntab);
     ItemAcc acc;
     if (mode == 0) acc = run_item<E, 0>(a, slot, cseq);
     else if (mode == 1) acc = run_item<E, 1>(a, slot, cseq);

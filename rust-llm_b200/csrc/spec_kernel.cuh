@@ -21,9 +21,9 @@ constexpr int kNS = 3;                     // chunk stages in flight per CTA
 constexpr int kStageBytes = kCE * 4;       // one stage (f32 chunk; bf16 uses half)
 constexpr int kMaskWords = kCE / 32;       // allowed-token mask words per chunk (128)
 constexpr int kN = 128;                    // candidate keys kept per (row, segment)
-constexpr int kWcap = 256;                 // per-warp candidate buffer (shared memory)
+constexpr int kWcap = 512;                 // per-warp candidate buffer (shared memory)
 constexpr int kWovf = 512;                 // per-warp overflow (global): one chunk slice of appends
-constexpr int kWcompact = 192;             // a warp compacts before a chunk when it holds more keys
+constexpr int kWcompact = 384;             // a warp compacts before a chunk when it holds more keys
 constexpr int kNB = 1024;                  // histogram bins (window)
 constexpr float kRbin = 16.0f;             // bins per nat of x / T
 constexpr int kHead = 128;                 // window bins above the anchoring max (8 nats)
