@@ -877,17 +877,37 @@ __device__ __forceinline__ uint32_t mask_bytes(const SpecArgs& a, int row, int s
 // ---------------------------------------------------------------------------
 // Copy warp
 // ---------------------------------------------------------------------------
+// Bulk copy with an L2 eviction-priority hint (rows the finisher may re-read
+// are kept in L2 with evict_last).
+__device__ __forceinline__ void bulk_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 template <typename E>
 __device__ __noinline__ void producer_loop(const SpecArgs& a) {
   if ((threadIdx.x & 31) != 0) return;
   const Smem sm = smem_map();
   const int S = spec_chunks(a.V);
+  const uint64_t keep_l2 = evict_last_policy();
   int seq = 0;
   bool ok = true;
   for (int item = blockIdx.x; item < a.nitems && ok; item += gridDim.x) {
     const int row = item / a.nseg;
     const int seg = item - row * a.nseg;
     const int c0 = seg * a.cps, c1 = min(S, c0 + a.cps);
+    // rows on the histogram path may be re-read by their finisher
+    const float T = a.params[row].temperature;
+    const int tk = a.params[row].top_k;
+    const bool hint = (fabsf(T) < RL_POS_INF) && T > 0.0f && !(tk > 0 && tk <= kN);
     for (int c = c0; c < c1; ++c, ++seq) {
       const int s = seq % kNS;
       const uint32_t ph = static_cast<uint32_t>((seq / kNS) & 1);
@@ -901,9 +921,11 @@ __device__ __noinline__ void producer_loop(const SpecArgs& a) {
       const uint32_t db = chunk_bytes<E>(a, row, start, len);
       const uint32_t mb = mask_bytes(a, row, start, len);
       mbar_expect_tx(&sm.full[s], db + mb);
-      if (db)
-        bulk_g2s(sm.stage + s * kStageBytes,
-                 reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start, db, &sm.full[s]);
+      if (db) {
+        const E* src = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start;
+        if (hint) bulk_g2s_hint(sm.stage + s * kStageBytes, src, db, &sm.full[s], keep_l2);
+        else bulk_g2s(sm.stage + s * kStageBytes, src, db, &sm.full[s]);
+      }
       if (mb)
         bulk_g2s(sm.maskst + s * kMaskWords, a.mask + static_cast<int64_t>(row) * a.mask_stride + (start >> 5), mb,
                  &sm.full[s]);
@@ -1044,14 +1066,14 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
       if (hl > 0) ntab = gather_history(a, row, hl, tab);
     }
     // Histogram window depth W (nats below the anchor): the mass below it is
-    // at most V e^-W of the row max, kept under a quarter of the smallest
-    // tail mass that the cutoff or the draw can reach.
+    // at most V e^-W of the row max, kept under a quarter of the tail mass
+    // that the top-p cutoff leaves (or, without a cutoff, that the draw
+    // leaves). A draw that still lands below the window is resolved by the
+    // exact radix walk.
     int wbins = kNB - 1;
     if (mode == 2 && prm.top_k <= 0) {
       const double p = static_cast<double>(prm.top_p);
-      double tail = 1.0;
-      if (p < 1.0) tail = fmin(tail, 1.0 - p);
-      tail = fmin(tail, (1.0 - static_cast<double>(u)) * fmin(p, 1.0));
+      const double tail = (p < 1.0) ? 1.0 - p : 1.0 - static_cast<double>(u);
       if (tail > 0.0 && p > 0.0) {
         const double W = log(4.0 * static_cast<double>(a.V) / tail) + 1.0;
         wbins = min(wbins, kHead + max(64, static_cast<int>(ceil(W * kRbin))));
@@ -1127,19 +1149,47 @@ __device__ __forceinline__ int tab_lower_bound(const uint32_t* tab, int ntab, in
 }
 // Row re-read: the warp's slice of chunk `start` from global memory,
 // penalised and masked (-inf outside the row or disallowed).
+// Raw logits of a warp's slice of chunk `start` (-inf past the row end):
+// 16-byte vector loads when the chunk is whole and aligned.
 template <typename E>
-__device__ __forceinline__ void load_slice_global(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int& hp,
-                                                  int start, int base, float (&v)[4][4]) {
+__device__ __forceinline__ void load_slice_raw(const E* rowp, int V, int start, int base, float (&v)[4][4]) {
   const int lane = threadIdx.x & 31;
-  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
-  const int len = min(kCE, a.V - start);
+  const int len = min(kCE, V - start);
+  const bool vec = len == kCE && (reinterpret_cast<uintptr_t>(rowp) & 15u) == 0;
+  if (vec) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int el = base + (q * 32 + lane) * 4 + k;
-      v[q][k] = el < len ? to_f32<E>(__ldcg(rowp + start + el)) : RL_NEG_INF;
+    for (int q = 0; q < 4; ++q) {
+      const int el0 = base + (q * 32 + lane) * 4;
+      if constexpr (sizeof(E) == 4) {
+        const float4 f = __ldcs(reinterpret_cast<const float4*>(rowp + start + el0));
+        v[q][0] = f.x;
+        v[q][1] = f.y;
+        v[q][2] = f.z;
+        v[q][3] = f.w;
+      } else {
+        const uint2 h = __ldcs(reinterpret_cast<const uint2*>(rowp + start + el0));
+        v[q][0] = __uint_as_float(h.x << 16);
+        v[q][1] = __uint_as_float(h.x & 0xffff0000u);
+        v[q][2] = __uint_as_float(h.y << 16);
+        v[q][3] = __uint_as_float(h.y & 0xffff0000u);
+      }
     }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int el = base + (q * 32 + lane) * 4 + k;
+        v[q][k] = el < len ? to_f32<E>(__ldcg(rowp + start + el)) : RL_NEG_INF;
+      }
+  }
+}
+// Penalties and mask applied to a raw slice (row re-reads).
+template <typename E>
+__device__ __forceinline__ void finish_slice(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int& hp,
+                                             int start, int base, float (&v)[4][4]) {
+  const int lane = threadIdx.x & 31;
+  const int len = min(kCE, a.V - start);
   if (mt.ntab > 0) pen_regs(v, start + base, start + base + kSlice, tab, mt.ntab, hp, mt);
   if (mt.mask_on) {
     const uint32_t* mrow = a.mask + static_cast<int64_t>(mt.row) * a.mask_stride;
@@ -1152,6 +1202,47 @@ __device__ __forceinline__ void load_slice_global(const SpecArgs& a, const ItemM
       for (int k = 0; k < 4; ++k)
         if (!((bits >> k) & 1u)) v[q][k] = RL_NEG_INF;
     }
+  }
+}
+template <typename E>
+__device__ __forceinline__ void load_slice_global(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int& hp,
+                                                  int start, int base, float (&v)[4][4]) {
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
+  load_slice_raw<E>(rowp, a.V, start, base, v);
+  finish_slice<E>(a, mt, tab, hp, start, base, v);
+}
+// Streams a row (warp w: slice w of every chunk) with the next chunk's loads
+// in flight while the current one is processed; f(x, id) for every allowed
+// finite logit.
+template <typename E, typename F>
+__device__ __forceinline__ void stream_row(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, F f) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int S = spec_chunks(a.V);
+  const int base = warp * kSlice;
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
+  int hp = 0;
+  // three slices in registers: the one being processed and two in flight
+  float n1[4][4], n2[4][4];
+  load_slice_raw<E>(rowp, a.V, 0, base, n1);
+  if (S > 1) load_slice_raw<E>(rowp, a.V, kCE, base, n2);
+#pragma unroll 1
+  for (int c = 0; c < S; ++c) {
+    float v[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[q][k] = n1[q][k];
+        n1[q][k] = n2[q][k];
+      }
+    if (c + 2 < S) load_slice_raw<E>(rowp, a.V, (c + 2) * kCE, base, n2);
+    const int start = c * kCE;
+    finish_slice<E>(a, mt, tab, hp, start, base, v);
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (v[q][k] > RL_NEG_INF) f(v[q][k], start + base + (q * 32 + lane) * 4 + k);
   }
 }
 
@@ -1170,27 +1261,15 @@ __device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status
 template <typename E>
 __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, uint64_t* buf,
                            Ctl* ctl) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int S = spec_chunks(a.V);
   if (threadIdx.x == 0) ctl->cnt = 0;
   cbar();
-  int hp = 0;
-  for (int c = 0; c < S; ++c) {
-    const int start = c * kCE;
-    float v[4][4];
-    load_slice_global<E>(a, mt, tab, hp, start, warp * kSlice, v);
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float x = v[q][k];
-        if (x > RL_NEG_INF && bin_of(x, mt.rt) == A) {
-          const int i = atomicAdd(&ctl->cnt, 1);
-          if (i < kCollect)
-            buf[i] = cand_key(x, static_cast<uint32_t>(start + warp * kSlice + (q * 32 + lane) * 4 + k));
-        }
-      }
-  }
+  const RowT rt = mt.rt;
+  stream_row<E>(a, mt, tab, [&](float x, int id) {
+    if (bin_of(x, rt) == A) {
+      const int i = atomicAdd(&ctl->cnt, 1);
+      if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+    }
+  });
   cbar();
   const int n = ctl->cnt;
   cbar();
@@ -1206,8 +1285,7 @@ template <typename E>
 __device__ __noinline__ uint64_t radix_walk(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float M, int kind,
                                long long cnt_target, double target, long long* cnt_before, double* mass_before) {
   const Smem sm = smem_map();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, tid = threadIdx.x;
-  const int S = spec_chunks(a.V);
+  const int tid = threadIdx.x;
   uint32_t* bcnt = sm.radix;
   double* bmass = reinterpret_cast<double*>(sm.radix + 256);
   unsigned long long* bmax = reinterpret_cast<unsigned long long*>(bmass + 256);
@@ -1219,30 +1297,20 @@ __device__ __noinline__ uint64_t radix_walk(const SpecArgs& a, const ItemMeta& m
     cbar();
     long long my_c = 0;
     double my_m = 0.0;
-    int hp = 0;
-    for (int c = 0; c < S; ++c) {
-      const int start = c * kCE;
-      float v[4][4];
-      load_slice_global<E>(a, mt, tab, hp, start, warp * kSlice, v);
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float x = v[q][k];
-          if (!(x > RL_NEG_INF)) continue;
-          const uint64_t key = cand_key(x, static_cast<uint32_t>(start + warp * kSlice + (q * 32 + lane) * 4 + k));
-          const double e = static_cast<double>(exact_e(x, M, mt.rt));
-          if (hi_match(key, prefix, shift + 8)) {
-            const int b = static_cast<int>((key >> shift) & 255u);
-            atomicAdd(&bcnt[b], 1u);
-            atomicAdd(&bmass[b], e);
-            atomicMax(&bmax[b], static_cast<unsigned long long>(key));
-          } else if (key > prefix) {
-            my_c += 1;
-            my_m += e;
-          }
-        }
-    }
+    const RowT rt = mt.rt;
+    stream_row<E>(a, mt, tab, [&](float x, int id) {
+      const uint64_t key = cand_key(x, static_cast<uint32_t>(id));
+      const double e = static_cast<double>(exact_e(x, M, rt));
+      if (hi_match(key, prefix, shift + 8)) {
+        const int b = static_cast<int>((key >> shift) & 255u);
+        atomicAdd(&bcnt[b], 1u);
+        atomicAdd(&bmass[b], e);
+        atomicMax(&bmax[b], static_cast<unsigned long long>(key));
+      } else if (key > prefix) {
+        my_c += 1;
+        my_m += e;
+      }
+    });
     cbar();
     // logits above the current prefix range
     const long long ca = static_cast<long long>(csum_u64(static_cast<unsigned long long>(my_c), sm.red));
@@ -1750,63 +1818,107 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
     }
   }
   cbar();
-  if (mode != 0) {
-    // every bound is in: short sorted lists
-    wcnt = warp_filter(wbuf, wcnt, sm.ctl->tau_shared);
-    warp_sort_desc(wbuf, wcnt);
+  // every bound is in: each warp keeps its keys >= the item's bound (<= nkeep)
+  if (mode != 0) wcnt = warp_filter(wbuf, wcnt, sm.ctl->tau_shared);
+  // ---- reductions, round 1: max, allowed count, flags, mass sums ----
+  Red* rs = sm.red;
+  {
+    const float wm = warp_max(m_run);
+    const int wn = warp_sum_i(nal);
+    const uint32_t wf = (__any_sync(0xffffffffu, bad) ? 1u : 0u) | (__any_sync(0xffffffffu, tmo) ? 2u : 0u);
+    unsigned long long q = qs, bsum = 0ull;
+    if (mode == 2)
+      for (int i = tid; i < kNB; i += kConsumers) bsum += sm.hmass[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      q += __shfl_xor_sync(0xffffffffu, q, o);
+      bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+    }
+    if (lane == 0) {
+      rs->f[warp] = wm;
+      rs->i[warp] = wn;
+      rs->u[warp] = wf;
+      rs->q[warp] = q;
+      rs->d[warp] = static_cast<double>(bsum);  // < 2^53: exact
+      sm.wcnt[warp] = wcnt;
+    }
   }
-  if (lane == 0) sm.wcnt[warp] = wcnt;
   cbar();
-  const float m_item = cmax_f(m_run, sm.red);
-  const int nallow = csum_i(nal, sm.red);
-  const int badf = cor_i(bad, sm.red);
-  const int tmof = cor_i(tmo, sm.red);
+  float m_item = RL_NEG_INF;
+  int nallow = 0;
+  uint32_t fl = 0u;
+  unsigned long long tq = 0ull;
+  double tb = 0.0;
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) {
+    m_item = fmaxf(m_item, rs->f[w]);
+    nallow += rs->i[w];
+    fl |= rs->u[w];
+    tq += rs->q[w];
+    tb += rs->d[w];
+  }
+  const int badf = fl & 1u, tmof = (fl >> 1) & 1u;
+  // the warps' kept keys, flattened into the (free) radix area
+  uint64_t* flat = reinterpret_cast<uint64_t*>(sm.radix);
+  int total = 0;
+  if (mode != 0) {
+    int off = 0;
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) {
+      if (w < warp) off += sm.wcnt[w];
+      total += sm.wcnt[w];
+    }
+    for (int i = lane; i < wcnt; i += 32) flat[off + i] = wbuf[i];
+  }
+  cbar();
+  // ---- round 2: argmax (greedy) or Z relative to the item max ----
   int argmax = INT_MAX;
   double z_item = 0.0;
-  if (mode == 0) {
-    argmax = cmin_i((m_run == m_item && m_item > RL_NEG_INF) ? arg_run : INT_MAX, sm.red);
-  } else {
+  {
+    int wa = INT_MAX;
     double zl = 0.0;
-    if (zref > RL_NEG_INF && m_item > RL_NEG_INF)
-      zl = static_cast<double>(zs) *
-           exp2((static_cast<double>(zref) - static_cast<double>(m_item)) * (kLog2e / static_cast<double>(rt.T)));
-    z_item = csum_d(zl, sm.red);
+    if (mode == 0) {
+      wa = (m_run == m_item && m_item > RL_NEG_INF) ? arg_run : INT_MAX;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wa = min(wa, __shfl_xor_sync(0xffffffffu, wa, o));
+    } else {
+      if (zref > RL_NEG_INF && m_item > RL_NEG_INF)
+        zl = static_cast<double>(zs) *
+             exp2((static_cast<double>(zref) - static_cast<double>(m_item)) * (kLog2e / static_cast<double>(rt.T)));
+      zl = warp_sum_d(zl);
+      zl = __shfl_sync(0xffffffffu, zl, 0);
+    }
+    if (lane == 0) {
+      rs->i[warp] = wa;
+      rs->d[warp] = zl;
+    }
+  }
+  cbar();
+#pragma unroll
+  for (int w = 0; w < kCW; ++w) {
+    argmax = min(argmax, rs->i[w]);
+    z_item += rs->d[w];
   }
   int hflags = 0;
-  if (mode == 2) {
-    // every fixed-point mass added must still be in the bins (no u32 wrap)
-    unsigned long long bsum = 0ull;
-    for (int i = tid; i < kNB; i += kConsumers) bsum += sm.hmass[i];
-    const unsigned long long tb = csum_u64(bsum, sm.red);
-    const unsigned long long tq = csum_u64(qs, sm.red);
-    if (tb != tq || !hist_on) hflags = kFlagHistBad;
-  }
+  if (mode == 2 && (static_cast<double>(tq) != tb || !hist_on)) hflags = kFlagHistBad;
   int ncand = 0;
   if (mode != 0) {
-    int total = 0;
-    for (int w = 0; w < kCW; ++w) total += sm.wcnt[w];
     const int need = min(total, nkeep);
     if (need > 0) {
-      // rank of each key among the eight sorted lists; the first need go to
-      // sm.top in order
-      for (int f = tid; f < kCW * kN; f += kConsumers) {
-        const int w = f / kN, i = f - w * kN;
-        if (i >= sm.wcnt[w]) continue;
-        const uint64_t key = sm.wbuf[w * kWcap + i];
-        int rank = i;
-#pragma unroll
-        for (int w2 = 0; w2 < kCW; ++w2) {
-          if (w2 == w) continue;
-          // keys of list w2 greater than key (list sorted descending)
-          const uint64_t* l2 = sm.wbuf + w2 * kWcap;
-          int lo = 0, hi = sm.wcnt[w2];
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (l2[mid] > key) lo = mid + 1;
-            else hi = mid;
-          }
-          rank += lo;
+      // rank of each key (distinct keys: the count of greater ones), one key
+      // per thread; the first need go to sm.top in order
+      for (int t = tid; t < total; t += kConsumers) {
+        const uint64_t key = flat[t];
+        int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+        int j = 0;
+        for (; j + 4 <= total; j += 4) {
+          r0 += flat[j] > key ? 1 : 0;
+          r1 += flat[j + 1] > key ? 1 : 0;
+          r2 += flat[j + 2] > key ? 1 : 0;
+          r3 += flat[j + 3] > key ? 1 : 0;
         }
+        for (; j < total; ++j) r0 += flat[j] > key ? 1 : 0;
+        const int rank = (r0 + r1) + (r2 + r3);
         if (rank < need) sm.top[rank] = key;
       }
       cbar();
@@ -2204,27 +2316,58 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
           }
         }
       }
-      if (atop != kNoAnchor && lm >= x_lo) {
+      if (atop != kNoAnchor && __any_sync(0xffffffffu, lm >= x_lo)) {
+        // the warp's logits that may fall in the window, compacted into its
+        // 256-float scratch (batches), then binned one per lane
+        float* scr = reinterpret_cast<float*>(bins_w);
         unsigned hm = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
           for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= x_lo) ? (1u << (q * 4 + k)) : 0u;
-        // per-lane compact loop over the logits that may fall in the window
 #pragma unroll 1
-        while (hm) {
-          const int sl = __ffs(hm) - 1;
-          hm &= hm - 1u;
-          const float x = pick16(v, sl);
-          const float af = bin_of(x, rt);
-          const float rf = atop_f - af;
-          if (rf >= 0.0f && rf <= wb_f) {
-            const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
-            const int r = static_cast<int>(rf);
-            atomicAdd(&sm.hmass[r], qm);
-            if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
-            qs += qm;
+        while (__any_sync(0xffffffffu, hm != 0u)) {
+          // this lane's share of the batch: its lowest set slots, up to 8
+          unsigned take = hm;
+          int mine = __popc(take);
+          if (mine > 8) {
+            take = 0u;
+            unsigned t = hm;
+            for (int j = 0; j < 8; ++j) {
+              take |= t & (0u - t);
+              t &= t - 1u;
+            }
+            mine = 8;
           }
+          hm &= ~take;
+          int inc = mine;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+          }
+          const int total = __shfl_sync(0xffffffffu, inc, 31);
+          int off = inc - mine;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if ((take >> (q * 4 + k)) & 1u) scr[off++] = v[q][k];
+          __syncwarp();
+#pragma unroll 1
+          for (int i = lane; i < total; i += 32) {
+            const float x = scr[i];
+            const float af = bin_of(x, rt);
+            const float rf = atop_f - af;
+            if (rf >= 0.0f && rf <= wb_f) {
+              const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
+              const int r = static_cast<int>(rf);
+              atomicAdd(&sm.hmass[r], qm);
+              if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
+              qs += qm;
+            }
+          }
+          __syncwarp();
         }
       }
     }
