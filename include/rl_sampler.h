@@ -119,6 +119,26 @@ rl_status rl_sample_host(rl_sampler* h, const float* logits, int B, int V, const
                          int32_t* out_tok, float* out_prob);
 
 /*
+ * rl_sample_batch without a handle and without any allocation. No
+ * counterpart in the reference: it serves callers that cannot allocate where
+ * they sample (inside CUDA-graph capture, allocator-free decode loops, FFI
+ * callers with no place to keep a handle). Same arguments and results as
+ * rl_sample_batch, on the current device. Its scratch is a fixed device array
+ * of the library (9.7 MB, the candidate overflow of at most 296 CTAs); sizes
+ * beyond V <= 2093056, hist_stride <= 1024, B <= 65535 return RL_ERR_SHAPE.
+ * The first call on a device looks up the scratch's address and the SM count
+ * (no allocation) -- make it before any stream capture. Nothing in the
+ * scratch must start at zero. Calls that overlap in time on one device share
+ * the scratch and race: serialise them.
+ */
+rl_status rl_sample_batch_static(const void* logits, rl_dtype dtype, int B, int V, int64_t ld,
+                                 const int32_t* hist, const int32_t* hist_len, int hist_stride,
+                                 const uint32_t* mask, int64_t mask_stride,
+                                 const rl_row_params* params, const float* uniforms,
+                                 int32_t* out_tok, float* out_prob, int32_t* row_status,
+                                 void* stream);
+
+/*
  * ref_exact profile: Decoder::sample_with_params (src/decoder.rs:35-100)
  * reproduced quirk for quirk, per row: temperature softmax; if top_p < 1 a
  * stable descending sort, cumsum >= top_p cutoff, zeroing of ORIGINAL ids

@@ -2486,4 +2486,14 @@ cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream
   return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
 }
 
+cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream) {
+  if (args.B == 0) return cudaSuccess;
+  SpecArgs a = args;
+  a.nseg = 1;
+  a.cps = spec_chunks(a.V);
+  a.nitems = a.B;
+  const int nctas = max(1, min(min(a.B, 2 * num_sms), max_ctas));
+  return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
+}
+
 }  // namespace rl

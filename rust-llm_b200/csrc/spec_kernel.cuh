@@ -97,5 +97,8 @@ int spec_max_ws_items(int num_sms);
 // CTAs of the largest launch (the per-warp overflow areas).
 inline int spec_max_ctas(int num_sms) { return 2 * num_sms; }
 cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream);
+// One segment per row (no per-item workspace: only ws.wovf is used), at most
+// max_ctas CTAs (the persistent CTAs loop over the rows).
+cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream);
 
 }  // namespace rl

@@ -82,6 +82,8 @@ def lib():
         L.rl_sample_batch_debug.restype = I
         L.rl_sample_batch_debug.argtypes = [P, P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P,
                                             P, P, I, P]
+        L.rl_sample_batch_static.restype = I
+        L.rl_sample_batch_static.argtypes = [P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P]
         L.rl_sample_host.restype = I
         L.rl_sample_host.argtypes = [P, P, I, I, P, P, I, P, I64, P, P, P, P]
         L.rl_decoder_sample.restype = I
@@ -214,3 +216,28 @@ def params_tensor(p: np.ndarray, device):
     import torch
 
     return torch.from_numpy(np.ascontiguousarray(p).view(np.uint8).copy()).to(device)
+
+
+def sample_static(logits, params, uniforms, hist=None, hist_len=None, mask=None, out_tok=None, out_prob=None,
+                  row_status=None, stream=None):
+    """rl_sample_batch_static: spec sampling on the current device with no
+    handle and no allocation inside the call (outputs are allocated here when
+    not given). Same arguments and results as Sampler.sample."""
+    import torch
+
+    B, V = logits.shape
+    dtype = RL_BF16 if logits.dtype == torch.bfloat16 else RL_F32
+    dev = logits.device
+    if out_tok is None:
+        out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+    if out_prob is None:
+        out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+    if row_status is None:
+        row_status = torch.empty(B, dtype=torch.int32, device=dev)
+    hs = hist.shape[1] if hist is not None else 0
+    ms = mask.shape[1] if mask is not None else 0
+    check(lib().rl_sample_batch_static(_ptr(logits), dtype, B, V, logits.stride(0), _ptr(hist), _ptr(hist_len), hs,
+                                       _ptr(mask), ms, _ptr(params), _ptr(uniforms), _ptr(out_tok), _ptr(out_prob),
+                                       _ptr(row_status), _stream(stream)),
+          "rl_sample_batch_static")
+    return out_tok, out_prob, row_status
