@@ -165,6 +165,56 @@ rl_status rl_grammar_greedy(rl_sampler* h, const float* logits, int B, int V, in
                             void* stream);
 
 /*
+ * Vocabulary-sharded sampling (a row's logits split by vocabulary across
+ * devices). No single reference function: it splits the spec pipeline above
+ * so that each device streams only its columns and the devices exchange 4 KB
+ * per row. Per step:
+ *   1. every shard g calls rl_sample_partial on its columns [off_g, off_g+V_g);
+ *   2. the callers all-gather the keys and stats (e.g. NCCL) into [G, B, ...];
+ *   3. rl_sample_merge draws each row's token from the G partial results.
+ * The result equals rl_sample_batch on the whole row (up to the order in
+ * which the softmax sums are added). Rows with temperature <= 0 take the
+ * argmax; sampled rows need 1 <= top_k <= 128 (RL_ERR_UNSUPPORTED in
+ * row_status otherwise).
+ */
+typedef struct {
+  float m;        /* max over the shard's allowed finite logits (-inf if none) */
+  int32_t argmax; /* lowest global id at m, -1 if none                      */
+  int32_t nallow; /* allowed finite logits of the shard                      */
+  int32_t flags;  /* 1: non-finite input, 2: a device wait ran out            */
+  double z;       /* sum of exp((x - m) / T) over the shard                  */
+  int32_t n;      /* keys in the shard's list                                */
+  int32_t pad;
+} rl_part_stats;  /* 32 bytes */
+
+#define RL_PART_KEYS 128 /* keys per row of a partial list */
+
+/*
+ * One shard's partial result: penalties (history ids are global; ids outside
+ * the shard are skipped), mask (bit i <-> the shard's column i), temperature
+ * and the row's sorted top-min(top_k, 128) list.
+ *  out_keys  [B, RL_PART_KEYS] uint64 keys, descending: bits 63..32 the
+ *            penalised logit as an order-preserving uint32, bits 31..0 the
+ *            bitwise NOT of the global id (equal logits: lower id first).
+ *  out_stats [B] rl_part_stats.
+ */
+rl_status rl_sample_partial(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V,
+                            int64_t ld, int vocab_offset, const int32_t* hist,
+                            const int32_t* hist_len, int hist_stride, const uint32_t* mask,
+                            int64_t mask_stride, const rl_row_params* params, uint64_t* out_keys,
+                            rl_part_stats* out_stats, void* stream);
+
+/*
+ * Merge of G <= 16 partial results per row: keys [G, B, RL_PART_KEYS],
+ * stats [G, B] (shard-major, as an all-gather lays them out). Outputs as
+ * rl_sample_batch.
+ */
+rl_status rl_sample_merge(rl_sampler* h, int G, int B, const uint64_t* keys,
+                          const rl_part_stats* stats, const rl_row_params* params,
+                          const float* uniforms, int32_t* out_tok, float* out_prob,
+                          int32_t* row_status, void* stream);
+
+/*
  * One beam-search step for `items` independent searches of `beams` beams
  * (BeamSearch::search, src/decoder.rs:227-270, batched over items and beams).
  *  logits      [items*beams, V] (row = item*beams + beam), stride ld
@@ -178,8 +228,9 @@ rl_status rl_grammar_greedy(rl_sampler* h, const float* logits, int B, int V, in
  * (decoder.rs:278-284); done = (id == eos). Output per item: the best n_out
  * candidates ordered by score desc, then beam asc, then logit desc, then id asc
  * (the reference's stable-sort order), n_out <= 2*beams:
- *  out_beam/out_tok/out_score/out_done [items, n_out].
- * beams <= 16, 2*beams <= 32.
+ *  out_beam/out_tok/out_score/out_done [items, n_out]; an item with fewer
+ *  candidates than n_out pads with beam = tok = -1, score = -inf.
+ * 1 <= beams <= 16; items * beams <= max_batch; V <= max_vocab.
  */
 rl_status rl_beam_step(rl_sampler* h, const float* logits, int items, int beams, int V,
                        int64_t ld, const float* beam_scores, const uint8_t* beam_done,

@@ -5,11 +5,18 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstddef>
+#include <cstdint>
 #include <string>
 
 #include "rl_sampler.h"
 #include "spec_kernel.cuh"
 #include "internal.h"
+
+static_assert(sizeof(rl_part_stats) == sizeof(rl::PartStats) && offsetof(rl_part_stats, z) == offsetof(rl::PartStats, z) &&
+                  offsetof(rl_part_stats, n) == offsetof(rl::PartStats, nt),
+              "rl_part_stats layout");
+static_assert(RL_PART_KEYS == rl::kN, "partial list length");
 
 namespace {
 
@@ -114,11 +121,12 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
                                const rl_row_params* params, const float* uniforms, int32_t* out_tok,
                                float* out_prob, int32_t* row_status, int32_t* list_ids,
                                float* list_probs, int32_t* list_len, int list_cap, void* stream,
-                               int vocab_offset) {
+                               int vocab_offset, uint64_t* part_keys = nullptr,
+                               rl::PartStats* part_stats = nullptr) {
   if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: handle is NULL");
   if (B < 0 || V <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: B=%d V=%d", B, V);
   if (B == 0) return RL_OK;
-  if (!logits || !params || !uniforms || !out_tok)
+  if (!logits || !params || !uniforms || !(out_tok || part_keys))
     return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: logits, params, uniforms and out_tok are required");
   if (dtype != RL_F32 && dtype != RL_BF16) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: bad dtype %d", dtype);
   if (ld < V) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: ld %lld < V %d", (long long)ld, V);
@@ -157,6 +165,8 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.list_len = list_len;
   a.list_cap = list_cap;
   a.vocab_offset = vocab_offset;
+  a.part_keys = part_keys;
+  a.part_stats = part_stats;
   a.ws = h->ws;
   cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
@@ -182,6 +192,95 @@ rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtyp
   return sample_common(h, logits, dtype, B, V, ld, hist, hist_len, hist_stride, mask, mask_stride, params,
                        uniforms, out_tok, out_prob, row_status, list_ids, list_probs, list_len, list_cap,
                        stream, 0);
+}
+
+rl_status rl_sample_partial(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V, int64_t ld,
+                            int vocab_offset, const int32_t* hist, const int32_t* hist_len, int hist_stride,
+                            const uint32_t* mask, int64_t mask_stride, const rl_row_params* params,
+                            uint64_t* out_keys, rl_part_stats* out_stats, void* stream) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_partial: handle is NULL");
+  if (!out_keys || !out_stats) return fail(RL_ERR_INVALID_ARG, "rl_sample_partial: out_keys and out_stats are required");
+  if (vocab_offset < 0 || static_cast<int64_t>(vocab_offset) + V > INT32_MAX)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_partial: vocab_offset %d out of range", vocab_offset);
+  if (B > h->max_batch) return fail(RL_ERR_SHAPE, "rl_sample_partial: B=%d > max_batch %d", B, h->max_batch);
+  return sample_common(h, logits, dtype, B, V, ld, hist, hist_len, hist_stride, mask, mask_stride, params,
+                       h->zero_u, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, stream, vocab_offset,
+                       out_keys, reinterpret_cast<rl::PartStats*>(out_stats));
+}
+
+rl_status rl_sample_merge(rl_sampler* h, int G, int B, const uint64_t* keys, const rl_part_stats* stats,
+                          const rl_row_params* params, const float* uniforms, int32_t* out_tok, float* out_prob,
+                          int32_t* row_status, void* stream) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_merge: handle is NULL");
+  if (G <= 0 || B < 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_merge: G=%d B=%d", G, B);
+  if (G > rl::kMergeMaxShards) return fail(RL_ERR_SHAPE, "rl_sample_merge: G=%d > %d", G, rl::kMergeMaxShards);
+  if (B == 0) return RL_OK;
+  if (!keys || !stats || !params || !uniforms || !out_tok)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_merge: keys, stats, params, uniforms and out_tok are required");
+  DeviceGuard g(h->device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  rl::MergeArgs m = {};
+  m.keys = keys;
+  m.stats = reinterpret_cast<const rl::PartStats*>(stats);
+  m.G = G;
+  m.B = B;
+  m.params = params;
+  m.uniforms = uniforms;
+  m.out_tok = out_tok;
+  m.out_prob = out_prob;
+  m.row_status = row_status;
+  cudaError_t e = rl::launch_shard_merge(m, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rl_sample_merge launch");
+  return RL_OK;
+}
+
+rl_status rl_beam_step(rl_sampler* h, const float* logits, int items, int beams, int V, int64_t ld,
+                       const float* beam_scores, const uint8_t* beam_done, const int32_t* beam_len, float alpha,
+                       int eos, int log_softmax, int n_out, int32_t* out_beam, int32_t* out_tok, float* out_score,
+                       uint8_t* out_done, void* stream) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_beam_step: handle is NULL");
+  if (items < 0 || beams < 1 || beams > rl::kBeamMaxBeams)
+    return fail(RL_ERR_INVALID_ARG, "rl_beam_step: items=%d beams=%d (1 <= beams <= %d)", items, beams,
+                rl::kBeamMaxBeams);
+  if (n_out < 1 || n_out > 2 * beams)
+    return fail(RL_ERR_INVALID_ARG, "rl_beam_step: n_out=%d not in [1, 2*beams]", n_out);
+  if (items == 0) return RL_OK;
+  if (!logits || !beam_scores || !beam_done || !out_beam || !out_tok || !out_score || !out_done ||
+      (alpha != 1.0f && !beam_len))
+    return fail(RL_ERR_INVALID_ARG, "rl_beam_step: a required pointer is NULL");
+  const int rows = items * beams;
+  if (static_cast<int64_t>(items) * beams > h->max_batch)
+    return fail(RL_ERR_SHAPE, "rl_beam_step: items*beams=%lld > max_batch %d",
+                static_cast<long long>(items) * beams, h->max_batch);
+  DeviceGuard g(h->device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // every row: T = 1, top_k = 2*beams, no nucleus cut, no penalties
+  cudaError_t e = rl::launch_fill_params(h->beam_params, rows, 2 * beams, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rl_beam_step: params");
+  rl_status st = sample_common(h, logits, RL_F32, rows, V, ld, nullptr, nullptr, 0, nullptr, 0, h->beam_params,
+                               h->zero_u, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, stream, 0,
+                               h->part_keys, h->part_stats);
+  if (st != RL_OK) return st;
+  rl::BeamArgs b = {};
+  b.keys = h->part_keys;
+  b.stats = h->part_stats;
+  b.items = items;
+  b.beams = beams;
+  b.scores = beam_scores;
+  b.done = beam_done;
+  b.lens = beam_len;
+  b.alpha = alpha;
+  b.eos = eos;
+  b.log_softmax = log_softmax;
+  b.n_out = n_out;
+  b.out_beam = out_beam;
+  b.out_tok = out_tok;
+  b.out_score = out_score;
+  b.out_done = out_done;
+  e = rl::launch_beam_combine(b, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rl_beam_step: combine launch");
+  return RL_OK;
 }
 
 rl_status rl_sample_host(rl_sampler* h, const float* logits, int B, int V, const int32_t* hist,

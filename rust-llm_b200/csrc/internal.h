@@ -28,6 +28,11 @@ struct rl_sampler {
   int32_t* stage_status = nullptr;
   // workspace of the chunked spec kernel (arrival counters zeroed at create)
   rl::Workspace ws = {};
+  // partial results of rl_beam_step (allocated at create, [max_batch])
+  uint64_t* part_keys = nullptr;      // [max_batch * kN]
+  rl::PartStats* part_stats = nullptr;
+  rl_row_params* beam_params = nullptr;
+  float* zero_u = nullptr;            // uniforms of partial launches (unused, zero)
 };
 
 namespace rl {

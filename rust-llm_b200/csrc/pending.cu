@@ -10,9 +10,4 @@ rl_status rl_decoder_sample(rl_sampler*, const float*, int, int, int64_t, const 
   return rl::set_error(RL_ERR_UNSUPPORTED, "rl_decoder_sample: not built yet");
 }
 
-rl_status rl_beam_step(rl_sampler*, const float*, int, int, int, int64_t, const float*, const uint8_t*,
-                       const int32_t*, float, int, int, int, int32_t*, int32_t*, float*, uint8_t*, void*) {
-  return rl::set_error(RL_ERR_UNSUPPORTED, "rl_beam_step: not built yet");
-}
-
 }  // extern "C"

@@ -1250,6 +1250,19 @@ __device__ __forceinline__ void stream_row(const SpecArgs& a, const ItemMeta& mt
 // Finisher
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status, int token, float prob) {
+  if (a.part_keys) {
+    // partial launch: an unfinished row is reported through its summary
+    PartStats ps;
+    ps.m = RL_NEG_INF;
+    ps.argmax = -1;
+    ps.nallow = 0;
+    ps.flags = status == RL_ERR_TIMEOUT ? kFlagTimeout : kFlagBad;
+    ps.z = 0.0;
+    ps.nt = 0;
+    ps.pad = 0;
+    a.part_stats[row] = ps;
+    return;
+  }
   const bool ok = status == 0;
   a.out_tok[row] = ok ? token + a.vocab_offset : -1;
   if (a.out_prob) a.out_prob[row] = ok ? prob : 0.0f;
@@ -1388,6 +1401,31 @@ __device__ int sweep_sorted(const uint64_t* keys, int n, float M, double Z, cons
   return INT_MAX;
 }
 
+// Softmax sum of a row from its segment summaries, relative to the row max.
+__device__ __forceinline__ double row_z(const ItemSum* sums, int nseg, float M, float T) {
+  const double cd = kLog2e / static_cast<double>(T);
+  double Z = 0.0;
+  for (int s = 0; s < nseg; ++s) {
+    const ItemSum& q = sums[s];
+    if (q.nallow > 0 && q.m > RL_NEG_INF) Z += q.z * exp2((static_cast<double>(q.m) - static_cast<double>(M)) * cd);
+  }
+  return Z;
+}
+
+// Summary of a partial launch's row (global argmax id, -1 if none).
+__device__ __forceinline__ void write_part(const SpecArgs& a, int row, float M, int argmax, int nallow, int flags,
+                                           double Z, int nt) {
+  PartStats ps;
+  ps.m = M;
+  ps.argmax = (argmax == INT_MAX) ? -1 : argmax + a.vocab_offset;
+  ps.nallow = nallow;
+  ps.flags = flags & (kFlagBad | kFlagTimeout);
+  ps.z = Z;
+  ps.nt = nt;
+  ps.pad = 0;
+  a.part_stats[row] = ps;
+}
+
 // The finisher of a row (consumer threads). On entry sm.sums[0..nseg) hold
 // the segment summaries; for a one-segment row sm.top holds the sorted list
 // and the histogram is in shared memory.
@@ -1418,6 +1456,11 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
   if (flags & kFlagTimeout) status = RL_ERR_TIMEOUT;
   else if ((flags & kFlagBad) || nallow == 0 || !(fabsf(T) < RL_POS_INF)) status = RL_ERR_NONFINITE;
   const bool want_list = a.list_len != nullptr;
+  if (a.part_keys && (status != 0 || mt.mode != 1)) {
+    // partial launch of a row without a list (greedy, or not a top-k row)
+    if (tid == 0) write_part(a, row, M, argmax, nallow, flags, mt.mode == 0 ? 0.0 : row_z(sm.sums, nseg, M, T), 0);
+    return;
+  }
   if (status != 0 || mt.mode == 0) {
     if (tid == 0) {
       write_row(a, row, status, argmax, 1.0f);
@@ -1433,12 +1476,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
     return;
   }
   const RowT& rt = mt.rt;
-  const double cd = kLog2e / static_cast<double>(T);
-  double Z = 0.0;
-  for (int s = 0; s < nseg; ++s) {
-    const ItemSum& q = sm.sums[s];
-    if (q.nallow > 0 && q.m > RL_NEG_INF) Z += q.z * exp2((static_cast<double>(q.m) - static_cast<double>(M)) * cd);
-  }
+  const double Z = row_z(sm.sums, nseg, M, T);
   // ---- the row's sorted list ----
   int nt = 0;
   if (nseg == 1) {
@@ -1491,6 +1529,16 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         nt = gather_sorted<true>(base, nseg, kN, sm.segn, Tk, sm.top, ctl);
       }
     }
+  }
+  if (a.part_keys) {
+    // partial launch: the row's (shard's) sorted list with global ids
+    for (int i = tid; i < nt; i += kConsumers) {
+      const uint64_t k = sm.top[i];
+      a.part_keys[static_cast<int64_t>(row) * kN + i] =
+          cand_key(key_val(k), key_id(k) + static_cast<uint32_t>(a.vocab_offset));
+    }
+    if (tid == 0) write_part(a, row, M, argmax, nallow, flags, Z, nt);
+    return;
   }
   const int K = (mt.top_k > 0 && mt.top_k < nallow) ? mt.top_k : nallow;
   const bool mass_mode = mt.top_p < 1.0f;
@@ -2494,6 +2542,232 @@ cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int
   a.nitems = a.B;
   const int nctas = max(1, min(min(a.B, 2 * num_sms), max_ctas));
   return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Beam step: the rows' partial results combined per item (BeamSearch::search,
+// src/decoder.rs:227-270). One CTA of kConsumers threads per item.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kConsumers) beam_combine_kernel(const __grid_constant__ BeamArgs b) {
+  __shared__ float cs[kBeamMaxCand];
+  __shared__ int co[kBeamMaxCand];
+  __shared__ int ct[kBeamMaxCand];
+  __shared__ unsigned char cdn[kBeamMaxCand];
+  __shared__ int nc;
+  const int item = blockIdx.x, tid = threadIdx.x;
+  const int k = 2 * b.beams;
+  if (tid == 0) nc = 0;
+  __syncthreads();
+  // candidates in the reference's push order: beam ascending, then the beam's
+  // list order (value desc, id asc); order key = beam * 64 + position
+  for (int f = tid; f < b.beams * k; f += blockDim.x) {
+    const int bm = f / k, j = f - bm * k;
+    const int row = item * b.beams + bm;
+    if (b.done[row]) {
+      if (j == 0) {
+        const int i = atomicAdd(&nc, 1);
+        cs[i] = b.scores[row];
+        co[i] = bm * 64;
+        ct[i] = -1;
+        cdn[i] = 1;
+      }
+      continue;
+    }
+    const PartStats ps = b.stats[row];
+    if (j >= ps.nt) continue;
+    const uint64_t key = b.keys[static_cast<int64_t>(row) * kN + j];
+    const float x = key_val(key);
+    float v = x;
+    if (b.log_softmax) {
+      const float lse = static_cast<float>(static_cast<double>(ps.m) + log(ps.z));
+      v = __fsub_rn(x, lse);
+    }
+    float lp = 1.0f;
+    if (b.alpha != 1.0f) lp = powf(__fdiv_rn(__fadd_rn(static_cast<float>(b.lens[row] + 1), 6.0f), 6.0f), b.alpha);
+    const int id = static_cast<int>(key_id(key));
+    const int i = atomicAdd(&nc, 1);
+    cs[i] = __fdiv_rn(__fadd_rn(b.scores[row], v), lp);
+    co[i] = bm * 64 + j;
+    ct[i] = id;
+    cdn[i] = id == b.eos ? 1 : 0;
+  }
+  __syncthreads();
+  const int n = nc;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float sc = cs[i];
+    const int oi = co[i];
+    int rank = 0;
+    for (int j = 0; j < n; ++j) rank += (cs[j] > sc || (!(cs[j] < sc) && !(cs[j] > sc) && co[j] < oi)) ? 1 : 0;
+    if (rank < b.n_out) {
+      const int64_t o = static_cast<int64_t>(item) * b.n_out + rank;
+      b.out_beam[o] = oi >> 6;
+      b.out_tok[o] = ct[i];
+      b.out_score[o] = sc;
+      b.out_done[o] = cdn[i];
+    }
+  }
+  for (int r = n + tid; r < b.n_out; r += blockDim.x) {
+    const int64_t o = static_cast<int64_t>(item) * b.n_out + r;
+    b.out_beam[o] = -1;
+    b.out_tok[o] = -1;
+    b.out_score[o] = RL_NEG_INF;
+    b.out_done[o] = 0;
+  }
+}
+
+cudaError_t launch_beam_combine(const BeamArgs& b, cudaStream_t stream) {
+  if (b.items == 0) return cudaSuccess;
+  beam_combine_kernel<<<b.items, kConsumers, 0, stream>>>(b);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Vocabulary shards: the G partial results of each row merged, then the
+// finisher's cutoff and draw. One CTA of kConsumers threads per row.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kConsumers) shard_merge_kernel(const __grid_constant__ MergeArgs m) {
+  __shared__ uint64_t keys[kMergeMax];
+  __shared__ uint64_t top[kN];
+  __shared__ double cum[kN];
+  __shared__ float ev[kN];
+  __shared__ double wsum[kCW];
+  __shared__ int cnt;
+  const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const rl_row_params prm = m.params[row];
+  const float T = prm.temperature;
+  // row summary over the shards (argmax: lowest global id at the max)
+  float M = RL_NEG_INF;
+  int argmax = INT_MAX, nallow = 0, flags = 0;
+  for (int g = 0; g < m.G; ++g) {
+    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    nallow += ps.nallow;
+    flags |= ps.flags;
+    if (ps.nallow == 0) continue;
+    if (ps.m > M) {
+      M = ps.m;
+      argmax = ps.argmax;
+    } else if (ps.m == M) {
+      argmax = min(argmax, ps.argmax);
+    }
+  }
+  int status = 0;
+  if (flags & kFlagTimeout) status = RL_ERR_TIMEOUT;
+  else if ((flags & kFlagBad) || nallow == 0 || !(fabsf(T) < RL_POS_INF)) status = RL_ERR_NONFINITE;
+  const bool greedy = !(T > 0.0f);
+  if (!greedy && status == 0 && !(prm.top_k > 0 && prm.top_k <= kN)) status = RL_ERR_UNSUPPORTED;
+  if (status != 0 || greedy) {
+    if (tid == 0) {
+      m.out_tok[row] = status == 0 ? argmax : -1;
+      if (m.out_prob) m.out_prob[row] = status == 0 ? 1.0f : 0.0f;
+      if (m.row_status) m.row_status[row] = status;
+    }
+    return;
+  }
+  const RowT rt = make_rowt(T);
+  const double cd = kLog2e / static_cast<double>(T);
+  double Z = 0.0;
+  for (int g = 0; g < m.G; ++g) {
+    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    if (ps.nallow > 0 && ps.m > RL_NEG_INF) Z += ps.z * exp2((static_cast<double>(ps.m) - static_cast<double>(M)) * cd);
+  }
+  const int K = min(prm.top_k, nallow);
+  // a shard list holding K keys bounds the row's K-th key by its K-th one
+  uint64_t bound = 0ull;
+  for (int g = 0; g < m.G; ++g) {
+    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    if (ps.nt >= K) {
+      const uint64_t kk = m.keys[(static_cast<int64_t>(g) * m.B + row) * kN + K - 1];
+      bound = kk > bound ? kk : bound;
+    }
+  }
+  if (tid == 0) cnt = 0;
+  __syncthreads();
+  for (int f = tid; f < m.G * kN; f += blockDim.x) {
+    const int g = f / kN, j = f - g * kN;
+    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    if (j >= ps.nt) continue;
+    const uint64_t kk = m.keys[(static_cast<int64_t>(g) * m.B + row) * kN + j];
+    if (kk >= bound) keys[atomicAdd(&cnt, 1)] = kk;  // at most G * kN keys
+  }
+  __syncthreads();
+  const int n = cnt;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const uint64_t kk = keys[i];
+    int r = 0;
+    for (int j = 0; j < n; ++j) r += keys[j] > kk ? 1 : 0;
+    if (r < K) top[r] = kk;
+  }
+  __syncthreads();
+  // exact e and the inclusive cumulative probabilities of the K keys
+  float e = 0.0f;
+  double s = 0.0;
+  if (tid < K) {
+    e = exact_e(key_val(top[tid]), M, rt);
+    s = static_cast<double>(e) / Z;
+  }
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  if (lane == 31) wsum[warp] = s;
+  __syncthreads();
+  double before = 0.0;
+  for (int w = 0; w < warp; ++w) before += wsum[w];
+  if (tid < K) {
+    cum[tid] = before + s;
+    ev[tid] = e;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // inclusive top-p cutoff (first cum >= p), then the strict draw
+    // (first cum > u * S), as the one-row finisher does
+    int cut = K - 1;
+    if (prm.top_p < 1.0f) {
+      const double pd = static_cast<double>(prm.top_p);
+      for (int j = 0; j < K; ++j)
+        if (cum[j] >= pd) {
+          cut = j;
+          break;
+        }
+    }
+    const double S = cum[cut];
+    const double tgt = static_cast<double>(m.uniforms[row]) * S;
+    int d = cut;
+    for (int j = 0; j <= cut; ++j)
+      if (cum[j] > tgt) {
+        d = j;
+        break;
+      }
+    m.out_tok[row] = static_cast<int>(key_id(top[d]));
+    if (m.out_prob) m.out_prob[row] = static_cast<float>((static_cast<double>(ev[d]) / Z) / S);
+    if (m.row_status) m.row_status[row] = 0;
+  }
+}
+
+cudaError_t launch_shard_merge(const MergeArgs& m, cudaStream_t stream) {
+  if (m.B == 0) return cudaSuccess;
+  shard_merge_kernel<<<m.B, kConsumers, 0, stream>>>(m);
+  return cudaGetLastError();
+}
+
+__global__ void fill_params_kernel(rl_row_params* p, int n, int top_k) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    rl_row_params q;
+    q.temperature = 1.0f;
+    q.top_p = 1.0f;
+    q.top_k = top_k;
+    q.repeat_penalty = 1.0f;
+    q.presence_penalty = 0.0f;
+    q.frequency_penalty = 0.0f;
+    p[i] = q;
+  }
+}
+
+cudaError_t launch_fill_params(rl_row_params* p, int n, int top_k, cudaStream_t stream) {
+  fill_params_kernel<<<(n + 255) / 256, 256, 0, stream>>>(p, n, top_k);
+  return cudaGetLastError();
 }
 
 }  // namespace rl

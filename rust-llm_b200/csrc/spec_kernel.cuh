@@ -62,6 +62,19 @@ struct Workspace {
   int max_items;      // items of a launch with more than one segment per row
 };
 
+// Per-row result of a partial launch (vocabulary shards, beam candidates):
+// the row's sorted top list goes to part_keys[row * kN ...], keys carrying
+// global ids (local id + vocab_offset).
+struct PartStats {  // layout of rl_part_stats
+  float m;       // max over allowed finite logits (-inf if none)
+  int argmax;    // lowest global id at m
+  int nallow;    // allowed finite logits
+  int flags;     // kFlagBad / kFlagTimeout
+  double z;      // sum of exp((x - m) / T) over the shard
+  int nt;        // keys written (min(top_k, nallow) on the threshold path, else 0)
+  int pad;
+};
+
 struct SpecArgs {
   const void* logits;
   int64_t ld;
@@ -82,11 +95,49 @@ struct SpecArgs {
   int32_t* list_len;
   int list_cap;
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
+  uint64_t* part_keys;   // non-null: partial launch, no draw (see PartStats)
+  PartStats* part_stats;
   int nseg;          // segments per row
   int cps;           // chunks per segment
   int nitems;        // B * nseg
   Workspace ws;
 };
+
+// Beam step: the rows' partial results combined per item.
+constexpr int kBeamMaxBeams = 16;
+constexpr int kBeamMaxCand = kBeamMaxBeams * 2 * kBeamMaxBeams;
+struct BeamArgs {
+  const uint64_t* keys;    // [items * beams * kN] partial top lists
+  const PartStats* stats;  // [items * beams]
+  int items, beams;
+  const float* scores;     // [items * beams]
+  const uint8_t* done;     // [items * beams]
+  const int32_t* lens;     // [items * beams]
+  float alpha;
+  int eos, log_softmax, n_out;
+  int32_t* out_beam;
+  int32_t* out_tok;
+  float* out_score;
+  uint8_t* out_done;
+};
+cudaError_t launch_beam_combine(const BeamArgs& b, cudaStream_t stream);
+// rows' params of a beam step: T = 1, top_p = 1, top_k, no penalties
+cudaError_t launch_fill_params(rl_row_params* p, int n, int top_k, cudaStream_t stream);
+
+// Vocabulary shards: the G partial results of each row merged and drawn.
+constexpr int kMergeMaxShards = 16;
+constexpr int kMergeMax = kMergeMaxShards * kN;
+struct MergeArgs {
+  const uint64_t* keys;    // [G, B, kN]
+  const PartStats* stats;  // [G, B]
+  int G, B;
+  const rl_row_params* params;
+  const float* uniforms;
+  int32_t* out_tok;
+  float* out_prob;
+  int32_t* row_status;
+};
+cudaError_t launch_shard_merge(const MergeArgs& m, cudaStream_t stream);
 
 int spec_smem_bytes();
 __host__ __device__ inline int spec_chunks(int V) { return (V + kCE - 1) / kCE; }

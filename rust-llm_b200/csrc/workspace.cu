@@ -31,7 +31,10 @@ rl_status alloc_workspace(rl_sampler* h) {
   ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, items) && dalloc(&h->ws.cands, items * kN) &&
        dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&
        dalloc(&h->ws.wovf, static_cast<size_t>(spec_max_ctas(h->num_sms)) * kCW * kWovf);
+  ok = ok && dalloc(&h->part_keys, B * kN) && dalloc(&h->part_stats, B) && dalloc(&h->beam_params, B) &&
+       dalloc(&h->zero_u, B);
   if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
+               cudaMemset(h->zero_u, 0, sizeof(float) * B) == cudaSuccess &&
                cudaDeviceSynchronize() == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
@@ -57,6 +60,14 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->ws.hmass);
   cudaFree(h->ws.wovf);
   h->ws = {};
+  cudaFree(h->part_keys);
+  cudaFree(h->part_stats);
+  cudaFree(h->beam_params);
+  cudaFree(h->zero_u);
+  h->part_keys = nullptr;
+  h->part_stats = nullptr;
+  h->beam_params = nullptr;
+  h->zero_u = nullptr;
   if (h->stream) cudaStreamDestroy(h->stream);
   h->stage_logits = nullptr;
   h->stream = nullptr;

@@ -29,6 +29,19 @@ RL_ERR_NONFINITE = 8
 RL_F32 = 0
 RL_BF16 = 1
 
+PART_KEYS = 128  # RL_PART_KEYS
+PART_STATS_DTYPE = np.dtype(
+    [
+        ("m", np.float32),
+        ("argmax", np.int32),
+        ("nallow", np.int32),
+        ("flags", np.int32),
+        ("z", np.float64),
+        ("n", np.int32),
+        ("pad", np.int32),
+    ]
+)
+
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "SHAPE", 3: "OOM", 4: "CUDA", 5: "NCCL",
                 6: "TIMEOUT", 7: "UNSUPPORTED", 8: "NONFINITE"}
 
@@ -94,6 +107,10 @@ def lib():
         L.rl_grammar_greedy.argtypes = [P, P, I, I, I64, P, I64, P, P]
         L.rl_beam_step.restype = I
         L.rl_beam_step.argtypes = [P, P, I, I, I, I64, P, P, P, F, I, I, I, P, P, P, P, P]
+        L.rl_sample_partial.restype = I
+        L.rl_sample_partial.argtypes = [P, P, I, I, I, I64, I, P, P, I, P, I64, P, P, P, P]
+        L.rl_sample_merge.restype = I
+        L.rl_sample_merge.argtypes = [P, I, I, P, P, P, P, P, P, P, P]
         _lib = L
     return _lib
 
@@ -189,6 +206,69 @@ class Sampler:
                                           _ptr(list_probs), _ptr(list_len), list_cap, _stream(stream)),
               "rl_sample_batch_debug")
         return out_tok, out_prob, row_status, list_ids, list_probs, list_len
+
+    # -- vocabulary shards -------------------------------------------------------
+    def sample_partial(self, logits, vocab_offset, params, hist=None, hist_len=None, mask=None, out_keys=None,
+                       out_stats=None, stream=None):
+        """One shard's partial result (rl_sample_partial): keys [B, PART_KEYS]
+        int64 (the uint64 key bits) and stats [B, 32] uint8 (rl_part_stats)."""
+        import torch
+
+        B, V = logits.shape
+        dtype = RL_BF16 if logits.dtype == torch.bfloat16 else RL_F32
+        dev = logits.device
+        if out_keys is None:
+            out_keys = torch.empty((B, PART_KEYS), dtype=torch.int64, device=dev)
+        if out_stats is None:
+            out_stats = torch.empty((B, PART_STATS_DTYPE.itemsize), dtype=torch.uint8, device=dev)
+        hs = hist.shape[1] if hist is not None else 0
+        ms = mask.shape[1] if mask is not None else 0
+        check(lib().rl_sample_partial(self.h, _ptr(logits), dtype, B, V, logits.stride(0), int(vocab_offset),
+                                      _ptr(hist), _ptr(hist_len), hs, _ptr(mask), ms, _ptr(params),
+                                      _ptr(out_keys), _ptr(out_stats), _stream(stream)),
+              "rl_sample_partial")
+        return out_keys, out_stats
+
+    def sample_merge(self, keys, stats, params, uniforms, out_tok=None, out_prob=None, row_status=None,
+                     stream=None):
+        """rl_sample_merge over keys [G, B, PART_KEYS] and stats [G, B, 32]."""
+        import torch
+
+        G, B = keys.shape[0], keys.shape[1]
+        dev = keys.device
+        if out_tok is None:
+            out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+        if out_prob is None:
+            out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        if row_status is None:
+            row_status = torch.empty(B, dtype=torch.int32, device=dev)
+        check(lib().rl_sample_merge(self.h, G, B, _ptr(keys.contiguous()), _ptr(stats.contiguous()), _ptr(params),
+                                    _ptr(uniforms), _ptr(out_tok), _ptr(out_prob), _ptr(row_status),
+                                    _stream(stream)),
+              "rl_sample_merge")
+        return out_tok, out_prob, row_status
+
+    # -- beam search ----------------------------------------------------------------
+    def beam_step(self, logits, items, beams, scores, done, lens=None, alpha=1.0, eos=2, log_softmax=1,
+                  n_out=None, stream=None):
+        """One BeamSearch::search step for items x beams rows of f32 logits
+        (row = item * beams + beam). Returns (beam, tok, score, done), each
+        [items, n_out]."""
+        import torch
+
+        R, V = logits.shape
+        assert R == items * beams
+        n_out = 2 * beams if n_out is None else n_out
+        dev = logits.device
+        ob = torch.empty((items, n_out), dtype=torch.int32, device=dev)
+        ot = torch.empty((items, n_out), dtype=torch.int32, device=dev)
+        osc = torch.empty((items, n_out), dtype=torch.float32, device=dev)
+        od = torch.empty((items, n_out), dtype=torch.uint8, device=dev)
+        check(lib().rl_beam_step(self.h, _ptr(logits), items, beams, V, logits.stride(0), _ptr(scores), _ptr(done),
+                                 _ptr(lens), float(alpha), int(eos), int(log_softmax), n_out, _ptr(ob), _ptr(ot),
+                                 _ptr(osc), _ptr(od), _stream(stream)),
+              "rl_beam_step")
+        return ob, ot, osc, od
 
     def sample_host(self, logits, params, uniforms, hist=None, hist_len=None, mask=None):
         """Host numpy buffers in and out (synchronous)."""

@@ -110,6 +110,31 @@ def config3(step, B=64, V=32000):
     return SampleBatch(x, p, uniforms(3, step, B), None, None, mask)
 
 
+@dataclass
+class BeamBatch:
+    logits: np.ndarray  # [items * beams, V] float32, row = item * beams + beam
+    items: int
+    beams: int
+    scores: np.ndarray  # [items * beams] float32 cumulative beam scores
+    done: np.ndarray    # [items * beams] uint8
+    lens: np.ndarray    # [items * beams] int32
+    alpha: float = 1.0
+    eos: int = 2
+
+
+def config4(step, items=16, beams=8, V=151936, done_frac=0.0):
+    """Beam-search step: logits ~ N(0, 3^2), scores ~ U[-20, 0], length
+    penalty 1.0, EOS id 2. `done_frac` marks a share of the beams complete
+    (the benchmark configuration has none)."""
+    r = _rng(4, step)
+    R = items * beams
+    x = r.normal(0.0, 3.0, (R, V)).astype(np.float32)
+    scores = r.uniform(-20.0, 0.0, R).astype(np.float32)
+    done = (r.random(R) < done_frac).astype(np.uint8)
+    lens = r.integers(1, 64, R).astype(np.int32)
+    return BeamBatch(x, items, beams, scores, done, lens)
+
+
 def config5_rows(step, B=1024, V=256000, rows=None):
     r = _rng(5, step)
     hist = r.integers(0, V, (B, 256)).astype(np.int32)
