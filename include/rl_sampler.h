@@ -147,7 +147,11 @@ rl_status rl_sample_batch_static(const void* logits, rl_dtype dtype, int B, int 
  * Decoder::sample (decoder.rs:31-33) is temperature = 1, top_p = 0.9.
  *  temperature[B], top_p[B], uniforms[B]: device arrays.
  *  out_prob[B]: the returned id's entry of the final probability array (nullable).
- * V must be <= 53248 (the row is held in one CTA's shared memory).
+ * Every sum is the reference's left-to-right f32 accumulation, reproduced bit
+ * for bit; exp is the correctly rounded f32 exponential. A row holding NaN or
+ * +-inf gets token -1 and probability 0 (the reference's result there depends
+ * on NaN ordering). V must be <= 53248 (the row is held in one CTA's shared
+ * memory) and <= the handle's max_vocab; B <= max_batch.
  */
 rl_status rl_decoder_sample(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
                             const float* temperature, const float* top_p, const float* uniforms,
