@@ -2037,6 +2037,30 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
   cbar();
 }
 
+// A warp's candidate buffer brought back to (about) nkeep keys: a bound from
+// the top 16 value bits (two radix passes) keeps nkeep keys and the rest of
+// their bucket; exact only when that is too many. Returns the new bound,
+// shared through tau_shared.
+__device__ __noinline__ uint64_t compact_warp_buf(uint64_t* wbuf, const uint64_t* gov, int* wcnt, int nkeep,
+                                                  uint32_t* bins_w, int* wc, unsigned long long* tau_shared) {
+  const int lane = threadIdx.x & 31;
+  const int n = *wcnt;
+  uint64_t tau = warp_select(wbuf, gov, n, nkeep, bins_w, 48);
+  int kept = warp_count_ge(wbuf, gov, n, tau);
+  if (kept > kWcompact - 64) {
+    tau = warp_select(wbuf, gov, n, nkeep, bins_w);
+    kept = nkeep;
+  }
+  warp_keep_ge(wbuf, gov, n, tau);
+  *wcnt = kept;
+  if (lane == 0) {
+    *wc = kept;
+    atomicMax(tau_shared, static_cast<unsigned long long>(tau));
+  }
+  __syncwarp();
+  return tau;
+}
+
 // ---------------------------------------------------------------------------
 // Consumer warps
 // ---------------------------------------------------------------------------
@@ -2086,6 +2110,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       sm.hcnt[i] = 0u;
     }
   if (tid == 0) sm.ctl->tau_shared = 0ull;
+  if (lane == 0) sm.wcnt[warp] = 0;
   cbar();
   bool pre_patched = false;
   if constexpr (MODE != 0 && es == 4) {
@@ -2126,21 +2151,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   }
 
   for (int c = mt.c0; c < mt.c1; ++c, ++cseq) {
-    if (wcnt > kWcompact) {
-      // room for a whole slice of appends (the only call in the loop; no
-      // logits are live here)
-      // a bound from the top 16 value bits (two radix passes) keeps nkeep
-      // keys and the rest of their bucket; exact only when that is too many
-      tau = warp_select(wbuf, gov, wcnt, nkeep, bins_w, 48);
-      int kept = warp_count_ge(wbuf, gov, wcnt, tau);
-      if (kept > kWcompact - 64) {
-        tau = warp_select(wbuf, gov, wcnt, nkeep, bins_w);
-        kept = nkeep;
-      }
-      warp_keep_ge(wbuf, gov, wcnt, tau);
-      wcnt = kept;
+    if (MODE != 0 && wcnt > kWcompact) {
+      // room for a whole slice of appends (no logits are live here)
+      tau = compact_warp_buf(wbuf, gov, &wcnt, nkeep, bins_w, sm.wcnt + warp, &sm.ctl->tau_shared);
       tau_v = key_val(tau);
-      if (lane == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
     }
     const int s = cseq % kNS;
     const uint32_t ph = static_cast<uint32_t>((cseq / kNS) & 1);
@@ -2256,17 +2270,27 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
           lm = fmaxf(lm, x);
         }
     } else {
-      float fin = 0.0f;
+      // trees (depth 4) rather than 16-long dependent chains; the sum is
+      // finite exactly when every logit is (or a huge finite sum overflows,
+      // which the exact check below sorts out)
+      float mx[8], sx[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int j = 0; j < 8; ++j) {
+        mx[j] = fmaxf(v[j >> 1][(j & 1) * 2], v[j >> 1][(j & 1) * 2 + 1]);
+        sx[j] = v[j >> 1][(j & 1) * 2] + v[j >> 1][(j & 1) * 2 + 1];
+      }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          lm = fmaxf(lm, v[q][k]);
-          fin = __fmaf_rn(v[q][k], 0.0f, fin);
+      for (int w2 = 4; w2 > 0; w2 >>= 1)
+#pragma unroll
+        for (int j = 0; j < w2; ++j) {
+          mx[j] = fmaxf(mx[j], mx[j + w2]);
+          sx[j] = sx[j] + sx[j + w2];
         }
-      if (fin == 0.0f) {
+      lm = mx[0];
+      if (fabsf(sx[0]) < RL_POS_INF) {
         nal += 16;
       } else {
+        lm = RL_NEG_INF;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
@@ -2279,17 +2303,19 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
             }
             if (x != x) x = RL_NEG_INF;
             v[q][k] = x;
+            lm = fmaxf(lm, x);
           }
       }
     }
     if (mode == 0) {
-      int la = INT_MAX;
-#pragma unroll
-      for (int q = 3; q >= 0; --q)
-#pragma unroll
-        for (int k = 3; k >= 0; --k)
-          if (v[q][k] == lm) la = start + base + (q * 32 + lane) * 4 + k;
+      // a strictly larger maximum moves the lane's argmax (lowest id of it)
       if (lm > m_run) {
+        int la = INT_MAX;
+#pragma unroll
+        for (int q = 3; q >= 0; --q)
+#pragma unroll
+          for (int k = 3; k >= 0; --k)
+            if (v[q][k] == lm) la = start + base + (q * 32 + lane) * 4 + k;
         m_run = lm;
         arg_run = la;
       }
@@ -2304,11 +2330,12 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         zs *= ex2_approx((zref - lm) * rt.c);
         zref = lm;
       }
+      const float zc = zref * rt.c;
       float z4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int q = 0; q < 4; ++q)
 #pragma unroll
-        for (int k = 0; k < 4; ++k) z4[k] += ex2_approx((v[q][k] - zref) * rt.c);
+        for (int k = 0; k < 4; ++k) z4[k] += ex2_approx(fmaf(v[q][k], rt.c, -zc));
       zs += (z4[0] + z4[1]) + (z4[2] + z4[3]);
     }
     // ---- candidates ----
@@ -2319,33 +2346,26 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         tau_v = key_val(ts);
       }
       if (__any_sync(0xffffffffu, lm > RL_NEG_INF && lm >= tau_v)) {
-        // slots where some lane may take a logit
-        unsigned m16 = 0u;
+        // every slot statically indexed (no register-array indexing); the
+        // takers reserve buffer places with a per-warp shared counter
+        int* wc = sm.wcnt + warp;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            m16 |= (v[q][k] > RL_NEG_INF && v[q][k] >= tau_v) ? (1u << (q * 4 + k)) : 0u;
-        unsigned wm = m16;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) wm |= __shfl_xor_sync(0xffffffffu, wm, o);
-        // a compact (not unrolled) loop over the slots where some lane takes
-#pragma unroll 1
-        while (wm) {
-          const int sl = __ffs(wm) - 1;
-          wm &= wm - 1u;
-          const float x = pick16(v, sl);
-          const uint32_t id = static_cast<uint32_t>(start + base + ((sl >> 2) * 32 + lane) * 4 + (sl & 3));
-          const bool take = ((m16 >> sl) & 1u) && (x > tau_v || cand_key(x, id) >= tau);
-          const unsigned bal = __ballot_sync(0xffffffffu, take);
-          if (take) {
-            const int idx = wcnt + __popc(bal & ((1u << lane) - 1u));
-            const uint64_t key = cand_key(x, id);
-            if (idx < kWcap) wbuf[idx] = key;
-            else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
+          for (int k = 0; k < 4; ++k) {
+            const float x = v[q][k];
+            if (x > RL_NEG_INF && x >= tau_v) {
+              const uint32_t id = static_cast<uint32_t>(start + base + (q * 32 + lane) * 4 + k);
+              const uint64_t key = cand_key(x, id);
+              if (x > tau_v || key >= tau) {
+                const int idx = atomicAdd(wc, 1);
+                if (idx < kWcap) wbuf[idx] = key;
+                else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
+              }
+            }
           }
-          wcnt += __popc(bal);
-        }
+        __syncwarp();
+        wcnt = *reinterpret_cast<volatile int*>(wc);
       }
     }
     // ---- windowed histogram ----
@@ -2365,58 +2385,23 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         }
       }
       if (atop != kNoAnchor && __any_sync(0xffffffffu, lm >= x_lo)) {
-        // the warp's logits that may fall in the window, compacted into its
-        // 256-float scratch (batches), then binned one per lane
-        float* scr = reinterpret_cast<float*>(bins_w);
-        unsigned hm = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
-          for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= x_lo) ? (1u << (q * 4 + k)) : 0u;
-#pragma unroll 1
-        while (__any_sync(0xffffffffu, hm != 0u)) {
-          // this lane's share of the batch: its lowest set slots, up to 8
-          unsigned take = hm;
-          int mine = __popc(take);
-          if (mine > 8) {
-            take = 0u;
-            unsigned t = hm;
-            for (int j = 0; j < 8; ++j) {
-              take |= t & (0u - t);
-              t &= t - 1u;
-            }
-            mine = 8;
-          }
-          hm &= ~take;
-          int inc = mine;
-#pragma unroll
-          for (int o = 1; o < 32; o <<= 1) {
-            const int t = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += t;
-          }
-          const int total = __shfl_sync(0xffffffffu, inc, 31);
-          int off = inc - mine;
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if ((take >> (q * 4 + k)) & 1u) scr[off++] = v[q][k];
-          __syncwarp();
-#pragma unroll 1
-          for (int i = lane; i < total; i += 32) {
-            const float x = scr[i];
-            const float af = bin_of(x, rt);
-            const float rf = atop_f - af;
-            if (rf >= 0.0f && rf <= wb_f) {
-              const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
-              const int r = static_cast<int>(rf);
-              atomicAdd(&sm.hmass[r], qm);
-              if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
-              qs += qm;
+          for (int k = 0; k < 4; ++k) {
+            const float x = v[q][k];
+            if (x >= x_lo) {
+              const float af = bin_of(x, rt);
+              const float rf = atop_f - af;
+              if (rf >= 0.0f && rf <= wb_f) {
+                const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
+                const int r = static_cast<int>(rf);
+                atomicAdd(&sm.hmass[r], qm);
+                if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
+                qs += qm;
+              }
             }
           }
-          __syncwarp();
-        }
       }
     }
   }
