@@ -116,6 +116,7 @@ struct Ctl {
   int sel_bucket;
   uint32_t sel_above, sel_cnt;
   int res_i, res_j;
+  float cx_lo, cx_hi;  // value interval of the bin being collected
 };
 
 struct Red {
@@ -1018,11 +1019,85 @@ __device__ __noinline__ void sort_table(uint32_t* tab, int n) {
   cbar();
 }
 
+// The metadata of an item and the raw (unsorted) history table of its row,
+// written by one warp. want_tab false: the table is built only for rows on
+// the histogram path (the only ones that re-read the row).
+__device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& mt, uint32_t* tab, bool want_tab) {
+  const int lane = threadIdx.x & 31;
+  const int S = spec_chunks(a.V);
+  const int row = item / a.nseg;
+  const int seg = item - row * a.nseg;
+  // every global read of the row issued up front
+  const rl_row_params prm = a.params[row];
+  const float u = a.uniforms[row];
+  const int hl_raw = a.hist ? a.hist_len[row] : 0;
+  const float T = prm.temperature;
+  int mode;
+  if (!(fabsf(T) < RL_POS_INF) || !(T > 0.0f)) mode = 0;  // greedy; a non-finite T is reported at the end
+  else if (prm.top_k > 0 && prm.top_k <= kN) mode = 1;
+  else mode = 2;
+  // allowed-mask flag: an empty allowed set means every id is allowed
+  int mask_on = 0;
+  if (a.mask) {
+    const uint32_t* mrow = a.mask + static_cast<int64_t>(row) * a.mask_stride;
+    const int nw = (a.V + 31) >> 5;
+    uint32_t any = 0u;
+    for (int w = lane; w < nw; w += 32) {
+      uint32_t bits = __ldg(mrow + w);
+      const int rem = a.V - w * 32;
+      if (rem < 32) bits &= (1u << rem) - 1u;
+      any |= bits;
+    }
+    mask_on = __any_sync(0xffffffffu, any != 0u) ? 1 : 0;
+  }
+  // history table (only when the penalties are not the identity)
+  const bool pen = !(prm.repeat_penalty == 1.0f && prm.frequency_penalty == 0.0f && prm.presence_penalty == 0.0f);
+  int ntab = 0;
+  if (a.hist && pen && (want_tab || mode == 2)) {
+    const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
+    if (hl > 0) ntab = gather_history(a, row, hl, tab);
+  }
+  // Histogram window depth W (nats below the anchor): the mass below it is
+  // at most V e^-W of the row max, kept under a quarter of the tail mass
+  // that the top-p cutoff leaves (or, without a cutoff, that the draw
+  // leaves). A draw that still lands below the window is resolved by the
+  // exact radix walk.
+  int wbins = kNB - 1;
+  if (mode == 2 && prm.top_k <= 0) {
+    const double p = static_cast<double>(prm.top_p);
+    const double tail = (p < 1.0) ? 1.0 - p : 1.0 - static_cast<double>(u);
+    if (tail > 0.0 && p > 0.0) {
+      const double W = log(4.0 * static_cast<double>(a.V) / tail) + 1.0;
+      wbins = min(wbins, kHead + max(64, static_cast<int>(ceil(W * kRbin))));
+    }
+  }
+  if (lane == 0) {
+    mt.item = item;
+    mt.row = row;
+    mt.seg = seg;
+    mt.c0 = seg * a.cps;
+    mt.c1 = min(S, mt.c0 + a.cps);
+    mt.mode = mode;
+    mt.nkeep = mode == 1 ? prm.top_k : kN;
+    mt.need_count = (mode == 2 && prm.top_k > 0) ? 1 : 0;
+    mt.mask_on = mask_on;
+    mt.ntab = ntab;
+    mt.wbins = wbins;
+    mt.top_k = prm.top_k;
+    mt.top_p = prm.top_p;
+    mt.u = u;
+    mt.rp = prm.repeat_penalty;
+    mt.pres = prm.presence_penalty;
+    mt.freq = prm.frequency_penalty;
+    mt.rt = make_rowt(mode == 0 ? 1.0f : T);
+    mt.rt.T = T;  // the raw temperature (greedy rows check it at the end)
+  }
+}
+
 template <typename E>
 __device__ __noinline__ void meta_loop(const SpecArgs& a) {
   const Smem sm = smem_map();
   const int lane = threadIdx.x & 31;
-  const int S = spec_chunks(a.V);
   int mseq = 0;
   for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
     const int slot = mseq & 1;
@@ -1031,75 +1106,7 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
       if (lane == 0) atomicExch(&sm.ctl->abort, 1);
       return;
     }
-    ItemMeta& mt = sm.meta[slot];
-    uint32_t* tab = sm.tab + slot * kHmax;
-    const int row = item / a.nseg;
-    const int seg = item - row * a.nseg;
-    // every global read of the row issued up front
-    const rl_row_params prm = a.params[row];
-    const float u = a.uniforms[row];
-    const int hl_raw = a.hist ? a.hist_len[row] : 0;
-    const float T = prm.temperature;
-    int mode;
-    if (!(fabsf(T) < RL_POS_INF) || !(T > 0.0f)) mode = 0;  // greedy; a non-finite T is reported at the end
-    else if (prm.top_k > 0 && prm.top_k <= kN) mode = 1;
-    else mode = 2;
-    // allowed-mask flag: an empty allowed set means every id is allowed
-    int mask_on = 0;
-    if (a.mask) {
-      const uint32_t* mrow = a.mask + static_cast<int64_t>(row) * a.mask_stride;
-      const int nw = (a.V + 31) >> 5;
-      uint32_t any = 0u;
-      for (int w = lane; w < nw; w += 32) {
-        uint32_t bits = __ldg(mrow + w);
-        const int rem = a.V - w * 32;
-        if (rem < 32) bits &= (1u << rem) - 1u;
-        any |= bits;
-      }
-      mask_on = __any_sync(0xffffffffu, any != 0u) ? 1 : 0;
-    }
-    // history table (only when the penalties are not the identity)
-    const bool pen = !(prm.repeat_penalty == 1.0f && prm.frequency_penalty == 0.0f && prm.presence_penalty == 0.0f);
-    int ntab = 0;
-    if (a.hist && pen) {
-      const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
-      if (hl > 0) ntab = gather_history(a, row, hl, tab);
-    }
-    // Histogram window depth W (nats below the anchor): the mass below it is
-    // at most V e^-W of the row max, kept under a quarter of the tail mass
-    // that the top-p cutoff leaves (or, without a cutoff, that the draw
-    // leaves). A draw that still lands below the window is resolved by the
-    // exact radix walk.
-    int wbins = kNB - 1;
-    if (mode == 2 && prm.top_k <= 0) {
-      const double p = static_cast<double>(prm.top_p);
-      const double tail = (p < 1.0) ? 1.0 - p : 1.0 - static_cast<double>(u);
-      if (tail > 0.0 && p > 0.0) {
-        const double W = log(4.0 * static_cast<double>(a.V) / tail) + 1.0;
-        wbins = min(wbins, kHead + max(64, static_cast<int>(ceil(W * kRbin))));
-      }
-    }
-    if (lane == 0) {
-      mt.item = item;
-      mt.row = row;
-      mt.seg = seg;
-      mt.c0 = seg * a.cps;
-      mt.c1 = min(S, mt.c0 + a.cps);
-      mt.mode = mode;
-      mt.nkeep = mode == 1 ? prm.top_k : kN;
-      mt.need_count = (mode == 2 && prm.top_k > 0) ? 1 : 0;
-      mt.mask_on = mask_on;
-      mt.ntab = ntab;
-      mt.wbins = wbins;
-      mt.top_k = prm.top_k;
-      mt.top_p = prm.top_p;
-      mt.u = u;
-      mt.rp = prm.repeat_penalty;
-      mt.pres = prm.presence_penalty;
-      mt.freq = prm.frequency_penalty;
-      mt.rt = make_rowt(mode == 0 ? 1.0f : T);
-      mt.rt.T = T;  // the raw temperature (greedy rows check it at the end)
-    }
+    build_meta(a, item, sm.meta[slot], sm.tab + slot * kHmax, true);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.mfull[slot]);
   }
@@ -1269,20 +1276,120 @@ __device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status
   if (a.row_status) a.row_status[row] = status;
 }
 
+// Whether the sorted history table holds `id` (entries (id << 11) | count).
+__device__ __forceinline__ bool tab_has(const uint32_t* tab, int ntab, int id) {
+  int lo = 0, hi = ntab;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (static_cast<int>(tab[mid] >> 11) < id) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo < ntab && static_cast<int>(tab[lo] >> 11) == id;
+}
+
+// The smallest float x with bin_of(x) >= A (bin_of is non-decreasing in x
+// for T > 0): a guess within a few ulps, then single-ulp steps (bounded).
+__device__ float bin_floor_x(float A, const RowT& rt) {
+  float g = __fdiv_rn(A, rt.cb_hi);
+  for (int it = 0; it < 4096 && bin_of(g, rt) >= A; ++it) g = nextafterf(g, RL_NEG_INF);
+  for (int it = 0; it < 4096 && bin_of(g, rt) < A; ++it) g = nextafterf(g, RL_POS_INF);
+  return g;
+}
+
 // Keys of the allowed logits of absolute bin A, gathered from a re-read of
-// the row into buf; returns the count (> kCollect: too many).
-template <typename E>
+// the row into buf; returns the count (> kCollect: too many). The stream
+// compares raw logits against the bin's value interval and leaves out the
+// history ids, which are then tested with their penalised values.
+template <typename E, bool SPLIT>
 __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, uint64_t* buf,
                            Ctl* ctl) {
-  if (threadIdx.x == 0) ctl->cnt = 0;
-  cbar();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowT rt = mt.rt;
-  stream_row<E>(a, mt, tab, [&](float x, int id) {
-    if (bin_of(x, rt) == A) {
+  if (tid == 0) {
+    ctl->cnt = 0;
+    ctl->cx_lo = bin_floor_x(A, rt);
+    ctl->cx_hi = bin_floor_x(A + 1.0f, rt);
+  }
+  cbar();
+  const float xlo = ctl->cx_lo;
+  const float xhi = ctl->cx_hi;
+  if constexpr (!SPLIT) {
+    // inside the streaming kernel: the penalised stream (few registers)
+    stream_row<E>(a, mt, tab, [&](float x, int id) {
+      if (x >= xlo && x < xhi) {
+        const int i = atomicAdd(&ctl->cnt, 1);
+        if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+      }
+    });
+    cbar();
+    const int n0 = ctl->cnt;
+    cbar();
+    return n0;
+  }
+  const int ntab = mt.ntab;
+  const int V = a.V;
+  const int S = spec_chunks(V);
+  const int base = warp * kSlice;
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
+  const uint32_t* mrow = mt.mask_on ? a.mask + static_cast<int64_t>(mt.row) * a.mask_stride : nullptr;
+  float n1[4][4], n2[4][4], n3[4][4];
+  load_slice_raw<E>(rowp, V, 0, base, n1);
+  if (S > 1) load_slice_raw<E>(rowp, V, kCE, base, n2);
+  if (S > 2) load_slice_raw<E>(rowp, V, 2 * kCE, base, n3);
+#pragma unroll 1
+  for (int c = 0; c < S; ++c) {
+    float v[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[q][k] = n1[q][k];
+        n1[q][k] = n2[q][k];
+        n2[q][k] = n3[q][k];
+      }
+    if (c + 3 < S) load_slice_raw<E>(rowp, V, (c + 3) * kCE, base, n3);
+    const int start = c * kCE;
+    bool hit = false;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) hit |= v[q][k] >= xlo && v[q][k] < xhi;
+    if (!__any_sync(0xffffffffu, hit)) continue;
+    const int len = min(kCE, V - start);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e0 = base + (q * 32 + lane) * 4;
+      uint32_t bits = 15u;
+      if (mrow) {
+        const uint32_t word = e0 < len ? __ldcg(mrow + ((start + e0) >> 5)) : 0u;
+        bits = (word >> ((start + e0) & 31)) & 15u;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float x = v[q][k];
+        const int id = start + e0 + k;
+        if (x >= xlo && x < xhi && ((bits >> k) & 1u) && !(ntab > 0 && tab_has(tab, ntab, id))) {
+          const int i = atomicAdd(&ctl->cnt, 1);
+          if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+        }
+      }
+    }
+  }
+  // history ids: their penalised values
+  for (int j = tid; j < ntab; j += kConsumers) {
+    const uint32_t ent = tab[j];
+    const int cnt = static_cast<int>(ent & 2047u);
+    const int id = static_cast<int>(ent >> 11);
+    if (cnt == 0 || id >= V) continue;
+    if (mrow && !((__ldcg(mrow + (id >> 5)) >> (id & 31)) & 1u)) continue;
+    const float raw = to_f32<E>(rowp[id]);
+    if (raw != raw) continue;
+    const float x = pen_value(raw, cnt, mt.rp, mt.freq, mt.pres);
+    if (x >= xlo && x < xhi) {
       const int i = atomicAdd(&ctl->cnt, 1);
       if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
     }
-  });
+  }
   cbar();
   const int n = ctl->cnt;
   cbar();
@@ -1429,7 +1536,7 @@ __device__ __forceinline__ void write_part(const SpecArgs& a, int row, float M, 
 // The finisher of a row (consumer threads). On entry sm.sums[0..nseg) hold
 // the segment summaries; for a one-segment row sm.top holds the sorted list
 // and the histogram is in shared memory.
-template <typename E>
+template <typename E, bool SPLIT>
 __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, int first_item) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x;
@@ -1699,7 +1806,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         if (f == INT_MAX) break;
         const double mb = base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
         const long long cb = base_c + ccorr + (f > 0 ? static_cast<long long>(cc[f - 1]) : 0);
-        nheld = collect_bin<E>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
+        nheld = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
         if (nheld > kCollect) break;
         csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
         held = f;
@@ -1750,7 +1857,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             if (cut_pos >= 0 && (f == INT_MAX || f > i_c)) f = i_c;
             if (f == INT_MAX) break;
             if (held != f) {
-              nheld = collect_bin<E>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
+              nheld = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
               if (nheld > kCollect) break;
               csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
               held = f;
@@ -1833,7 +1940,7 @@ struct ItemAcc {
 
 // End of an item (consumer threads): the item's summary and top list, then
 // the row's finisher when this CTA is the last of the row to arrive.
-template <typename E>
+template <typename E, bool SPLIT>
 __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, ItemAcc acc) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1985,6 +2092,24 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
   is.pad = 0;
   is.qsum = qs;
   const int first_item = row * a.nseg;
+  if constexpr (SPLIT) {
+    // the finish kernel merges the row's items: every item goes to the
+    // workspace
+    if (tid == 0) a.ws.sums[item] = is;
+    uint64_t* gc = a.ws.cands + static_cast<int64_t>(item) * kN;
+    for (int i = tid; i < ncand; i += kConsumers) gc[i] = sm.top[i];
+    if (mode == 2) {
+      uint32_t* gm = a.ws.hmass + static_cast<int64_t>(item) * kNB;
+      uint32_t* gk = a.ws.hcnt + static_cast<int64_t>(item) * kNB;
+      for (int i = tid; i < kNB; i += kConsumers) {
+        gm[i] = sm.hmass[i];
+        if (mt.need_count) gk[i] = sm.hcnt[i];
+      }
+    }
+    (void)first_item;
+    cbar();
+    return;
+  }
   bool run_finisher;
   if (a.nseg == 1) {
     if (tid == 0) sm.sums[0] = is;
@@ -2031,7 +2156,7 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
     }
   }
   if (run_finisher) {
-    finish_row<E>(a, mt, tab, first_item);
+    finish_row<E, false>(a, mt, tab, first_item);
     if (a.nseg > 1 && tid == 0) a.ws.row_done[row] = 0;  // ready for the next launch
   }
   cbar();
@@ -2422,7 +2547,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   return acc;
 }
 
-template <typename E>
+template <typename E, bool SPLIT>
 __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x;
@@ -2433,9 +2558,19 @@ __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
     if (cor_i(timeout || *reinterpret_cast<volatile int*>(&sm.ctl->abort), sm.red)) {
       if (tid == 0) {
         atomicExch(&sm.ctl->abort, 1);
-        // rows of this CTA that will not be finished
-        for (int it = item; it < a.nitems; it += gridDim.x)
-          if ((it % a.nseg) == 0) write_row(a, it / a.nseg, RL_ERR_TIMEOUT, -1, 0.0f);
+        // items of this CTA that will not be streamed
+        for (int it = item; it < a.nitems; it += gridDim.x) {
+          if constexpr (SPLIT) {
+            ItemSum t = {};
+            t.m = RL_NEG_INF;
+            t.argmax = INT_MAX;
+            t.flags = kFlagTimeout;
+            t.atop = kNoAnchor;
+            a.ws.sums[it] = t;
+          } else if ((it % a.nseg) == 0) {
+            write_row(a, it / a.nseg, RL_ERR_TIMEOUT, -1, 0.0f);
+          }
+        }
       }
       return;
     }
@@ -2446,7 +2581,7 @@ __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
     else if (mode == 1) acc = run_item<E, 1>(a, slot, cseq);
     else acc = run_item<E, 2>(a, slot, cseq);
     cseq = acc.cseq;
-    item_end<E>(a, item, slot, acc);
+    item_end<E, SPLIT>(a, item, slot, acc);
     // the row data of this slot may be rebuilt
     if ((tid & 31) == 0) mbar_arrive(&sm.mempty[slot]);
   }
@@ -2455,7 +2590,7 @@ __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <typename E>
+template <typename E, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_constant__ SpecArgs a) {
   const Smem sm = smem_map();
   if (threadIdx.x == 0) {
@@ -2474,7 +2609,53 @@ __global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_con
   const int warp = threadIdx.x >> 5;
   if (warp == kProdWarp) producer_loop<E>(a);
   else if (warp == kMetaWarp) meta_loop<E>(a);
-  else consumer_loop<E>(a);
+  else consumer_loop<E, SPLIT>(a);
+}
+
+// The finish kernel: one CTA of kConsumers threads per row merges the row's
+// item summaries, top lists and histograms written by the streaming kernel
+// and draws the token (the same finisher the single-kernel path runs inline).
+template <typename E>
+__global__ void __launch_bounds__(kConsumers, 2) spec_finish_kernel(const __grid_constant__ SpecArgs a) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  const int row = blockIdx.x;
+  const int first_item = row * a.nseg;
+  if (tid < 32) build_meta(a, first_item, sm.meta[0], sm.tab, false);
+  for (int s2 = tid; s2 < a.nseg; s2 += kConsumers) {
+    const ItemSum* src = a.ws.sums + first_item + s2;
+    ItemSum t;
+    t.m = __ldcg(&src->m);
+    t.argmax = __ldcg(&src->argmax);
+    t.nallow = __ldcg(&src->nallow);
+    t.flags = __ldcg(&src->flags);
+    t.z = __ldcg(&src->z);
+    t.ncand = __ldcg(&src->ncand);
+    t.atop = __ldcg(&src->atop);
+    t.wlo = __ldcg(&src->wlo);
+    t.pad = 0;
+    t.qsum = __ldcg(&src->qsum);
+    sm.sums[s2] = t;
+  }
+  __syncthreads();
+  const ItemMeta& mt = sm.meta[0];
+  if (mt.ntab > 0) sort_table(sm.tab, mt.ntab);
+  if (a.nseg == 1) {
+    // a one-segment row: its list and histogram where the finisher expects
+    // them (shared memory)
+    const int nc = sm.sums[0].ncand;
+    for (int i = tid; i < nc; i += kConsumers) sm.top[i] = __ldcg(a.ws.cands + static_cast<int64_t>(first_item) * kN + i);
+    if (mt.mode == 2) {
+      const uint32_t* gm = a.ws.hmass + static_cast<int64_t>(first_item) * kNB;
+      const uint32_t* gk = a.ws.hcnt + static_cast<int64_t>(first_item) * kNB;
+      for (int i = tid; i < kNB; i += kConsumers) {
+        sm.hmass[i] = __ldcg(gm + i);
+        sm.hcnt[i] = mt.need_count ? __ldcg(gk + i) : 0u;
+      }
+    }
+  }
+  __syncthreads();
+  finish_row<E, true>(a, mt, sm.tab, first_item);
 }
 
 // ---------------------------------------------------------------------------
@@ -2494,18 +2675,25 @@ void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas) {
 
 int spec_max_ws_items(int num_sms) { return 2 * (2 * num_sms); }
 
-template <typename E>
+template <typename E, bool SPLIT>
 static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t stream) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(spec_pipe_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        cudaFuncSetAttribute(spec_pipe_kernel<E, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e == cudaSuccess && SPLIT)
+      e = cudaFuncSetAttribute(spec_finish_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, kOffStage);
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev] = 1;
   }
-  spec_pipe_kernel<E><<<nctas, kThreads, kSmemBytes, stream>>>(a);
+  spec_pipe_kernel<E, SPLIT><<<nctas, kThreads, kSmemBytes, stream>>>(a);
+  if (SPLIT) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    spec_finish_kernel<E><<<a.B, kConsumers, kOffStage, stream>>>(a);
+  }
   return cudaGetLastError();
 }
 
@@ -2515,8 +2703,8 @@ cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream
   int nctas = 0;
   spec_plan(a.B, a.V, num_sms, &a.nseg, &a.cps, &nctas);
   a.nitems = a.B * a.nseg;
-  if (a.nseg > 1 && a.nitems > a.ws.max_items) return cudaErrorInvalidValue;
-  return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
+  if (a.nitems > a.ws.max_items) return cudaErrorInvalidValue;
+  return dtype == RL_BF16 ? launch_typed<uint16_t, true>(a, nctas, stream) : launch_typed<float, true>(a, nctas, stream);
 }
 
 cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream) {
@@ -2526,7 +2714,8 @@ cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int
   a.cps = spec_chunks(a.V);
   a.nitems = a.B;
   const int nctas = max(1, min(min(a.B, 2 * num_sms), max_ctas));
-  return dtype == RL_BF16 ? launch_typed<uint16_t>(a, nctas, stream) : launch_typed<float>(a, nctas, stream);
+  return dtype == RL_BF16 ? launch_typed<uint16_t, false>(a, nctas, stream)
+                          : launch_typed<float, false>(a, nctas, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -24,9 +24,9 @@ rl_status alloc_workspace(rl_sampler* h) {
             dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
             dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
   // spec kernel workspace: per-item summaries, candidate lists and
-  // histograms of launches that split rows into segments (at most
-  // spec_max_ws_items items; one-segment rows stay in shared memory)
-  const size_t items = static_cast<size_t>(spec_max_ws_items(h->num_sms));
+  // histograms that the streaming kernel hands to the finish kernel (one
+  // item per row, or up to spec_max_ws_items segments of small batches)
+  const size_t items = static_cast<size_t>(max(spec_max_ws_items(h->num_sms), h->max_batch));
   h->ws.max_items = static_cast<int>(items);
   ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, items) && dalloc(&h->ws.cands, items * kN) &&
        dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&
