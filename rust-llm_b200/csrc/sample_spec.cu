@@ -149,6 +149,7 @@ constexpr int kSmemBytes = kOffStage + kNS * kStageBytes;
 static_assert(kOffRadix + kCW * 256 * 4 - kOffHist >= kCollect * 8, "collect buffer");
 static_assert(kCW * kWcap * 8 >= 2 * kNB * 8, "merged histogram");
 static_assert(256 * (4 + 8 + 8) <= kCW * 256 * 4, "radix walk bins");
+static_assert(kCW * kWcap >= 2 * kNB + 8 * kConsumers && kCollect <= 8 * kConsumers, "sort scratch");
 static_assert(sizeof(ItemMeta) <= 128 && sizeof(Ctl) <= 128 && sizeof(Red) <= 256, "smem header");
 static_assert(kOffMeta + 2 * 128 <= kOffTopE, "meta");
 static_assert(kOffStage % 128 == 0 && kOffMask % 16 == 0 && kOffSumS % 8 == 0 && kOffHist % 16 == 0, "alignment");
@@ -383,26 +384,84 @@ __device__ __forceinline__ uint32_t cscan_u32(uint32_t v, Red* r) {
 
 // Descending bitonic sort of a[0..n) (n <= P, P a power of two) by the
 // consumer threads; a[n..P) is padded with 0 (the smallest key).
-__device__ void csort_desc(uint64_t* a, int n, int P) {
+// Descending bitonic sort of KPT keys per consumer thread (positions
+// tid * KPT + e): compare-exchanges within a thread in registers, within a
+// warp by shuffles, across warps through the shared scratch xs (256 * KPT
+// keys) -- six block barriers pairs at most for 2048 keys.
+template <int KPT>
+__device__ __forceinline__ void bitonic_desc_regs(uint64_t (&r)[KPT], uint64_t* xs) {
   const int tid = threadIdx.x;
-  for (int i = n + tid; i < P; i += kConsumers) a[i] = 0ull;
-  cbar();
-  for (int k = 2; k <= P; k <<= 1) {
+  constexpr int NPOS = kConsumers * KPT;
+  for (int k = 2; k <= NPOS; k <<= 1) {
     for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < P; i += kConsumers) {
-        const int l = i ^ j;
-        if (l > i) {
-          const uint64_t x = a[i], y = a[l];
-          const bool desc = (i & k) == 0;
-          if (desc ? (x < y) : (x > y)) {
-            a[i] = y;
-            a[l] = x;
+      if (j < KPT) {
+#pragma unroll
+        for (int e = 0; e < KPT; ++e) {
+          const int f = e ^ j;
+          if (f > e) {
+            const bool desc = ((tid * KPT + e) & k) == 0;
+            const uint64_t x = r[e], y = r[f];
+            if (desc ? (x < y) : (x > y)) {
+              r[e] = y;
+              r[f] = x;
+            }
           }
         }
+      } else {
+        uint64_t y[KPT];
+        if (j < 32 * KPT) {
+#pragma unroll
+          for (int e = 0; e < KPT; ++e) y[e] = __shfl_xor_sync(0xffffffffu, r[e], j / KPT);
+        } else {
+#pragma unroll
+          for (int e = 0; e < KPT; ++e) xs[tid * KPT + e] = r[e];
+          cbar();
+#pragma unroll
+          for (int e = 0; e < KPT; ++e) y[e] = xs[(tid * KPT + e) ^ j];
+          cbar();
+        }
+#pragma unroll
+        for (int e = 0; e < KPT; ++e) {
+          const int i = tid * KPT + e;
+          const bool keep_max = ((i & j) == 0) == ((i & k) == 0);
+          const uint64_t hi = r[e] > y[e] ? r[e] : y[e];
+          const uint64_t lo = r[e] > y[e] ? y[e] : r[e];
+          r[e] = keep_max ? hi : lo;
+        }
       }
-      cbar();
     }
   }
+}
+
+template <int KPT>
+__device__ __forceinline__ void csort_kpt(uint64_t* a, int n, int P, uint64_t* xs) {
+  const int tid = threadIdx.x;
+  uint64_t r[KPT];
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    const int i = tid * KPT + e;
+    r[e] = i < n ? a[i] : 0ull;
+  }
+  cbar();
+  bitonic_desc_regs<KPT>(r, xs);
+#pragma unroll
+  for (int e = 0; e < KPT; ++e) {
+    const int i = tid * KPT + e;
+    if (i < P) a[i] = r[e];
+  }
+  cbar();
+}
+
+// Sorts a[0, n) descending (keys are > 0); positions [n, P) get 0. P is a
+// power of two <= kCollect. Consumer threads only.
+__device__ void csort_desc(uint64_t* a, int n, int P) {
+  // scratch: the second half of the warp-buffer area (the finisher keeps its
+  // merged histogram in the first half)
+  uint64_t* xs = smem_map().wbuf + 2 * kNB;
+  if (P <= kConsumers) csort_kpt<1>(a, n, P, xs);
+  else if (P <= 2 * kConsumers) csort_kpt<2>(a, n, P, xs);
+  else if (P <= 4 * kConsumers) csort_kpt<4>(a, n, P, xs);
+  else csort_kpt<8>(a, n, P, xs);
 }
 __device__ __forceinline__ int pow2_at_least(int n) {
   int p = 1;
@@ -1020,9 +1079,10 @@ __device__ __noinline__ void sort_table(uint32_t* tab, int n) {
 }
 
 // The metadata of an item and the raw (unsorted) history table of its row,
-// written by one warp. want_tab false: the table is built only for rows on
-// the histogram path (the only ones that re-read the row).
-__device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& mt, uint32_t* tab, bool want_tab) {
+// written by one warp. defer_tab: the table is not gathered; ntab holds minus
+// the history length to gather when a re-read of the row needs the table
+// (lazy_table).
+__device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& mt, uint32_t* tab, bool defer_tab) {
   const int lane = threadIdx.x & 31;
   const int S = spec_chunks(a.V);
   const int row = item / a.nseg;
@@ -1053,9 +1113,9 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
   // history table (only when the penalties are not the identity)
   const bool pen = !(prm.repeat_penalty == 1.0f && prm.frequency_penalty == 0.0f && prm.presence_penalty == 0.0f);
   int ntab = 0;
-  if (a.hist && pen && (want_tab || mode == 2)) {
+  if (a.hist && pen) {
     const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
-    if (hl > 0) ntab = gather_history(a, row, hl, tab);
+    if (hl > 0) ntab = defer_tab ? -hl : gather_history(a, row, hl, tab);
   }
   // Histogram window depth W (nats below the anchor): the mass below it is
   // at most V e^-W of the row max, kept under a quarter of the tail mass
@@ -1106,7 +1166,7 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
       if (lane == 0) atomicExch(&sm.ctl->abort, 1);
       return;
     }
-    build_meta(a, item, sm.meta[slot], sm.tab + slot * kHmax, true);
+    build_meta(a, item, sm.meta[slot], sm.tab + slot * kHmax, false);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.mfull[slot]);
   }
@@ -1218,38 +1278,64 @@ __device__ __forceinline__ void load_slice_global(const SpecArgs& a, const ItemM
   load_slice_raw<E>(rowp, a.V, start, base, v);
   finish_slice<E>(a, mt, tab, hp, start, base, v);
 }
-// Streams a row (warp w: slice w of every chunk) with the next chunk's loads
-// in flight while the current one is processed; f(x, id) for every allowed
-// finite logit.
+// The raw slices of a row (warp w: slice w of every chunk) with three chunks
+// of loads in flight in fixed registers: the loop is unrolled by three, so no
+// register copy waits on a load still in flight. f(v, start) per slice, in
+// chunk order.
 template <typename E, typename F>
+__device__ __forceinline__ void stream_raw3(const E* rowp, int V, int base, F f) {
+  const int S = spec_chunks(V);
+  float b0[4][4], b1[4][4], b2[4][4];
+  load_slice_raw<E>(rowp, V, 0, base, b0);
+  if (S > 1) load_slice_raw<E>(rowp, V, kCE, base, b1);
+  if (S > 2) load_slice_raw<E>(rowp, V, 2 * kCE, base, b2);
+#pragma unroll 1
+  for (int c = 0; c < S; c += 3) {
+    f(b0, c * kCE);
+    if (c + 3 < S) load_slice_raw<E>(rowp, V, (c + 3) * kCE, base, b0);
+    if (c + 1 < S) {
+      f(b1, (c + 1) * kCE);
+      if (c + 4 < S) load_slice_raw<E>(rowp, V, (c + 4) * kCE, base, b1);
+    }
+    if (c + 2 < S) {
+      f(b2, (c + 2) * kCE);
+      if (c + 5 < S) load_slice_raw<E>(rowp, V, (c + 5) * kCE, base, b2);
+    }
+  }
+}
+// Streams a row with penalties and mask applied; f(x, id) for every allowed
+// finite logit. DEEP: three chunks in flight (the finish kernel, which has the
+// registers); otherwise one chunk ahead (inside the streaming kernel).
+template <typename E, bool DEEP, typename F>
 __device__ __forceinline__ void stream_row(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, F f) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int S = spec_chunks(a.V);
   const int base = warp * kSlice;
   const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
   int hp = 0;
-  // three slices in registers: the one being processed and two in flight
-  float n1[4][4], n2[4][4];
-  load_slice_raw<E>(rowp, a.V, 0, base, n1);
-  if (S > 1) load_slice_raw<E>(rowp, a.V, kCE, base, n2);
-#pragma unroll 1
-  for (int c = 0; c < S; ++c) {
-    float v[4][4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[q][k] = n1[q][k];
-        n1[q][k] = n2[q][k];
-      }
-    if (c + 2 < S) load_slice_raw<E>(rowp, a.V, (c + 2) * kCE, base, n2);
-    const int start = c * kCE;
+  auto slice = [&](float (&v)[4][4], int start) {
     finish_slice<E>(a, mt, tab, hp, start, base, v);
 #pragma unroll
     for (int q = 0; q < 4; ++q)
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         if (v[q][k] > RL_NEG_INF) f(v[q][k], start + base + (q * 32 + lane) * 4 + k);
+  };
+  if constexpr (DEEP) {
+    stream_raw3<E>(rowp, a.V, base, slice);
+  } else {
+    const int S = spec_chunks(a.V);
+    float n1[4][4];
+    load_slice_raw<E>(rowp, a.V, 0, base, n1);
+#pragma unroll 1
+    for (int c = 0; c < S; ++c) {
+      float v[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[q][k] = n1[q][k];
+      if (c + 1 < S) load_slice_raw<E>(rowp, a.V, (c + 1) * kCE, base, n1);
+      slice(v, c * kCE);
+    }
   }
 }
 
@@ -1315,7 +1401,7 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
   const float xhi = ctl->cx_hi;
   if constexpr (!SPLIT) {
     // inside the streaming kernel: the penalised stream (few registers)
-    stream_row<E>(a, mt, tab, [&](float x, int id) {
+    stream_row<E, false>(a, mt, tab, [&](float x, int id) {
       if (x >= xlo && x < xhi) {
         const int i = atomicAdd(&ctl->cnt, 1);
         if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
@@ -1332,48 +1418,46 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
   const int base = warp * kSlice;
   const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
   const uint32_t* mrow = mt.mask_on ? a.mask + static_cast<int64_t>(mt.row) * a.mask_stride : nullptr;
-  float n1[4][4], n2[4][4], n3[4][4];
-  load_slice_raw<E>(rowp, V, 0, base, n1);
-  if (S > 1) load_slice_raw<E>(rowp, V, kCE, base, n2);
-  if (S > 2) load_slice_raw<E>(rowp, V, 2 * kCE, base, n3);
-#pragma unroll 1
-  for (int c = 0; c < S; ++c) {
-    float v[4][4];
+  stream_raw3<E>(rowp, V, base, [&](float (&v)[4][4], int start) {
+    unsigned hm = 0u;
 #pragma unroll
     for (int q = 0; q < 4; ++q)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        v[q][k] = n1[q][k];
-        n1[q][k] = n2[q][k];
-        n2[q][k] = n3[q][k];
-      }
-    if (c + 3 < S) load_slice_raw<E>(rowp, V, (c + 3) * kCE, base, n3);
-    const int start = c * kCE;
-    bool hit = false;
+      for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= xlo && v[q][k] < xhi) ? (1u << (q * 4 + k)) : 0u;
+    if (!__any_sync(0xffffffffu, hm != 0u)) return;
+    // the few hits: a compact loop that reloads the logit (still in cache)
+    while (hm) {
+      const int b = __ffs(hm) - 1;
+      hm &= hm - 1u;
+      const int id = start + base + ((b >> 2) * 32 + lane) * 4 + (b & 3);
+      if (mrow && !((__ldcg(mrow + (id >> 5)) >> (id & 31)) & 1u)) continue;
+      const float x = to_f32<E>(rowp[id]);
+      const int i = atomicAdd(&ctl->cnt, 1);
+      if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+    }
+  });
+  cbar();
+  const int n_all = ctl->cnt;
+  if (ntab > 0 && n_all <= kCollect) {
+    // history ids were taken with their raw values: drop them (one search
+    // per collected key), then test their penalised values (an overflowing
+    // bin keeps its count above kCollect and is not filtered)
+    const int n0 = n_all;
+    cbar();
+    if (tid == 0) ctl->cnt = 0;
+    cbar();
+    uint64_t keep[kCollect / kConsumers];
+    int nk = 0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) hit |= v[q][k] >= xlo && v[q][k] < xhi;
-    if (!__any_sync(0xffffffffu, hit)) continue;
-    const int len = min(kCE, V - start);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int e0 = base + (q * 32 + lane) * 4;
-      uint32_t bits = 15u;
-      if (mrow) {
-        const uint32_t word = e0 < len ? __ldcg(mrow + ((start + e0) >> 5)) : 0u;
-        bits = (word >> ((start + e0) & 31)) & 15u;
-      }
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float x = v[q][k];
-        const int id = start + e0 + k;
-        if (x >= xlo && x < xhi && ((bits >> k) & 1u) && !(ntab > 0 && tab_has(tab, ntab, id))) {
-          const int i = atomicAdd(&ctl->cnt, 1);
-          if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
-        }
+    for (int r = 0; r < kCollect / kConsumers; ++r) {
+      const int i = tid + r * kConsumers;
+      if (i < n0) {
+        const uint64_t key = buf[i];
+        if (!tab_has(tab, ntab, static_cast<int>(key_id(key)))) keep[nk++] = key;
       }
     }
+    cbar();
+    for (int r = 0; r < nk; ++r) buf[atomicAdd(&ctl->cnt, 1)] = keep[r];
   }
   // history ids: their penalised values
   for (int j = tid; j < ntab; j += kConsumers) {
@@ -1401,7 +1485,7 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
 // mass (e units, relative to M) reaches target (kind 1: >=, kind 2: >).
 // Returns its key and its exclusive cumulative count and mass; when the
 // target is never reached, *cnt_before = -1 and *mass_before = the total.
-template <typename E>
+template <typename E, bool SPLIT>
 __device__ __noinline__ uint64_t radix_walk(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float M, int kind,
                                long long cnt_target, double target, long long* cnt_before, double* mass_before) {
   const Smem sm = smem_map();
@@ -1418,7 +1502,7 @@ __device__ __noinline__ uint64_t radix_walk(const SpecArgs& a, const ItemMeta& m
     long long my_c = 0;
     double my_m = 0.0;
     const RowT rt = mt.rt;
-    stream_row<E>(a, mt, tab, [&](float x, int id) {
+    stream_row<E, SPLIT>(a, mt, tab, [&](float x, int id) {
       const uint64_t key = cand_key(x, static_cast<uint32_t>(id));
       const double e = static_cast<double>(exact_e(x, M, rt));
       if (hi_match(key, prefix, shift + 8)) {
@@ -1506,6 +1590,23 @@ __device__ int sweep_sorted(const uint64_t* keys, int n, float M, double Z, cons
   }
   *run_end = run;
   return INT_MAX;
+}
+
+// The finish kernel's history table, gathered and sorted when a re-read of
+// the row first needs it (build_meta left minus the history length in ntab).
+__device__ __noinline__ void lazy_table(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab_c) {
+  ItemMeta& m = const_cast<ItemMeta&>(mt);
+  uint32_t* tab = const_cast<uint32_t*>(tab_c);
+  const int hl = -m.ntab;
+  if (hl <= 0) return;
+  cbar();
+  if (threadIdx.x < 32) {
+    const int n = gather_history(a, m.row, hl, tab);
+    if (threadIdx.x == 0) m.ntab = n;
+  }
+  cbar();
+  if (m.ntab > 0) sort_table(tab, m.ntab);
+  cbar();
 }
 
 // Softmax sum of a row from its segment summaries, relative to the row max.
@@ -1710,6 +1811,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
   }
 
   if (!done) {
+    if constexpr (SPLIT) lazy_table(a, mt, tab);
     // ---- below the list: the merged histogram, then the exact radix walk ----
     const double base_m = complete > 0 ? sm.topc[complete - 1] : 0.0;  // probability units
     const long long base_c = complete;
@@ -1737,8 +1839,14 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       {
         double lm[BPT], lc[BPT];
         double sm_ = 0.0, sc_ = 0.0;
+        // bin A's mass unit exp((A+1)/kRbin - M/T) / (kMassQ Z): one exp2 per
+        // thread, then the ratio between neighbouring bins
+        const double rho = exp2(-kLog2e / static_cast<double>(kRbin));
+        double fac = exp2(((static_cast<double>(A_hi - tid * BPT) + 1.0) / static_cast<double>(kRbin) -
+                           static_cast<double>(M) / static_cast<double>(T)) * kLog2e) /
+                     (static_cast<double>(kMassQ) * Z);
 #pragma unroll
-        for (int r = 0; r < BPT; ++r) {
+        for (int r = 0; r < BPT; ++r, fac *= rho) {
           const int i = tid * BPT + r;
           double mq = 0.0, cq = 0.0;
           if (i < nb) {
@@ -1757,9 +1865,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
                 if (mt.need_count) cq += static_cast<double>(__ldcg(a.ws.hcnt + gb));
               }
             }
-            mq *= exp2(((static_cast<double>(A) + 1.0) / static_cast<double>(kRbin) -
-                        static_cast<double>(M) / static_cast<double>(T)) * kLog2e) /
-                  (static_cast<double>(kMassQ) * Z);
+            mq *= fac;
           }
           lm[r] = mq;
           lc[r] = cq;
@@ -1889,7 +1995,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       double Sx_e = 0.0;
       bool have_cut = false;
       if (count_mode) {
-        const uint64_t kk = radix_walk<E>(a, mt, tab, M, 0, K, 0.0, &cb1, &mb1);
+        const uint64_t kk = radix_walk<E, SPLIT>(a, mt, tab, M, 0, K, 0.0, &cb1, &mb1);
         if (cb1 >= 0) {
           kc = kk;
           Sx_e = mb1 + static_cast<double>(exact_e(key_val(kk), M, rt));
@@ -1897,7 +2003,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         }
       }
       if (mass_mode) {
-        const uint64_t kp = radix_walk<E>(a, mt, tab, M, 1, 0, pd * Z, &cb2, &mb2);
+        const uint64_t kp = radix_walk<E, SPLIT>(a, mt, tab, M, 1, 0, pd * Z, &cb2, &mb2);
         if (cb2 >= 0 && (!have_cut || kp > kc)) {
           kc = kp;
           Sx_e = mb2 + static_cast<double>(exact_e(key_val(kp), M, rt));
@@ -1907,12 +2013,12 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       if (!have_cut) {
         long long cbt;
         double tot;
-        radix_walk<E>(a, mt, tab, M, 0, LLONG_MAX, 0.0, &cbt, &tot);
+        radix_walk<E, SPLIT>(a, mt, tab, M, 0, LLONG_MAX, 0.0, &cbt, &tot);
         Sx_e = tot;
       }
       long long cbd;
       double mbd;
-      uint64_t kd = radix_walk<E>(a, mt, tab, M, 2, 0, ud * Sx_e, &cbd, &mbd);
+      uint64_t kd = radix_walk<E, SPLIT>(a, mt, tab, M, 2, 0, ud * Sx_e, &cbd, &mbd);
       if (cbd < 0 || (have_cut && kd < kc)) kd = kc;
       if (kd == 0ull || !(Sx_e > 0.0)) {
         st = RL_ERR_UNSUPPORTED;
@@ -2621,7 +2727,7 @@ __global__ void __launch_bounds__(kConsumers, 2) spec_finish_kernel(const __grid
   const int tid = threadIdx.x;
   const int row = blockIdx.x;
   const int first_item = row * a.nseg;
-  if (tid < 32) build_meta(a, first_item, sm.meta[0], sm.tab, false);
+  if (tid < 32) build_meta(a, first_item, sm.meta[0], sm.tab, true);
   for (int s2 = tid; s2 < a.nseg; s2 += kConsumers) {
     const ItemSum* src = a.ws.sums + first_item + s2;
     ItemSum t;
