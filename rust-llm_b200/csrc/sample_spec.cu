@@ -117,6 +117,7 @@ struct Ctl {
   uint32_t sel_above, sel_cnt;
   int res_i, res_j;
   float cx_lo, cx_hi;  // value interval of the bin being collected
+  int tab_seq;         // split streaming kernel: item sequence + 1 whose table is sorted
 };
 
 struct Red {
@@ -127,7 +128,7 @@ struct Red {
   uint32_t u[kCW];
 };
 
-constexpr int kOffBar = 0;                         // 12 mbarriers
+constexpr int kOffBar = 0;                         // up to 16 mbarriers
 constexpr int kOffCtl = 128;
 constexpr int kOffRed = 256;
 constexpr int kOffWcnt = 512;                      // per-warp candidate counts
@@ -162,6 +163,7 @@ struct Smem {
   uint64_t* empty;   // [kNS]
   uint64_t* mfull;   // [2]
   uint64_t* mempty;  // [2]
+  uint64_t* ready;   // [kNS] split kernel: the chunk in the stage is patched
   Ctl* ctl;
   Red* red;
   int* wcnt;
@@ -187,6 +189,7 @@ __device__ __forceinline__ Smem smem_map() {
   m.empty = m.full + kNS;
   m.mfull = m.empty + kNS;
   m.mempty = m.mfull + 2;
+  m.ready = m.mempty + 2;
   m.ctl = reinterpret_cast<Ctl*>(s + kOffCtl);
   m.red = reinterpret_cast<Red*>(s + kOffRed);
   m.wcnt = reinterpret_cast<int*>(s + kOffWcnt);
@@ -1028,6 +1031,49 @@ __device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, u
   return n;
 }
 
+// Consumers: sorts the raw history ids tab[0, n) (n <= kHmax) with the
+// register bitonic sort (64-bit keys ~id in the radix area, descending =
+// ascending ids) and packs (id << 11) | count like sort_table.
+__device__ __noinline__ void block_sort_table(uint32_t* tab, int n) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  uint64_t* k64 = reinterpret_cast<uint64_t*>(sm.radix);
+  for (int i = tid; i < n; i += kConsumers) k64[i] = static_cast<uint64_t>(~tab[i]);
+  int P = 1;
+  while (P < n) P <<= 1;
+  cbar();
+  csort_desc(k64, n, P);
+#pragma unroll
+  for (int r = 0; r < kHmax / kConsumers; ++r) {
+    const int p = tid + r * kConsumers;
+    if (p < n) tab[p] = ~static_cast<uint32_t>(k64[p]);
+  }
+  cbar();
+  uint32_t packed[kHmax / kConsumers];
+#pragma unroll
+  for (int r = 0; r < kHmax / kConsumers; ++r) {
+    const int p = tid + r * kConsumers;
+    packed[r] = 0u;
+    if (p < n) {
+      const uint32_t id = tab[p];
+      uint32_t c = 0u;
+      if (p == 0 || tab[p - 1] != id) {
+        int q = p + 1;
+        while (q < n && tab[q] == id) ++q;
+        c = static_cast<uint32_t>(min(q - p, 2047));
+      }
+      packed[r] = (id << 11) | c;
+    }
+  }
+  cbar();
+#pragma unroll
+  for (int r = 0; r < kHmax / kConsumers; ++r) {
+    const int p = tid + r * kConsumers;
+    if (p < n) tab[p] = packed[r];
+  }
+  cbar();
+}
+
 // Consumers: sorts the slot's raw history ids and packs them as
 // (id << 11) | count -- the first copy of an id carries its count, later
 // copies count 0 (skipped).
@@ -1076,6 +1122,18 @@ __device__ __noinline__ void sort_table(uint32_t* tab, int n) {
     if (p < n) tab[p] = packed[r];
   }
   cbar();
+}
+
+// Cursor start: the number of table entries with id < lo.
+__device__ __forceinline__ int tab_lower_bound(const uint32_t* tab, int ntab, int lo) {
+  const int lane = threadIdx.x & 31;
+  int c = 0;
+  for (int j0 = 0; j0 < ntab; j0 += 32) {
+    const int j = j0 + lane;
+    const bool lt = j < ntab && static_cast<int>(tab[j] >> 11) < lo;
+    c += __popc(__ballot_sync(0xffffffffu, lt));
+  }
+  return c;
 }
 
 // The metadata of an item and the raw (unsorted) history table of its row,
@@ -1154,11 +1212,12 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
   }
 }
 
-template <typename E>
+template <typename E, bool SPLIT>
 __device__ __noinline__ void meta_loop(const SpecArgs& a) {
   const Smem sm = smem_map();
   const int lane = threadIdx.x & 31;
-  int mseq = 0;
+  const int S = spec_chunks(a.V);
+  int mseq = 0, cseq = 0;
   for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
     const int slot = mseq & 1;
     if (!mbar_wait(&sm.mempty[slot], static_cast<uint32_t>(((mseq >> 1) & 1) ^ 1), kWaitBudget) ||
@@ -1166,9 +1225,73 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
       if (lane == 0) atomicExch(&sm.ctl->abort, 1);
       return;
     }
-    build_meta(a, item, sm.meta[slot], sm.tab + slot * kHmax, false);
+    ItemMeta& mt = sm.meta[slot];
+    uint32_t* tab = sm.tab + slot * kHmax;
+    build_meta(a, item, mt, tab, false);
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.mfull[slot]);
+    if constexpr (SPLIT) {
+      // each chunk of the item: penalties patched into the stage (f32 slices
+      // wholly in the stage; the rest is penalised in registers by the
+      // consumers), then released to the consumers
+      const int row = item / a.nseg;
+      const int seg = item - row * a.nseg;
+      const int c0 = seg * a.cps, c1 = min(S, c0 + a.cps);
+      const int ntab = mt.ntab;
+      const float rp = mt.rp, fq = mt.freq, pr = mt.pres;
+      const bool row_al = (reinterpret_cast<uintptr_t>(reinterpret_cast<const E*>(a.logits) +
+                                                       static_cast<int64_t>(row) * a.ld) & 15u) == 0;
+      bool tab_ok = true;
+      if (sizeof(E) == 4 && ntab > 0 && row_al) {
+        // the consumers sort the table; wait (bounded) for their signal
+        const long long t0 = clock64();
+        while (*reinterpret_cast<volatile int*>(&sm.ctl->tab_seq) != mseq + 1) {
+          if (clock64() - t0 > kWaitBudget || *reinterpret_cast<volatile int*>(&sm.ctl->abort)) {
+            tab_ok = false;
+            break;
+          }
+        }
+        __syncwarp();
+        __threadfence_block();
+      }
+      if (!tab_ok) {
+        if (lane == 0) atomicExch(&sm.ctl->abort, 1);
+        return;
+      }
+      int hp = ntab > 0 ? tab_lower_bound(tab, ntab, c0 * kCE) : 0;
+      for (int c = c0; c < c1; ++c, ++cseq) {
+        const int s = cseq % kNS;
+        if (!mbar_wait(&sm.full[s], static_cast<uint32_t>((cseq / kNS) & 1), kWaitBudget)) {
+          if (lane == 0) atomicExch(&sm.ctl->abort, 1);
+          return;
+        }
+        if (sizeof(E) == 4 && ntab > 0 && row_al) {
+          const int start = c * kCE;
+          const int len = min(kCE, a.V - start);
+          const int nfast = ((len * 4) & ~15) / 4;
+          const int hi = start + (nfast / kSlice) * kSlice;  // whole slices in the stage
+          float* f = reinterpret_cast<float*>(sm.stage + s * kStageBytes);
+          bool wrote = false;
+          while (true) {
+            const int j = hp + lane;
+            const uint32_t ent = j < ntab ? tab[j] : 0xffffffffu;
+            const int id = static_cast<int>(ent >> 11);
+            const bool below = j < ntab && id < hi;
+            if (below && id >= start && (ent & 2047u) != 0u) {
+              f[id - start] = pen_value(f[id - start], static_cast<int>(ent & 2047u), rp, fq, pr);
+              wrote = true;
+            }
+            const int adv = __popc(__ballot_sync(0xffffffffu, below));
+            hp += adv;
+            if (adv < 32) break;
+          }
+          // generic writes ordered before the next bulk copy into this stage
+          if (__any_sync(0xffffffffu, wrote)) fence_proxy_async();
+          __syncwarp();
+        }
+        if (lane == 0) mbar_arrive(&sm.ready[s]);
+      }
+    }
   }
 }
 
@@ -1202,17 +1325,6 @@ __device__ __forceinline__ void pen_regs(float (&v)[4][4], int lo, int hi, const
     hp += adv;
     if (adv < 32) break;
   }
-}
-// Cursor start: the number of table entries with id < lo.
-__device__ __forceinline__ int tab_lower_bound(const uint32_t* tab, int ntab, int lo) {
-  const int lane = threadIdx.x & 31;
-  int c = 0;
-  for (int j0 = 0; j0 < ntab; j0 += 32) {
-    const int j = j0 + lane;
-    const bool lt = j < ntab && static_cast<int>(tab[j] >> 11) < lo;
-    c += __popc(__ballot_sync(0xffffffffu, lt));
-  }
-  return c;
 }
 // Row re-read: the warp's slice of chunk `start` from global memory,
 // penalised and masked (-inf outside the row or disallowed).
@@ -1605,8 +1717,7 @@ __device__ __noinline__ void lazy_table(const SpecArgs& a, const ItemMeta& mt, c
     if (threadIdx.x == 0) m.ntab = n;
   }
   cbar();
-  if (m.ntab > 0) sort_table(tab, m.ntab);
-  cbar();
+  if (m.ntab > 0) block_sort_table(tab, m.ntab);
 }
 
 // Softmax sum of a row from its segment summaries, relative to the row max.
@@ -2297,7 +2408,7 @@ __device__ __noinline__ uint64_t compact_warp_buf(uint64_t* wbuf, const uint64_t
 // ---------------------------------------------------------------------------
 // The chunks of one item (consumer threads), specialised per row mode so
 // that each mode keeps only the state it needs in registers.
-template <typename E, int MODE>
+template <typename E, int MODE, bool SPLIT>
 __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -2355,9 +2466,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     if (!mask_on && nfast == kCE) {
       const int s = cseq % kNS;
       float* f = reinterpret_cast<float*>(sm.stage + s * kStageBytes);
-      if (mbar_wait(&sm.full[s], static_cast<uint32_t>((cseq / kNS) & 1), kWaitBudget)) {
+      // (split kernel: the row-preparation warp patched the stage already)
+      if (mbar_wait(SPLIT ? &sm.ready[s] : &sm.full[s], static_cast<uint32_t>((cseq / kNS) & 1), kWaitBudget)) {
         const int lo = start + base, hi = lo + kSlice;
-        while (ntab > 0) {
+        while (!SPLIT && ntab > 0) {
           const int j = hp + lane;
           const uint32_t ent = j < ntab ? tab[j] : 0xffffffffu;
           const int id = static_cast<int>(ent >> 11);
@@ -2389,7 +2501,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     }
     const int s = cseq % kNS;
     const uint32_t ph = static_cast<uint32_t>((cseq / kNS) & 1);
-    if (!mbar_wait(&sm.full[s], ph, kWaitBudget)) tmo = 1;
+    if (!mbar_wait(SPLIT ? &sm.ready[s] : &sm.full[s], ph, kWaitBudget)) tmo = 1;
     const int start = c * kCE;
     const int len = min(kCE, V - start);
     const int nfast = row_al ? ((len * es) & ~15) / es : 0;
@@ -2401,7 +2513,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     // penalties patched into the stage (f32 slices entirely in the stage)
     const bool patch = (es == 4) && (base + kSlice <= nfast);
     bool patched = false;
-    if (ntab > 0 && patch) {
+    if (!SPLIT && ntab > 0 && patch) {
       float* f = reinterpret_cast<float*>(stg);
       while (true) {
         const int j = hp + lane;
@@ -2681,11 +2793,22 @@ __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
       return;
     }
     const int mode = sm.meta[slot].mode;
-    if (sm.meta[slot].ntab > 0) sort_table(sm.tab + slot * kHmax, sm.meta[slot].ntab);
+    if (sm.meta[slot].ntab > 0) {
+      if constexpr (SPLIT) {
+        block_sort_table(sm.tab + slot * kHmax, sm.meta[slot].ntab);
+        // the row-preparation warp patches the stages with this table
+        if (tid == 0) {
+          __threadfence_block();
+          *reinterpret_cast<volatile int*>(&sm.ctl->tab_seq) = mseq + 1;
+        }
+      } else {
+        sort_table(sm.tab + slot * kHmax, sm.meta[slot].ntab);
+      }
+    }
     ItemAcc acc;
-    if (mode == 0) acc = run_item<E, 0>(a, slot, cseq);
-    else if (mode == 1) acc = run_item<E, 1>(a, slot, cseq);
-    else acc = run_item<E, 2>(a, slot, cseq);
+    if (mode == 0) acc = run_item<E, 0, SPLIT>(a, slot, cseq);
+    else if (mode == 1) acc = run_item<E, 1, SPLIT>(a, slot, cseq);
+    else acc = run_item<E, 2, SPLIT>(a, slot, cseq);
     cseq = acc.cseq;
     item_end<E, SPLIT>(a, item, slot, acc);
     // the row data of this slot may be rebuilt
@@ -2708,13 +2831,15 @@ __global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_con
       mbar_init(&sm.mfull[s], 1);
       mbar_init(&sm.mempty[s], kCW);
     }
+    for (int s = 0; s < kNS; ++s) mbar_init(&sm.ready[s], 1);
     sm.ctl->abort = 0;
+    sm.ctl->tab_seq = 0;
     fence_mbar_init();
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5;
   if (warp == kProdWarp) producer_loop<E>(a);
-  else if (warp == kMetaWarp) meta_loop<E>(a);
+  else if (warp == kMetaWarp) meta_loop<E, SPLIT>(a);
   else consumer_loop<E, SPLIT>(a);
 }
 
