@@ -2444,6 +2444,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   int atop = kNoAnchor;
   float atop_f = 0.0f, x_lo = RL_POS_INF;
   const float wb_f = static_cast<float>(mt.wbins);
+  // item fields the loop needs live in registers: a shared-memory read after
+  // a shared atomic waits for the atomic to complete
+  const bool need_cnt = mt.need_count != 0;
+  const int c0 = mt.c0, c1 = mt.c1;
   bool hist_on = MODE == 2;
   int hp = ntab > 0 ? tab_lower_bound(tab, ntab, mt.c0 * kCE) : 0;
   if (mode == 2)
@@ -2493,7 +2497,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
     }
   }
 
-  for (int c = mt.c0; c < mt.c1; ++c, ++cseq) {
+  for (int c = c0; c < c1; ++c, ++cseq) {
     if (MODE != 0 && wcnt > kWcompact) {
       // room for a whole slice of appends (no logits are live here)
       tau = compact_warp_buf(wbuf, gov, &wcnt, nkeep, bins_w, sm.wcnt + warp, &sm.ctl->tau_shared);
@@ -2588,7 +2592,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       }
     }
     // the stage is released: generic writes ordered before the next bulk copy
-    if (patched || (c == mt.c0 && pre_patched)) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (patched || (c == c0 && pre_patched)) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty[s]);
     // penalties in registers (bf16, or slices partly outside the stage)
@@ -2740,7 +2744,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
                 const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
                 const int r = static_cast<int>(rf);
                 atomicAdd(&sm.hmass[r], qm);
-                if (mt.need_count) atomicAdd(&sm.hcnt[r], 1u);
+                if (need_cnt) atomicAdd(&sm.hcnt[r], 1u);
                 qs += qm;
               }
             }
