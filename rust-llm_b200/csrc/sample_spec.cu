@@ -76,14 +76,24 @@ __device__ __forceinline__ float ex2_approx(float t) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
   return y;
 }
-// Absolute histogram bin of x: floor(x * kRbin / T), as a float.
-__device__ __forceinline__ float bin_of(float x, const RowT& r) { return floorf(__fmul_rn(x, r.cb_hi)); }
-// Mass of x relative to the top edge of its bin af: exp(x/T - (af+1)/kRbin).
-__device__ __forceinline__ float bin_rel_mass(float x, float af, const RowT& r) {
-  const float yh = __fmul_rn(x, r.cb_hi);
-  const float yl = __fmaf_rn(x, r.cb_hi, -yh) + x * r.cb_lo;
-  return ex2_approx(((yh - af) + yl - 1.0f) * r.dlt);
+// 1.5 * 2^23: adding it to a float f with |f| < 2^22 rounds f to the nearest
+// integer n (ties to even), and the sum's bit pattern is 0x4B400000 + n.
+constexpr float kMagic = 12582912.0f;
+constexpr uint32_t kMagicBits = 0x4B400000u;
+// Absolute histogram bin of x, about floor(x * kRbin / T): the nearest integer
+// to x * cb - 1/2 by the magic-number add (full-rate float adds, no
+// conversion instruction). Non-decreasing in x; equal to the floor except
+// that x * cb within rounding of an integer may land one bin lower. Valid for
+// |x * cb| < 2^22 (histogram windows anchor well inside that range).
+__device__ __forceinline__ int bin_int(float x, const RowT& r) {
+  return static_cast<int>(__float_as_uint(__fadd_rn(__fmaf_rn(x, r.cb_hi, -0.5f), kMagic)) - kMagicBits);
 }
+__device__ __forceinline__ float bin_of(float x, const RowT& r) { return static_cast<float>(bin_int(x, r)); }
+// kMassQ exp((u - 1) / kRbin) for the position u in [0, 1] of a logit in its
+// bin: the mass relative to the bin's top edge in 2^20 fixed point. A cubic in
+// u, the degree-3 Taylor polynomial of the exponential about u = 1/2 expanded
+// in powers of u (relative error < 6e-8 on [0, 1]).
+constexpr float kMq0 = 985045.9375f, kMq1 = 61565.6953125f, kMq2 = 1922.958740234375f, kMq3 = 41.35395050048828f;
 __device__ __forceinline__ float pen_value(float v, int cnt, float rp, float freq, float pres) {
   const float x1 = (v < 0.0f) ? mul_rn(v, rp) : div_rn(v, rp);
   return sub_rn(sub_rn(x1, mul_rn(static_cast<float>(cnt), freq)), pres);
@@ -1485,13 +1495,22 @@ __device__ __forceinline__ bool tab_has(const uint32_t* tab, int ntab, int id) {
   return lo < ntab && static_cast<int>(tab[lo] >> 11) == id;
 }
 
-// The smallest float x with bin_of(x) >= A (bin_of is non-decreasing in x
-// for T > 0): a guess within a few ulps, then single-ulp steps (bounded).
+// The smallest float x with bin_of(x) >= A. bin_of is non-decreasing in x
+// over |x * cb| < 2^22 (the range that histogram windows accept), so this is
+// a binary search (32 steps) over the order-preserving integer image of that
+// range. Near 0 a bin edge can lie many ulps away from A / cb (x * cb - 1/2
+// rounds to -1/2 for every |x * cb| < 2^-25), so no stepping from a guess.
 __device__ float bin_floor_x(float A, const RowT& rt) {
-  float g = __fdiv_rn(A, rt.cb_hi);
-  for (int it = 0; it < 4096 && bin_of(g, rt) >= A; ++it) g = nextafterf(g, RL_NEG_INF);
-  for (int it = 0; it < 4096 && bin_of(g, rt) < A; ++it) g = nextafterf(g, RL_POS_INF);
-  return g;
+  const float lim = 4190000.0f / rt.cb_hi;
+  if (bin_of(-lim, rt) >= A) return RL_NEG_INF;
+  if (bin_of(lim, rt) < A) return RL_POS_INF;
+  uint32_t lo = ord_key(-lim), hi = ord_key(lim);  // bin(lo) < A <= bin(hi)
+  while (hi - lo > 1u) {
+    const uint32_t mid = lo + ((hi - lo) >> 1);
+    if (bin_of(ord_key_inv(mid), rt) >= A) hi = mid;
+    else lo = mid;
+  }
+  return ord_key_inv(hi);
 }
 
 // Keys of the allowed logits of absolute bin A, gathered from a re-read of
@@ -2447,6 +2466,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   // item fields the loop needs live in registers: a shared-memory read after
   // a shared atomic waits for the atomic to complete
   const bool need_cnt = mt.need_count != 0;
+  const uint32_t wb_u = static_cast<uint32_t>(mt.wbins);
   const int c0 = mt.c0, c1 = mt.c1;
   bool hist_on = MODE == 2;
   int hp = ntab > 0 ? tab_lower_bound(tab, ntab, mt.c0 * kCE) : 0;
@@ -2722,7 +2742,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         const float bm = cmax_f(lm, sm.red);
         if (bm > RL_NEG_INF) {
           const float af = bin_of(bm, rt);
-          if (fabsf(af) < 4194304.0f) {
+          if (fabsf(af) < 4190000.0f) {
             atop = static_cast<int>(af) + kHead;
             atop_f = static_cast<float>(atop);
             x_lo = (atop_f - wb_f - 2.0f) / rt.cb_hi;  // logits below are outside the window
@@ -2732,23 +2752,29 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         }
       }
       if (atop != kNoAnchor && __any_sync(0xffffffffu, lm >= x_lo)) {
+        // straight-line per logit, only the atomics predicated: the window
+        // offset r of the bin (bin_int), the position u of x in its bin and
+        // the fixed-point mass from the cubic, rounded by the magic add; no
+        // exp, floor or conversion instructions (quarter-rate pipes)
+        const uint32_t K = static_cast<uint32_t>(atop) + kMagicBits;
+        uint32_t q32 = 0u;  // <= 16 * 2^20 per chunk
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float x = v[q][k];
-            if (x >= x_lo) {
-              const float af = bin_of(x, rt);
-              const float rf = atop_f - af;
-              if (rf >= 0.0f && rf <= wb_f) {
-                const uint32_t qm = __float2uint_rn(bin_rel_mass(x, af, rt) * kMassQ);
-                const int r = static_cast<int>(rf);
-                atomicAdd(&sm.hmass[r], qm);
-                if (need_cnt) atomicAdd(&sm.hcnt[r], 1u);
-                qs += qm;
-              }
+            const float sb = __fadd_rn(__fmaf_rn(x, rt.cb_hi, -0.5f), kMagic);
+            const uint32_t r = K - __float_as_uint(sb);
+            const float u = __fmaf_rn(x, rt.cb_lo, __fmaf_rn(x, rt.cb_hi, -__fsub_rn(sb, kMagic)));
+            const float pm = __fmaf_rn(__fmaf_rn(__fmaf_rn(kMq3, u, kMq2), u, kMq1), u, kMq0);
+            const uint32_t qm = __float_as_uint(__fadd_rn(pm, kMagic)) - kMagicBits;
+            if (r <= wb_u) {
+              atomicAdd(&sm.hmass[r], qm);
+              if (need_cnt) atomicAdd(&sm.hcnt[r], 1u);
+              q32 += qm;
             }
           }
+        qs += q32;
       }
     }
   }
