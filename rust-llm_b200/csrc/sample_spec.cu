@@ -2758,22 +2758,32 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         // exp, floor or conversion instructions (quarter-rate pipes)
         const uint32_t K = static_cast<uint32_t>(atop) + kMagicBits;
         uint32_t q32 = 0u;  // <= 16 * 2^20 per chunk
+        uint32_t rr[16], qq[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int j = 0; j < 16; ++j) {
+          const float x = v[j >> 2][j & 3];
+          const float sb = __fadd_rn(__fmaf_rn(x, rt.cb_hi, -0.5f), kMagic);
+          rr[j] = K - __float_as_uint(sb);
+          const float u = __fmaf_rn(x, rt.cb_lo, __fmaf_rn(x, rt.cb_hi, -__fsub_rn(sb, kMagic)));
+          const float pm = __fmaf_rn(__fmaf_rn(__fmaf_rn(kMq3, u, kMq2), u, kMq1), u, kMq0);
+          qq[j] = __float_as_uint(__fadd_rn(pm, kMagic)) - kMagicBits;
+          q32 += rr[j] <= wb_u ? qq[j] : 0u;
+        }
+        // the window's atomics back to back, predicated (no branches)
+        const uint32_t hb = smem_u32(sm.hmass);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float x = v[q][k];
-            const float sb = __fadd_rn(__fmaf_rn(x, rt.cb_hi, -0.5f), kMagic);
-            const uint32_t r = K - __float_as_uint(sb);
-            const float u = __fmaf_rn(x, rt.cb_lo, __fmaf_rn(x, rt.cb_hi, -__fsub_rn(sb, kMagic)));
-            const float pm = __fmaf_rn(__fmaf_rn(__fmaf_rn(kMq3, u, kMq2), u, kMq1), u, kMq0);
-            const uint32_t qm = __float_as_uint(__fadd_rn(pm, kMagic)) - kMagicBits;
-            if (r <= wb_u) {
-              atomicAdd(&sm.hmass[r], qm);
-              if (need_cnt) atomicAdd(&sm.hcnt[r], 1u);
-              q32 += qm;
-            }
-          }
+        for (int j = 0; j < 16; ++j)
+          asm volatile("{ .reg .pred p; setp.le.u32 p, %0, %1; @p red.shared.add.u32 [%2], %3; }" ::"r"(rr[j]), "r"(wb_u),
+                       "r"(hb + 4u * rr[j]), "r"(qq[j])
+                       : "memory");
+        if (need_cnt) {
+          const uint32_t cb = smem_u32(sm.hcnt);
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            asm volatile("{ .reg .pred p; setp.le.u32 p, %0, %1; @p red.shared.add.u32 [%2], 1; }" ::"r"(rr[j]), "r"(wb_u),
+                         "r"(cb + 4u * rr[j])
+                         : "memory");
+        }
         qs += q32;
       }
     }
