@@ -126,7 +126,8 @@ struct Ctl {
   int sel_bucket;
   uint32_t sel_above, sel_cnt;
   int res_i, res_j;
-  float cx_lo, cx_hi;  // value interval of the bin being collected
+  float cx_lo, cx_hi;    // value interval of the bin being collected
+  float cx_lo2, cx_hi2;  // a second bin collected by the same re-read (empty: +inf, -inf)
   int tab_seq;         // split streaming kernel: item sequence + 1 whose table is sorted
 };
 
@@ -468,6 +469,24 @@ __device__ __forceinline__ void csort_kpt(uint64_t* a, int n, int P, uint64_t* x
 // Sorts a[0, n) descending (keys are > 0); positions [n, P) get 0. P is a
 // power of two <= kCollect. Consumer threads only.
 __device__ void csort_desc(uint64_t* a, int n, int P) {
+  if (P <= 32) {
+    // one warp, one key per lane
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      uint64_t r = lane < n ? a[lane] : 0ull;
+#pragma unroll
+      for (int k = 2; k <= 32; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          const uint64_t y = __shfl_xor_sync(0xffffffffu, r, j);
+          const bool keep_max = ((lane & j) == 0) == ((lane & k) == 0);
+          r = keep_max ? (r > y ? r : y) : (r > y ? y : r);
+        }
+      if (lane < P) a[lane] = r;
+    }
+    cbar();
+    return;
+  }
   // scratch: the second half of the warp-buffer area (the finisher keeps its
   // merged histogram in the first half)
   uint64_t* xs = smem_map().wbuf + 2 * kNB;
@@ -1513,27 +1532,36 @@ __device__ float bin_floor_x(float A, const RowT& rt) {
   return ord_key_inv(hi);
 }
 
-// Keys of the allowed logits of absolute bin A, gathered from a re-read of
-// the row into buf; returns the count (> kCollect: too many). The stream
-// compares raw logits against the bin's value interval and leaves out the
-// history ids, which are then tested with their penalised values.
+// Keys of the allowed logits of absolute bin A (and of bin A2 unless A2 is
+// NaN), gathered from one re-read of the row into buf; returns the count
+// (> kCollect: too many). The stream compares raw logits against the bins'
+// value intervals and leaves out the history ids, which are then tested with
+// their penalised values.
 template <typename E, bool SPLIT>
-__device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, uint64_t* buf,
-                           Ctl* ctl) {
+__device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, float A2,
+                                        uint64_t* buf, Ctl* ctl) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowT rt = mt.rt;
+  // the four bin edges, one thread each
   if (tid == 0) {
     ctl->cnt = 0;
     ctl->cx_lo = bin_floor_x(A, rt);
+  } else if (tid == 32) {
     ctl->cx_hi = bin_floor_x(A + 1.0f, rt);
+  } else if (tid == 64) {
+    ctl->cx_lo2 = A2 == A2 ? bin_floor_x(A2, rt) : RL_POS_INF;
+  } else if (tid == 96) {
+    ctl->cx_hi2 = A2 == A2 ? bin_floor_x(A2 + 1.0f, rt) : RL_NEG_INF;
   }
   cbar();
   const float xlo = ctl->cx_lo;
   const float xhi = ctl->cx_hi;
+  const float xlo2 = ctl->cx_lo2;
+  const float xhi2 = ctl->cx_hi2;
   if constexpr (!SPLIT) {
     // inside the streaming kernel: the penalised stream (few registers)
     stream_row<E, false>(a, mt, tab, [&](float x, int id) {
-      if (x >= xlo && x < xhi) {
+      if ((x >= xlo && x < xhi) || (x >= xlo2 && x < xhi2)) {
         const int i = atomicAdd(&ctl->cnt, 1);
         if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
       }
@@ -1549,14 +1577,8 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
   const int base = warp * kSlice;
   const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
   const uint32_t* mrow = mt.mask_on ? a.mask + static_cast<int64_t>(mt.row) * a.mask_stride : nullptr;
-  stream_raw3<E>(rowp, V, base, [&](float (&v)[4][4], int start) {
-    unsigned hm = 0u;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= xlo && v[q][k] < xhi) ? (1u << (q * 4 + k)) : 0u;
-    if (!__any_sync(0xffffffffu, hm != 0u)) return;
-    // the few hits: a compact loop that reloads the logit (still in cache)
+  // the few hits: a compact loop that reloads the logit (still in cache)
+  auto take = [&](unsigned hm, int start) {
     while (hm) {
       const int b = __ffs(hm) - 1;
       hm &= hm - 1u;
@@ -1566,7 +1588,36 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
       const int i = atomicAdd(&ctl->cnt, 1);
       if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
     }
-  });
+  };
+  if (!(xlo2 < xhi2)) {
+    // one bin: two compares per logit
+    stream_raw3<E>(rowp, V, base, [&](float (&v)[4][4], int start) {
+      unsigned hm = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= xlo && v[q][k] < xhi) ? (1u << (q * 4 + k)) : 0u;
+      if (__any_sync(0xffffffffu, hm != 0u)) take(hm, start);
+    });
+  } else {
+    // two bins (xhi <= xlo2): one compare against the lower edge, the exact
+    // test only where a lane of the warp passes it
+    stream_raw3<E>(rowp, V, base, [&](float (&v)[4][4], int start) {
+      unsigned hm = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= xlo) ? (1u << (q * 4 + k)) : 0u;
+      if (!__any_sync(0xffffffffu, hm != 0u)) return;
+      hm = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          hm |= ((v[q][k] >= xlo && v[q][k] < xhi) || (v[q][k] >= xlo2 && v[q][k] < xhi2)) ? (1u << (q * 4 + k)) : 0u;
+      if (__any_sync(0xffffffffu, hm != 0u)) take(hm, start);
+    });
+  }
   cbar();
   const int n_all = ctl->cnt;
   if (ntab > 0 && n_all <= kCollect) {
@@ -1600,7 +1651,7 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
     const float raw = to_f32<E>(rowp[id]);
     if (raw != raw) continue;
     const float x = pen_value(raw, cnt, mt.rp, mt.freq, mt.pres);
-    if (x >= xlo && x < xhi) {
+    if ((x >= xlo && x < xhi) || (x >= xlo2 && x < xhi2)) {
       const int i = atomicAdd(&ctl->cnt, 1);
       if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
     }
@@ -1723,14 +1774,25 @@ __device__ int sweep_sorted(const uint64_t* keys, int n, float M, double Z, cons
   return INT_MAX;
 }
 
-// The finish kernel's history table, gathered and sorted when a re-read of
-// the row first needs it (build_meta left minus the history length in ntab).
-__device__ __noinline__ void lazy_table(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab_c) {
+// The finish kernel's history table, when a re-read of the row first needs
+// it (build_meta left minus the history length in ntab): the sorted table
+// the streaming kernel left for the row's first item, else gathered and
+// sorted here.
+__device__ __noinline__ void lazy_table(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab_c, int first_item) {
   ItemMeta& m = const_cast<ItemMeta&>(mt);
   uint32_t* tab = const_cast<uint32_t*>(tab_c);
   const int hl = -m.ntab;
   if (hl <= 0) return;
   cbar();
+  if (a.ws.tabs) {
+    const int n = __ldcg(a.ws.tabn + first_item);
+    const uint32_t* src = a.ws.tabs + static_cast<int64_t>(first_item) * kHmax;
+    for (int i = threadIdx.x; i < n; i += kConsumers) tab[i] = __ldcg(src + i);
+    cbar();
+    if (threadIdx.x == 0) m.ntab = n;
+    cbar();
+    return;
+  }
   if (threadIdx.x < 32) {
     const int n = gather_history(a, m.row, hl, tab);
     if (threadIdx.x == 0) m.ntab = n;
@@ -1941,7 +2003,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
   }
 
   if (!done) {
-    if constexpr (SPLIT) lazy_table(a, mt, tab);
+    if constexpr (SPLIT) lazy_table(a, mt, tab, first_item);
     // ---- below the list: the merged histogram, then the exact radix walk ----
     const double base_m = complete > 0 ? sm.topc[complete - 1] : 0.0;  // probability units
     const long long base_c = complete;
@@ -2018,8 +2080,9 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         cbar();
       }
       uint64_t* buf = reinterpret_cast<uint64_t*>(sm.hmass);  // collect buffer (the histogram is merged)
-      int held = -1;  // bin whose sorted keys are in buf
-      int nheld = 0;
+      // sorted keys in buf: bin held at [off1, off1 + n1), bin held2 (read
+      // with it, higher values) at [0, n2)
+      int held = -1, held2 = -1, off1 = 0, n1 = 0, n2 = 0;
       double corr = 0.0;  // exact minus histogram mass of the bins passed so far
       long long ccorr = 0;
       // -- the cutoff bin --
@@ -2042,13 +2105,53 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         if (f == INT_MAX) break;
         const double mb = base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
         const long long cb = base_c + ccorr + (f > 0 ? static_cast<long long>(cc[f - 1]) : 0);
-        nheld = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
-        if (nheld > kCollect) break;
-        csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
+        // the draw bin, when a cutoff in bin f already fixes it: read in the
+        // same pass. S lies in [bin start, bin end]; with top_p alone, in
+        // [top_p, top_p + the mass of one logit at the bin's top edge]
+        int fd = -1;
+        {
+          const bool p_only = mass_mode && !count_mode;
+          const double e_top = exp2((static_cast<double>(A_hi - f + 1) / static_cast<double>(kRbin) -
+                                     static_cast<double>(M) / static_cast<double>(T)) * kLog2e) / Z;
+          const double s_end = base_m + corr + cm[f];
+          const double t_lo = ud * (p_only ? fmax(mb, pd) : mb);
+          const double t_hi = ud * (p_only ? fmin(s_end, fmax(mb, pd) + e_top) : s_end);
+          if (t_lo >= base_m) {
+            int b_lo = INT_MAX, b_hi = INT_MAX;
+#pragma unroll
+            for (int r = 0; r < BPT; ++r) {
+              const int i = tid * BPT + r;
+              if (i < f) {
+                const double e_i = base_m + corr + cm[i];
+                if (e_i > t_lo && i < b_lo) b_lo = i;
+                if (e_i > t_hi && i < b_hi) b_hi = i;
+              }
+            }
+            b_lo = cmin_i(b_lo, rs);
+            b_hi = cmin_i(b_hi, rs);
+            if (b_lo == b_hi && b_lo < f) fd = b_lo;
+          }
+        }
+        const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
+                                               fd >= 0 ? static_cast<float>(A_hi - fd) : __int_as_float(0x7fc00000), buf, ctl);
+        if (ntot > kCollect) break;
+        csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
+        n2 = 0;
+        if (fd >= 0) {
+          const float lo_d = ctl->cx_lo2;
+          int j0 = INT_MAX;
+          for (int j = tid; j < ntot; j += kConsumers)
+            if (key_val(buf[j]) < lo_d) j0 = min(j0, j);
+          j0 = cmin_i(j0, rs);
+          n2 = j0 == INT_MAX ? ntot : j0;
+        }
         held = f;
+        held2 = fd;
+        off1 = n2;
+        n1 = ntot - n2;
         double cum_at = 0.0, run_end = 0.0;
         const int g = sweep_sorted(
-            buf, nheld, M, Z, rt, mb,
+            buf + off1, n1, M, Z, rt, mb,
             [&](int j, double cum) {
               return (count_mode && cb + j == static_cast<long long>(K) - 1) || (mass_mode && cum >= pd);
             },
@@ -2062,7 +2165,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         } else {
           // the histogram overstated this bin: continue with its exact mass
           corr += (run_end - mb) - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
-          ccorr += static_cast<long long>(nheld) - static_cast<long long>(cc[f] - (f > 0 ? cc[f - 1] : 0.0));
+          ccorr += static_cast<long long>(n1) - static_cast<long long>(cc[f] - (f > 0 ? cc[f - 1] : 0.0));
           i0 = f + 1;
         }
       }
@@ -2092,21 +2195,31 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             int f = cmin_i(best, rs);
             if (cut_pos >= 0 && (f == INT_MAX || f > i_c)) f = i_c;
             if (f == INT_MAX) break;
-            if (held != f) {
-              nheld = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), buf, ctl);
-              if (nheld > kCollect) break;
-              csort_desc(buf, nheld, pow2_at_least(max(nheld, 1)));
+            const uint64_t* kb = buf + off1;
+            int kn = n1;
+            if (held2 == f) {
+              kb = buf;
+              kn = n2;
+            } else if (held != f) {
+              const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), __int_as_float(0x7fc00000), buf, ctl);
+              if (ntot > kCollect) break;
+              csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
               held = f;
+              held2 = -1;
+              off1 = 0;
+              n1 = ntot;
+              kb = buf;
+              kn = ntot;
             }
             const bool at_cut = cut_pos >= 0 && f == i_c;
             const double mb = at_cut ? bm_cut : base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
-            const int lim = at_cut ? cut_pos + 1 : nheld;
+            const int lim = at_cut ? cut_pos + 1 : kn;
             double cum_at = 0.0, run_end = 0.0;
             int g = sweep_sorted(
-                buf, lim, M, Z, rt, mb, [&](int, double cum) { return cum > tgt; }, rs, ctl, &cum_at, &run_end);
+                kb, lim, M, Z, rt, mb, [&](int, double cum) { return cum > tgt; }, rs, ctl, &cum_at, &run_end);
             if (g == INT_MAX && at_cut) g = cut_pos;
             if (g != INT_MAX) {
-              const uint64_t key = buf[g];
+              const uint64_t key = kb[g];
               token = static_cast<int>(key_id(key));
               prob = static_cast<float>((static_cast<double>(exact_e(key_val(key), M, rt)) / Z) / Sx);
               resolved = true;
@@ -2330,8 +2443,15 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
   const int first_item = row * a.nseg;
   if constexpr (SPLIT) {
     // the finish kernel merges the row's items: every item goes to the
-    // workspace
-    if (tid == 0) a.ws.sums[item] = is;
+    // workspace (with its sorted history table, for the rows that re-read)
+    if (tid == 0) {
+      a.ws.sums[item] = is;
+      a.ws.tabn[item] = mt.ntab;
+    }
+    if (mode != 0) {
+      uint32_t* gt = a.ws.tabs + static_cast<int64_t>(item) * kHmax;
+      for (int i = tid; i < mt.ntab; i += kConsumers) gt[i] = tab[i];
+    }
     uint64_t* gc = a.ws.cands + static_cast<int64_t>(item) * kN;
     for (int i = tid; i < ncand; i += kConsumers) gc[i] = sm.top[i];
     if (mode == 2) {

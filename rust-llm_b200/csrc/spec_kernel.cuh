@@ -59,6 +59,8 @@ struct Workspace {
   uint32_t* hmass;    // [max_items * kNB]
   uint32_t* hcnt;     // [max_items * kNB]
   uint64_t* wovf;     // [max_ctas * kCW * kWovf] per-warp candidate overflow
+  uint32_t* tabs;     // [max_items * kHmax] the item's sorted history table (split launch)
+  int32_t* tabn;      // [max_items] its entry count
   int max_items;      // items of a launch with more than one segment per row
 };
 

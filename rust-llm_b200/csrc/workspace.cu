@@ -30,6 +30,7 @@ rl_status alloc_workspace(rl_sampler* h) {
   h->ws.max_items = static_cast<int>(items);
   ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, items) && dalloc(&h->ws.cands, items * kN) &&
        dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&
+       dalloc(&h->ws.tabs, items * kHmax) && dalloc(&h->ws.tabn, items) &&
        dalloc(&h->ws.wovf, static_cast<size_t>(spec_max_ctas(h->num_sms)) * kCW * kWovf);
   ok = ok && dalloc(&h->part_keys, B * kN) && dalloc(&h->part_stats, B) && dalloc(&h->beam_params, B) &&
        dalloc(&h->zero_u, B);
@@ -59,6 +60,8 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->ws.hcnt);
   cudaFree(h->ws.hmass);
   cudaFree(h->ws.wovf);
+  cudaFree(h->ws.tabs);
+  cudaFree(h->ws.tabn);
   h->ws = {};
   cudaFree(h->part_keys);
   cudaFree(h->part_stats);
