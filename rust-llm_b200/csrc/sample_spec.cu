@@ -984,12 +984,18 @@ __device__ __forceinline__ uint64_t evict_last_policy() {
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
 template <typename E>
 __device__ __noinline__ void producer_loop(const SpecArgs& a) {
   if ((threadIdx.x & 31) != 0) return;
   const Smem sm = smem_map();
   const int S = spec_chunks(a.V);
   const uint64_t keep_l2 = evict_last_policy();
+  const uint64_t drop_l2 = evict_first_policy();
   int seq = 0;
   bool ok = true;
   for (int item = blockIdx.x; item < a.nitems && ok; item += gridDim.x) {
@@ -1015,8 +1021,9 @@ __device__ __noinline__ void producer_loop(const SpecArgs& a) {
       mbar_expect_tx(&sm.full[s], db + mb);
       if (db) {
         const E* src = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(row) * a.ld + start;
-        if (hint) bulk_g2s_hint(sm.stage + s * kStageBytes, src, db, &sm.full[s], keep_l2);
-        else bulk_g2s(sm.stage + s * kStageBytes, src, db, &sm.full[s]);
+        // rows that are read once leave L2 first, so that the histogram
+        // rows stay for their finisher's re-read
+        bulk_g2s_hint(sm.stage + s * kStageBytes, src, db, &sm.full[s], hint ? keep_l2 : drop_l2);
       }
       if (mb)
         bulk_g2s(sm.maskst + s * kMaskWords, a.mask + static_cast<int64_t>(row) * a.mask_stride + (start >> 5), mb,
@@ -1039,15 +1046,16 @@ __device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, u
   const int lane = threadIdx.x & 31;
   const int32_t* h = a.hist + static_cast<int64_t>(row) * a.hist_stride;
   int n = 0;
-  for (int g0 = 0; g0 < hl; g0 += 256) {
-    int ids[8];
+  for (int g0 = 0; g0 < hl; g0 += 512) {
+    // 16 loads in flight per lane: a 512-token history in one round trip
+    int ids[16];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < 16; ++r) {
       const int i = g0 + r * 32 + lane;
       ids[r] = i < hl ? __ldg(h + i) : -1;
     }
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
+    for (int r = 0; r < 16; ++r) {
       const int i = g0 + r * 32 + lane;
       const int id = ids[r] - a.vocab_offset;
       const bool ok = i < hl && id >= 0 && id < a.V;
@@ -1279,6 +1287,7 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
             tab_ok = false;
             break;
           }
+          __nanosleep(128);  // leave the issue slots to the sorting warps
         }
         __syncwarp();
         __threadfence_block();
