@@ -1586,16 +1586,22 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
   const int base = warp * kSlice;
   const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
   const uint32_t* mrow = mt.mask_on ? a.mask + static_cast<int64_t>(mt.row) * a.mask_stride : nullptr;
-  // the few hits: a compact loop that reloads the logit (still in cache)
-  auto take = [&](unsigned hm, int start) {
-    while (hm) {
-      const int b = __ffs(hm) - 1;
-      hm &= hm - 1u;
-      const int id = start + base + ((b >> 2) * 32 + lane) * 4 + (b & 3);
-      if (mrow && !((__ldcg(mrow + (id >> 5)) >> (id & 31)) & 1u)) continue;
-      const float x = to_f32<E>(rowp[id]);
-      const int i = atomicAdd(&ctl->cnt, 1);
-      if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+  // While the row streams, hits are only noted: a per-warp queue of
+  // (chunk, lane, 16-bit mask) words filled by a ballot, no atomics and no
+  // loads in the loop (either would hold up the loads in flight); the keys
+  // are built from the queue afterwards. The queue lives in the sort
+  // scratch of the warp-buffer area, free until the keys are sorted.
+  constexpr int kQcap = 512;
+  static_assert(2 * kNB * 8 + kCW * kQcap * 4 <= kCW * kWcap * 8, "collect queue");
+  uint32_t* wq = reinterpret_cast<uint32_t*>(smem_map().wbuf + 2 * kNB) + warp * kQcap;
+  int nq = 0;  // warp-uniform
+  auto note = [&](unsigned hm, int start) {
+    const unsigned ball = __ballot_sync(0xffffffffu, hm != 0u);
+    if (ball) {
+      const int j = nq + __popc(ball & ((1u << lane) - 1u));
+      if (hm && j < kQcap)
+        wq[j] = (static_cast<uint32_t>(start / kCE) << 21) | (static_cast<uint32_t>(lane) << 16) | hm;
+      nq += __popc(ball);
     }
   };
   if (!(xlo2 < xhi2)) {
@@ -1606,7 +1612,7 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
       for (int q = 0; q < 4; ++q)
 #pragma unroll
         for (int k = 0; k < 4; ++k) hm |= (v[q][k] >= xlo && v[q][k] < xhi) ? (1u << (q * 4 + k)) : 0u;
-      if (__any_sync(0xffffffffu, hm != 0u)) take(hm, start);
+      note(hm, start);
     });
   } else {
     // two bins (xhi <= xlo2): one compare against the lower edge, the exact
@@ -1624,9 +1630,27 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           hm |= ((v[q][k] >= xlo && v[q][k] < xhi) || (v[q][k] >= xlo2 && v[q][k] < xhi2)) ? (1u << (q * 4 + k)) : 0u;
-      if (__any_sync(0xffffffffu, hm != 0u)) take(hm, start);
+      note(hm, start);
     });
   }
+  __syncwarp();
+  // the queued hits: keys from (cached) reloads, one queue word per lane
+  for (int e = lane; e < min(nq, kQcap); e += 32) {
+    const uint32_t w = wq[e];
+    const int c = static_cast<int>(w >> 21), l = static_cast<int>((w >> 16) & 31u);
+    unsigned hm = w & 0xffffu;
+    while (hm) {
+      const int b = __ffs(hm) - 1;
+      hm &= hm - 1u;
+      const int id = c * kCE + base + ((b >> 2) * 32 + l) * 4 + (b & 3);
+      if (mrow && !((__ldcg(mrow + (id >> 5)) >> (id & 31)) & 1u)) continue;
+      const float x = to_f32<E>(rowp[id]);
+      const int i = atomicAdd(&ctl->cnt, 1);
+      if (i < kCollect) buf[i] = cand_key(x, static_cast<uint32_t>(id));
+    }
+  }
+  // a full queue (or a row too long for the chunk field) reports too many keys
+  if (lane == 0 && (nq > kQcap || spec_chunks(V) > 2048)) atomicMax(&ctl->cnt, kCollect + 1);
   cbar();
   const int n_all = ctl->cnt;
   if (ntab > 0 && n_all <= kCollect) {
