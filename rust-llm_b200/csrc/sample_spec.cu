@@ -3030,6 +3030,9 @@ __global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_con
     fence_mbar_init();
   }
   __syncthreads();
+  // a dependent finish grid may be scheduled as soon as resources free up
+  // (it waits for this grid's completion before reading its outputs)
+  if (SPLIT) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5;
   if (warp == kProdWarp) producer_loop<E>(a);
   else if (warp == kMetaWarp) meta_loop<E, SPLIT>(a);
@@ -3046,6 +3049,9 @@ __global__ void __launch_bounds__(kConsumers, 2) spec_finish_kernel(const __grid
   const int row = blockIdx.x;
   const int first_item = row * a.nseg;
   if (tid < 32) build_meta(a, first_item, sm.meta[0], sm.tab, true);
+  // the row's parameters come from the caller; everything below comes from
+  // the streaming kernel
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int s2 = tid; s2 < a.nseg; s2 += kConsumers) {
     const ItemSum* src = a.ws.sums + first_item + s2;
     ItemSum t;
@@ -3116,7 +3122,22 @@ static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t strea
   if (SPLIT) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    spec_finish_kernel<E><<<a.B, kConsumers, kOffStage, stream>>>(a);
+    // programmatic dependent launch: the finish kernel's CTAs are scheduled
+    // as the streaming kernel's CTAs retire and prepare their row while the
+    // last ones run; they read the streaming kernel's outputs only after
+    // the grid-dependency wait (which waits for that grid to complete)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(a.B));
+    cfg.blockDim = dim3(kConsumers);
+    cfg.dynamicSmemBytes = kOffStage;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, spec_finish_kernel<E>, a);
+    if (e != cudaSuccess) return e;
   }
   return cudaGetLastError();
 }
