@@ -1074,18 +1074,84 @@ __device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, u
 __device__ __noinline__ void block_sort_table(uint32_t* tab, int n) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x;
-  uint64_t* k64 = reinterpret_cast<uint64_t*>(sm.radix);
-  for (int i = tid; i < n; i += kConsumers) k64[i] = static_cast<uint64_t>(~tab[i]);
-  int P = 1;
-  while (P < n) P <<= 1;
-  cbar();
-  csort_desc(k64, n, P);
+  // Fast path: one counting pass into at most kCW * 256 id ranges, then
+  // each range (a few entries) put in order by one thread. A range with
+  // more than 64 entries (a history that repeats a few ids many times)
+  // takes the bitonic sort below instead.
+  {
+    constexpr int kBuckets = kCW * 256;
+    constexpr int BPT = kBuckets / kConsumers;
+    uint32_t mx = 0u;
+    for (int i = tid; i < n; i += kConsumers) mx = max(mx, tab[i]);
+    mx = static_cast<uint32_t>(cmax_u64(mx, sm.red));
+    int sh = 0;
+    while ((mx >> sh) >= static_cast<uint32_t>(kBuckets)) ++sh;
+    const int nb = static_cast<int>(mx >> sh) + 1;
+    uint32_t* cnt = sm.radix;                               // [nb] range sizes, then starts
+    uint32_t* tmp = reinterpret_cast<uint32_t*>(sm.wbuf);  // [kHmax] ids, [kHmax] ranks
+    for (int i = tid; i < nb; i += kConsumers) cnt[i] = 0u;
+    cbar();
+    for (int i = tid; i < n; i += kConsumers) {
+      const uint32_t id = tab[i];
+      tmp[i] = id;
+      tmp[kHmax + i] = atomicAdd(&cnt[id >> sh], 1u);
+    }
+    cbar();
+    uint32_t loc[BPT];
+    uint32_t sum = 0u, big = 0u;
 #pragma unroll
-  for (int r = 0; r < kHmax / kConsumers; ++r) {
-    const int p = tid + r * kConsumers;
-    if (p < n) tab[p] = ~static_cast<uint32_t>(k64[p]);
+    for (int r = 0; r < BPT; ++r) {
+      const int b = tid * BPT + r;
+      loc[r] = b < nb ? cnt[b] : 0u;
+      sum += loc[r];
+      big = max(big, loc[r]);
+    }
+    if (cmax_u64(big, sm.red) <= 64u) {
+      uint32_t run = cscan_u32(sum, sm.red) - sum;
+      uint32_t st[BPT];
+#pragma unroll
+      for (int r = 0; r < BPT; ++r) {
+        const int b = tid * BPT + r;
+        st[r] = run;
+        if (b < nb) cnt[b] = run;
+        run += loc[r];
+      }
+      cbar();
+      for (int i = tid; i < n; i += kConsumers) {
+        const uint32_t id = tmp[i];
+        tab[cnt[id >> sh] + tmp[kHmax + i]] = id;
+      }
+      cbar();
+      // insertion sort of this thread's ranges (sizes <= 64, mostly 0 or 1)
+#pragma unroll 1
+      for (int r = 0; r < BPT; ++r) {
+        uint32_t* t = tab + st[r];
+        for (int i = 1; i < static_cast<int>(loc[r]); ++i) {
+          const uint32_t x = t[i];
+          int j = i - 1;
+          while (j >= 0 && t[j] > x) {
+            t[j + 1] = t[j];
+            --j;
+          }
+          t[j + 1] = x;
+        }
+      }
+      cbar();
+    } else {
+      uint64_t* k64 = reinterpret_cast<uint64_t*>(sm.radix);
+      for (int i = tid; i < n; i += kConsumers) k64[i] = static_cast<uint64_t>(~tab[i]);
+      int P = 1;
+      while (P < n) P <<= 1;
+      cbar();
+      csort_desc(k64, n, P);
+#pragma unroll
+      for (int r = 0; r < kHmax / kConsumers; ++r) {
+        const int p = tid + r * kConsumers;
+        if (p < n) tab[p] = ~static_cast<uint32_t>(k64[p]);
+      }
+      cbar();
+    }
   }
-  cbar();
   uint32_t packed[kHmax / kConsumers];
 #pragma unroll
   for (int r = 0; r < kHmax / kConsumers; ++r) {
