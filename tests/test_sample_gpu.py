@@ -124,6 +124,27 @@ def test_small_shapes(sampler, case):
     compare(batch, run_gpu(sampler, batch), label=str(case))
 
 
+DEEP = [
+    # B, V, T, top_k, top_p, hist, scale, ties: full-vocabulary rows whose
+    # top-p cutoff lies far below the top-128 list (streamed histogram, one
+    # bin re-read with the draw bin predicted), a 1024-id history whose
+    # repeats overflow an id range of the counting sort, and rounded logits
+    # whose bins overflow the collect (exact radix walk)
+    (4, 128256, 1.3, 0, 0.9, 1024, 2.0, False),
+    (4, 128256, 0.8, 0, 0.97, 256, 3.0, False),
+    (3, 128256, 1.0, 0, 0.9, 64, 1.0, True),
+    (3, 128256, 1.0, 0, 1.0, 0, 2.0, False),
+]
+
+
+@pytest.mark.parametrize("case", DEEP, ids=lambda c: f"B{c[0]}_V{c[1]}_T{c[2]}_p{c[4]}_h{c[5]}_ties{int(c[7])}")
+def test_deep_top_p_rows(sampler, case):
+    B, V, T, k, tp, hl, scale, ties = case
+    rng = np.random.default_rng(hash(case) & 0xFFFFFFFF)
+    batch = make_batch(rng, B, V, T, k, tp, hl, None, scale=scale, ties=ties)
+    compare(batch, run_gpu(sampler, batch), label=str(case))
+
+
 def test_config2_rows(sampler):
     rows = list(range(0, 256, 16))
     total = 0
