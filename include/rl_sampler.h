@@ -92,11 +92,19 @@ rl_status rl_sample_batch(rl_sampler* h, const void* logits, rl_dtype dtype, int
                           float* out_prob, int32_t* row_status, void* stream);
 
 /*
- * Same as rl_sample_batch, and also writes each row's ordered top-k list
- * (ids and full-vocabulary probabilities, in (logit desc, id asc) order) for
- * inspection: list_ids / list_probs are [B, list_cap], list_len[B] gets
- * min(K, list_cap). Requires every row's K (top_k, or the allowed count when
- * top_k is off) to be <= 1024.
+ * Same as rl_sample_batch, and also writes, for inspection, what the
+ * reference's top_k_logits / sample_top_p (src/decoder.rs:112-144) would
+ * hold for each row, in (logit desc, id asc) order:
+ *  list_ids / list_probs [B, list_cap]: the top-k list (ids, full-vocabulary
+ *      probabilities); list_len[B] = min(K, list_cap) when the kernel holds
+ *      the whole list (K <= 128), else -1. K = top_k, or the allowed count
+ *      when top_k is off.
+ *  out_cut [B, 3] (nullable): K; the position in that order of the last
+ *      entry the top-k / top-p cutoff keeps; that entry's id (-2 when the
+ *      kernel does not resolve it: rows without a cutoff whose list is
+ *      longer than the kernel materialises). Together they fix the kept set
+ *      (every key at or above the last kept one). Debug launches also count
+ *      logits per histogram bin, so they run slower than rl_sample_batch.
  */
 rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtype, int B,
                                 int V, int64_t ld, const int32_t* hist, const int32_t* hist_len,
@@ -104,7 +112,7 @@ rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtyp
                                 const rl_row_params* params, const float* uniforms,
                                 int32_t* out_tok, float* out_prob, int32_t* row_status,
                                 int32_t* list_ids, float* list_probs, int32_t* list_len,
-                                int list_cap, void* stream);
+                                int list_cap, int32_t* out_cut, void* stream);
 
 /*
  * Host-buffer convenience wrapper of rl_sample_batch (f32 logits): copies the

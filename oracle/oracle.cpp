@@ -230,6 +230,7 @@ struct orc_spec_out {
   double cut_margin;   // min |cum - top_p| over the cumsums bracketing the cutoff
   double Z;
   float max_x;       // m (after penalties)
+  int32_t cut_id;    // id of the last kept entry (ids[cutoff])
 };
 
 int orc_spec_sample_row(const float* x_in, int V, const int32_t* hist, int hlen,
@@ -298,6 +299,7 @@ int orc_spec_sample_row(const float* x_in, int V, const int32_t* hist, int hlen,
     out->prob = 1.0f;
     out->K = 1;
     out->cutoff = 0;
+    out->cut_id = argmax;
     out->Z = 1.0;
     if (out_list_ids && list_cap > 0) {
       out_list_ids[0] = argmax;
@@ -369,6 +371,7 @@ int orc_spec_sample_row(const float* x_in, int V, const int32_t* hist, int hlen,
   out->prob = static_cast<float>((static_cast<double>(e[ids[j]]) / Z) / S);
   out->K = K;
   out->cutoff = cutoff;
+  out->cut_id = ids[cutoff];
   if (out_list_ids) {
     for (int t = 0; t < K && t < list_cap; ++t) {
       out_list_ids[t] = ids[t];

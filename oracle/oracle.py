@@ -51,6 +51,7 @@ class SpecOut(ctypes.Structure):
         ("cut_margin", ctypes.c_double),
         ("Z", ctypes.c_double),
         ("max_x", ctypes.c_float),
+        ("cut_id", ctypes.c_int32),
     ]
 
 
@@ -134,6 +135,7 @@ class SpecResult:
     max_x: float
     list_ids: np.ndarray
     list_p: np.ndarray
+    cut_id: int = -1
 
 
 def spec_sample_row(logits, hist, mask_row, params, u, list_cap=0) -> SpecResult:
@@ -150,7 +152,7 @@ def spec_sample_row(logits, hist, mask_row, params, u, list_cap=0) -> SpecResult
                                    float(u), ctypes.byref(out), _p(ids), _p(ps), list_cap)
     n = min(out.K, list_cap) if st == 0 else 0
     return SpecResult(st, out.token, out.prob, out.K, out.cutoff, out.draw_margin, out.cut_margin,
-                      out.Z, out.max_x, ids[:n].copy(), ps[:n].copy())
+                      out.Z, out.max_x, ids[:n].copy(), ps[:n].copy(), out.cut_id)
 
 
 def spec_sample_batch(logits, hist, hist_len, mask, params, uniforms, nthreads=1, dtype=0):

@@ -122,7 +122,7 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
                                float* out_prob, int32_t* row_status, int32_t* list_ids,
                                float* list_probs, int32_t* list_len, int list_cap, void* stream,
                                int vocab_offset, uint64_t* part_keys = nullptr,
-                               rl::PartStats* part_stats = nullptr) {
+                               rl::PartStats* part_stats = nullptr, int32_t* list_cut = nullptr) {
   if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: handle is NULL");
   if (B < 0 || V <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: B=%d V=%d", B, V);
   if (B == 0) return RL_OK;
@@ -164,6 +164,7 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.list_probs = list_probs;
   a.list_len = list_len;
   a.list_cap = list_cap;
+  a.list_cut = list_cut;
   a.vocab_offset = vocab_offset;
   a.part_keys = part_keys;
   a.part_stats = part_stats;
@@ -187,11 +188,12 @@ rl_status rl_sample_batch_debug(rl_sampler* h, const void* logits, rl_dtype dtyp
                                 int hist_stride, const uint32_t* mask, int64_t mask_stride,
                                 const rl_row_params* params, const float* uniforms, int32_t* out_tok,
                                 float* out_prob, int32_t* row_status, int32_t* list_ids,
-                                float* list_probs, int32_t* list_len, int list_cap, void* stream) {
+                                float* list_probs, int32_t* list_len, int list_cap, int32_t* out_cut,
+                                void* stream) {
   if (!list_len) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch_debug: list_len is NULL");
   return sample_common(h, logits, dtype, B, V, ld, hist, hist_len, hist_stride, mask, mask_stride, params,
                        uniforms, out_tok, out_prob, row_status, list_ids, list_probs, list_len, list_cap,
-                       stream, 0);
+                       stream, 0, nullptr, nullptr, out_cut);
 }
 
 rl_status rl_sample_partial(rl_sampler* h, const void* logits, rl_dtype dtype, int B, int V, int64_t ld,

@@ -46,8 +46,11 @@ __device__ __forceinline__ float ord_key_inv(uint32_t k) {
   return __uint_as_float(u);
 }
 // 64-bit sort key: larger key = earlier in (value desc, id asc) order.
+// -0.0 and +0.0 compare equal (IEEE, and the reference's partial_cmp), so
+// the value part is taken from x + 0 (which turns -0.0 into +0.0): equal
+// values then order by id alone.
 __device__ __forceinline__ uint64_t cand_key(float x, uint32_t id) {
-  return (static_cast<uint64_t>(ord_key(x)) << 32) | static_cast<uint64_t>(0xffffffffu - id);
+  return (static_cast<uint64_t>(ord_key(__fadd_rn(x, 0.0f))) << 32) | static_cast<uint64_t>(0xffffffffu - id);
 }
 __device__ __forceinline__ float key_val(uint64_t k) { return ord_key_inv(static_cast<uint32_t>(k >> 32)); }
 __device__ __forceinline__ uint32_t key_id(uint64_t k) {
@@ -77,16 +80,18 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 // Bounded wait on phase `parity`. Returns false when the budget expires.
+// Each try suspends the thread until the phase completes or a 20 us hint
+// runs out, so a waiting warp takes no issue slots from the working ones.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long budget_cycles) {
   const long long t0 = clock64();
   while (true) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(20000u)
         : "memory");
     if (done) return true;
     if (clock64() - t0 > budget_cycles) return false;

@@ -17,10 +17,11 @@ constexpr int kGNT = 256;
 
 // Packs (value, index) so that a larger u64 is the preferred candidate.
 // last_wins: ties prefer the larger index (greedy_sample); otherwise the
-// smaller index (sample_with_grammar).
+// smaller index (sample_with_grammar). -0.0 and +0.0 tie (v + 0 maps -0.0
+// to +0.0), as partial_cmp has them.
 __device__ __forceinline__ uint64_t pack_vi(float v, int i, bool last_wins) {
   const uint32_t lo = last_wins ? static_cast<uint32_t>(i) : 0xffffffffu - static_cast<uint32_t>(i);
-  return (static_cast<uint64_t>(ord_key(v)) << 32) | lo;
+  return (static_cast<uint64_t>(ord_key(__fadd_rn(v, 0.0f))) << 32) | lo;
 }
 
 __device__ __forceinline__ uint64_t block_max_u64(uint64_t v, uint64_t* red) {

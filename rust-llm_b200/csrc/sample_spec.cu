@@ -32,6 +32,7 @@
 // below the list, the merged histogram locates its bin and the row is
 // re-read for that bin's logits; an exact radix walk over re-reads of the
 // row covers what the histogram cannot.
+#include <atomic>
 #include <climits>
 
 #include "common.cuh"
@@ -162,8 +163,11 @@ static_assert(kOffRadix + kCW * 256 * 4 - kOffHist >= kCollect * 8, "collect buf
 static_assert(kCW * kWcap * 8 >= 2 * kNB * 8, "merged histogram");
 static_assert(256 * (4 + 8 + 8) <= kCW * 256 * 4, "radix walk bins");
 static_assert(kCW * kWcap >= 2 * kNB + 8 * kConsumers && kCollect <= 8 * kConsumers, "sort scratch");
+static_assert(kCW * kN <= 4 * kConsumers && kCW * kN * 8 <= kCW * 256 * 4, "item-end sort of the kept keys");
 static_assert(sizeof(ItemMeta) <= 128 && sizeof(Ctl) <= 128 && sizeof(Red) <= 256, "smem header");
+static_assert(3 * kNS + 4 <= 16, "mbarriers");
 static_assert(kOffMeta + 2 * 128 <= kOffTopE, "meta");
+static_assert(kOffWcnt + 32 + kCW * 8 <= kOffMeta && (kOffWcnt + 32) % 8 == 0, "per-warp counts and histogram totals");
 static_assert(kOffStage % 128 == 0 && kOffMask % 16 == 0 && kOffSumS % 8 == 0 && kOffHist % 16 == 0, "alignment");
 static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
 
@@ -1040,9 +1044,12 @@ __device__ __noinline__ void producer_loop(const SpecArgs& a) {
 // ---------------------------------------------------------------------------
 // Row-preparation warp
 // ---------------------------------------------------------------------------
-// The row's history ids in [0, V), in history order, into tab (the
-// consumers sort them when the item starts). Returns the count.
-__device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, uint32_t* tab) {
+// The row's history ids in [lo, hi) (row-local ids), in history order, into
+// tab. Returns the count. PRE: the row's first 512 entries are in pre[]
+// already (lane l holds entries r * 32 + l).
+template <bool PRE>
+__device__ __forceinline__ int gather_history_impl(const SpecArgs& a, int row, int hl, uint32_t* tab, int lo, int hi,
+                                                   const int (&pre)[16]) {
   const int lane = threadIdx.x & 31;
   const int32_t* h = a.hist + static_cast<int64_t>(row) * a.hist_stride;
   int n = 0;
@@ -1052,13 +1059,13 @@ __device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, u
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       const int i = g0 + r * 32 + lane;
-      ids[r] = i < hl ? __ldg(h + i) : -1;
+      ids[r] = (PRE && g0 == 0) ? pre[r] : (i < hl ? __ldg(h + i) : -1);
     }
 #pragma unroll
     for (int r = 0; r < 16; ++r) {
       const int i = g0 + r * 32 + lane;
       const int id = ids[r] - a.vocab_offset;
-      const bool ok = i < hl && id >= 0 && id < a.V;
+      const bool ok = i < hl && id >= lo && id < hi;
       const unsigned b = __ballot_sync(0xffffffffu, ok);
       if (ok) tab[n + __popc(b & ((1u << lane) - 1u))] = static_cast<uint32_t>(id);
       n += __popc(b);
@@ -1066,6 +1073,10 @@ __device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, u
   }
   __syncwarp();
   return n;
+}
+__device__ __noinline__ int gather_history(const SpecArgs& a, int row, int hl, uint32_t* tab, int lo, int hi) {
+  const int none[16] = {};
+  return gather_history_impl<false>(a, row, hl, tab, lo, hi, none);
 }
 
 // Consumers: sorts the raw history ids tab[0, n) (n <= kHmax) with the
@@ -1248,10 +1259,22 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
   const int S = spec_chunks(a.V);
   const int row = item / a.nseg;
   const int seg = item - row * a.nseg;
-  // every global read of the row issued up front
+  // every global read of the row issued up front: parameters, the first
+  // 512 history entries (entries past hist_len are read but not used) and
+  // the allowed mask, in one round trip
   const rl_row_params prm = a.params[row];
   const float u = a.uniforms[row];
   const int hl_raw = a.hist ? a.hist_len[row] : 0;
+  int pre[16];
+  {
+    const int hs = a.hist ? min(a.hist_stride, kHmax) : 0;
+    const int32_t* h = a.hist + static_cast<int64_t>(row) * a.hist_stride;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      const int i = r * 32 + lane;
+      pre[r] = (!defer_tab && i < hs) ? __ldg(h + i) : -1;
+    }
+  }
   const float T = prm.temperature;
   int mode;
   if (!(fabsf(T) < RL_POS_INF) || !(T > 0.0f)) mode = 0;  // greedy; a non-finite T is reported at the end
@@ -1262,12 +1285,41 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
   if (a.mask) {
     const uint32_t* mrow = a.mask + static_cast<int64_t>(row) * a.mask_stride;
     const int nw = (a.V + 31) >> 5;
+    const int nfull = a.V >> 5;  // words with no bit past the row end
     uint32_t any = 0u;
-    for (int w = lane; w < nw; w += 32) {
-      uint32_t bits = __ldg(mrow + w);
-      const int rem = a.V - w * 32;
-      if (rem < 32) bits &= (1u << rem) - 1u;
-      any |= bits;
+    if ((reinterpret_cast<uintptr_t>(mrow) & 15u) == 0) {
+      // 16-byte loads, eight in flight per lane
+      const uint4* m4 = reinterpret_cast<const uint4*>(mrow);
+      const int n4 = nfull >> 2;
+      for (int w0 = 0; w0 < n4; w0 += 256) {
+        uint4 q[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int w = w0 + r * 32 + lane;
+          q[r] = w < n4 ? __ldg(m4 + w) : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) any |= q[r].x | q[r].y | q[r].z | q[r].w;
+      }
+      for (int w = (n4 << 2) + lane; w < nw; w += 32) {
+        uint32_t bits = __ldg(mrow + w);
+        const int rem = a.V - w * 32;
+        if (rem < 32) bits &= (1u << rem) - 1u;
+        any |= bits;
+      }
+    } else {
+      for (int w0 = 0; w0 < nw; w0 += 256) {
+        uint32_t q[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const int w = w0 + r * 32 + lane;
+          q[r] = w < nw ? __ldg(mrow + w) : 0u;
+          const int rem = a.V - w * 32;
+          if (w < nw && rem < 32) q[r] &= (1u << rem) - 1u;
+        }
+#pragma unroll
+        for (int r = 0; r < 8; ++r) any |= q[r];
+      }
     }
     mask_on = __any_sync(0xffffffffu, any != 0u) ? 1 : 0;
   }
@@ -1276,7 +1328,7 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
   int ntab = 0;
   if (a.hist && pen) {
     const int hl = max(0, min(hl_raw, min(a.hist_stride, kHmax)));
-    if (hl > 0) ntab = defer_tab ? -hl : gather_history(a, row, hl, tab);
+    if (hl > 0) ntab = defer_tab ? -hl : gather_history_impl<true>(a, row, hl, tab, 0, a.V, pre);
   }
   // Histogram window depth W (nats below the anchor): the mass below it is
   // at most V e^-W of the row max, kept under a quarter of the tail mass
@@ -1300,7 +1352,9 @@ __device__ __noinline__ void build_meta(const SpecArgs& a, int item, ItemMeta& m
     mt.c1 = min(S, mt.c0 + a.cps);
     mt.mode = mode;
     mt.nkeep = mode == 1 ? prm.top_k : kN;
-    mt.need_count = (mode == 2 && prm.top_k > 0) ? 1 : 0;
+    // bins count logits too where a position is needed: top_k beyond the
+    // list, or a debug launch reporting the cutoff position
+    mt.need_count = (mode == 2 && (prm.top_k > 0 || a.list_cut != nullptr)) ? 1 : 0;
     mt.mask_on = mask_on;
     mt.ntab = ntab;
     mt.wbins = wbins;
@@ -1320,15 +1374,17 @@ __device__ __noinline__ void meta_loop(const SpecArgs& a) {
   const Smem sm = smem_map();
   const int lane = threadIdx.x & 31;
   const int S = spec_chunks(a.V);
-  int mseq = 0, cseq = 0;
-  for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
+  int cseq = 0;
+  for (int mseq = 0;; ++mseq) {
     const int slot = mseq & 1;
+    ItemMeta& mt = sm.meta[slot];
+    const int item = blockIdx.x + mseq * gridDim.x;
+    if (item >= a.nitems) return;
     if (!mbar_wait(&sm.mempty[slot], static_cast<uint32_t>(((mseq >> 1) & 1) ^ 1), kWaitBudget) ||
         *reinterpret_cast<volatile int*>(&sm.ctl->abort)) {
       if (lane == 0) atomicExch(&sm.ctl->abort, 1);
       return;
     }
-    ItemMeta& mt = sm.meta[slot];
     uint32_t* tab = sm.tab + slot * kHmax;
     build_meta(a, item, mt, tab, false);
     __syncwarp();
@@ -1893,7 +1949,7 @@ __device__ __noinline__ void lazy_table(const SpecArgs& a, const ItemMeta& mt, c
     return;
   }
   if (threadIdx.x < 32) {
-    const int n = gather_history(a, m.row, hl, tab);
+    const int n = gather_history(a, m.row, hl, tab, 0, a.V);
     if (threadIdx.x == 0) m.ntab = n;
   }
   cbar();
@@ -1963,6 +2019,11 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
   if (status != 0 || mt.mode == 0) {
     if (tid == 0) {
       write_row(a, row, status, argmax, 1.0f);
+      if (a.list_cut) {
+        a.list_cut[static_cast<int64_t>(row) * 3 + 0] = status == 0 ? 1 : 0;
+        a.list_cut[static_cast<int64_t>(row) * 3 + 1] = status == 0 ? 0 : -1;
+        a.list_cut[static_cast<int64_t>(row) * 3 + 2] = status == 0 ? argmax + a.vocab_offset : -1;
+      }
       if (want_list) {
         const bool ok = status == 0 && a.list_cap > 0;
         a.list_len[row] = ok ? 1 : 0;
@@ -2080,10 +2141,16 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
   int token = -1, st = 0;
   float prob = 0.0f;
   bool done = false;
+  // position of the last kept entry in list order and its id (debug
+  // launches; -2: the id is not resolved)
+  long long dbg_pos = -1;
+  int dbg_id = -2;
   // cutoff inside the complete prefix
   const int cut = cmin_i(
       (tid < complete && (tid == K - 1 || (mass_mode && sm.topc[tid] >= pd))) ? tid : INT_MAX, rs);
   if (cut != INT_MAX) {
+    dbg_pos = cut;
+    dbg_id = static_cast<int>(key_id(sm.top[cut]));
     const double Sx = sm.topc[cut];
     const double tgt = ud * Sx;
     int d = cmin_i((tid <= cut && sm.topc[tid] > tgt) ? tid : INT_MAX, rs);
@@ -2093,6 +2160,8 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
     done = true;
   } else if (!mass_mode && !count_mode) {
     // the list is every allowed id: S is the whole mass (1)
+    dbg_pos = K - 1;
+    dbg_id = (nt == nallow && nt > 0) ? static_cast<int>(key_id(sm.top[nt - 1])) : -2;
     const int d = cmin_i((tid < complete && sm.topc[tid] > ud) ? tid : INT_MAX, rs);
     if (d != INT_MAX) {
       token = static_cast<int>(key_id(sm.top[d]));
@@ -2109,16 +2178,22 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
     bool hist_ok = mt.mode == 2 && nt > 0;
     int A_hi = 0, A_lo = INT_MIN;
     if (hist_ok) {
+      // Logits above the list's last bin A_hi are all in the list. Below it
+      // every segment's histogram must be complete: its window reaches up to
+      // A_hi, or its maximum lies inside its window (segments later in a row
+      // anchor lower, and hold nothing above their window top then).
       A_hi = static_cast<int>(amin);
-      int atop_min = INT_MAX;
       for (int s = 0; s < nseg; ++s) {
         const ItemSum& q = sm.sums[s];
         if (q.nallow == 0) continue;
-        if (q.atop == kNoAnchor || (q.flags & kFlagHistBad)) hist_ok = false;
+        if (q.atop == kNoAnchor || (q.flags & kFlagHistBad)) {
+          hist_ok = false;
+          continue;
+        }
         A_lo = max(A_lo, q.wlo);
-        atop_min = min(atop_min, q.atop);
+        if (q.atop < A_hi && static_cast<int>(bin_of(q.m, rt)) > q.atop) hist_ok = false;
       }
-      if (A_hi > atop_min || A_hi < A_lo || A_hi - A_lo >= kNB) hist_ok = false;
+      if (A_hi < A_lo || A_hi - A_lo >= kNB) hist_ok = false;
     }
     bool resolved = false;
     if (hist_ok) {
@@ -2261,6 +2336,8 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
           Sx = cum_at;
           bm_cut = mb;
           cut_ok = true;
+          dbg_pos = cb + g;  // exact when the bins carry counts (debug launches)
+          dbg_id = static_cast<int>(key_id(buf[off1 + g]));
         } else {
           // the histogram overstated this bin: continue with its exact mass
           corr += (run_end - mb) - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
@@ -2271,6 +2348,8 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       if (!cut_ok && !mass_mode && !count_mode) {
         cut_ok = true;  // no cutoff: S is the whole mass
         Sx = 1.0;
+        dbg_pos = K - 1;
+        dbg_id = -2;
       }
       if (cut_ok) {
         const double tgt = ud * Sx;
@@ -2300,7 +2379,8 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
               kb = buf;
               kn = n2;
             } else if (held != f) {
-              const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), __int_as_float(0x7fc00000), buf, ctl);
+              const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
+                                                     __int_as_float(0x7fc00000), buf, ctl);
               if (ntot > kCollect) break;
               csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
               held = f;
@@ -2342,6 +2422,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
           kc = kk;
           Sx_e = mb1 + static_cast<double>(exact_e(key_val(kk), M, rt));
           have_cut = true;
+          dbg_pos = cb1;
         }
       }
       if (mass_mode) {
@@ -2350,7 +2431,14 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
           kc = kp;
           Sx_e = mb2 + static_cast<double>(exact_e(key_val(kp), M, rt));
           have_cut = true;
+          dbg_pos = cb2;
         }
+      }
+      if (have_cut) {
+        dbg_id = static_cast<int>(key_id(kc));
+      } else {
+        dbg_pos = K - 1;
+        dbg_id = -2;
       }
       if (!have_cut) {
         long long cbt;
@@ -2370,7 +2458,14 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       }
     }
   }
-  if (tid == 0) write_row(a, row, st, token, prob);
+  if (tid == 0) {
+    write_row(a, row, st, token, prob);
+    if (a.list_cut) {
+      a.list_cut[static_cast<int64_t>(row) * 3 + 0] = st == 0 ? K : 0;
+      a.list_cut[static_cast<int64_t>(row) * 3 + 1] = st == 0 ? static_cast<int>(dbg_pos) : -1;
+      a.list_cut[static_cast<int64_t>(row) * 3 + 2] = (st == 0 && dbg_id >= 0) ? dbg_id + a.vocab_offset : dbg_id;
+    }
+  }
 }
 
 // Per-thread accumulators of an item, handed to its end.
@@ -2419,12 +2514,15 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
       wcnt = nkeep;
       if (lane == 0) atomicMax(tsh, static_cast<unsigned long long>(T));
     }
+    cbar();
+    // every bound is in: each warp keeps its keys >= the item's bound (<= nkeep)
+    wcnt = warp_filter(wbuf, wcnt, sm.ctl->tau_shared);
   }
-  cbar();
-  // every bound is in: each warp keeps its keys >= the item's bound (<= nkeep)
-  if (mode != 0) wcnt = warp_filter(wbuf, wcnt, sm.ctl->tau_shared);
-  // ---- reductions, round 1: max, allowed count, flags, mass sums ----
+  // ---- one reduction round: per warp its max, allowed count, flags, mass
+  // sums, and its softmax sum relative to its own max (sampled rows) or its
+  // argmax (greedy rows); thread 0 combines the warps ----
   Red* rs = sm.red;
+  unsigned long long* wq2 = reinterpret_cast<unsigned long long*>(sm.wcnt + 8);  // per-warp histogram totals
   {
     const float wm = warp_max(m_run);
     const int wn = warp_sum_i(nal);
@@ -2437,12 +2535,26 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
       q += __shfl_xor_sync(0xffffffffu, q, o);
       bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
     }
+    double wz = 0.0;
+    if (mode == 0) {
+      int wa = (m_run == wm && wm > RL_NEG_INF) ? arg_run : INT_MAX;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wa = min(wa, __shfl_xor_sync(0xffffffffu, wa, o));
+      wz = static_cast<double>(wa);
+    } else {
+      double zl = 0.0;
+      if (zref > RL_NEG_INF && wm > RL_NEG_INF)
+        zl = static_cast<double>(zs) *
+             exp2((static_cast<double>(zref) - static_cast<double>(wm)) * (kLog2e / static_cast<double>(rt.T)));
+      wz = warp_sum_d(zl);
+    }
     if (lane == 0) {
       rs->f[warp] = wm;
       rs->i[warp] = wn;
       rs->u[warp] = wf;
       rs->q[warp] = q;
-      rs->d[warp] = static_cast<double>(bsum);  // < 2^53: exact
+      rs->d[warp] = wz;
+      wq2[warp] = bsum;
       sm.wcnt[warp] = wcnt;
     }
   }
@@ -2450,82 +2562,60 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
   float m_item = RL_NEG_INF;
   int nallow = 0;
   uint32_t fl = 0u;
-  unsigned long long tq = 0ull;
-  double tb = 0.0;
+  unsigned long long tq = 0ull, tb = 0ull;
 #pragma unroll
   for (int w = 0; w < kCW; ++w) {
     m_item = fmaxf(m_item, rs->f[w]);
     nallow += rs->i[w];
     fl |= rs->u[w];
     tq += rs->q[w];
-    tb += rs->d[w];
+    tb += wq2[w];
   }
   const int badf = fl & 1u, tmof = (fl >> 1) & 1u;
-  // the warps' kept keys, flattened into the (free) radix area
-  uint64_t* flat = reinterpret_cast<uint64_t*>(sm.radix);
-  int total = 0;
+  int argmax = INT_MAX;
+  double z_item = 0.0;
+  if (tid == 0) {
+    // (only thread 0 writes the item's summary)
+#pragma unroll
+    for (int w = 0; w < kCW; ++w) {
+      const float wm = rs->f[w];
+      if (mode == 0) {
+        if (wm == m_item && m_item > RL_NEG_INF) argmax = min(argmax, static_cast<int>(rs->d[w]));
+      } else if (wm > RL_NEG_INF) {
+        z_item += rs->d[w] * exp2((static_cast<double>(wm) - static_cast<double>(m_item)) *
+                                  (kLog2e / static_cast<double>(rt.T)));
+      }
+    }
+  }
+  int hflags = 0;
+  if (mode == 2 && (tq != tb || !hist_on)) hflags = kFlagHistBad;
+  int ncand = 0;
   if (mode != 0) {
-    int off = 0;
+    // the warps' kept keys, flattened into the (free) radix area
+    uint64_t* flat = reinterpret_cast<uint64_t*>(sm.radix);
+    int total = 0, off = 0;
 #pragma unroll
     for (int w = 0; w < kCW; ++w) {
       if (w < warp) off += sm.wcnt[w];
       total += sm.wcnt[w];
     }
     for (int i = lane; i < wcnt; i += 32) flat[off + i] = wbuf[i];
-  }
-  cbar();
-  // ---- round 2: argmax (greedy) or Z relative to the item max ----
-  int argmax = INT_MAX;
-  double z_item = 0.0;
-  {
-    int wa = INT_MAX;
-    double zl = 0.0;
-    if (mode == 0) {
-      wa = (m_run == m_item && m_item > RL_NEG_INF) ? arg_run : INT_MAX;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) wa = min(wa, __shfl_xor_sync(0xffffffffu, wa, o));
-    } else {
-      if (zref > RL_NEG_INF && m_item > RL_NEG_INF)
-        zl = static_cast<double>(zs) *
-             exp2((static_cast<double>(zref) - static_cast<double>(m_item)) * (kLog2e / static_cast<double>(rt.T)));
-      zl = warp_sum_d(zl);
-      zl = __shfl_sync(0xffffffffu, zl, 0);
-    }
-    if (lane == 0) {
-      rs->i[warp] = wa;
-      rs->d[warp] = zl;
-    }
-  }
-  cbar();
-#pragma unroll
-  for (int w = 0; w < kCW; ++w) {
-    argmax = min(argmax, rs->i[w]);
-    z_item += rs->d[w];
-  }
-  int hflags = 0;
-  if (mode == 2 && (static_cast<double>(tq) != tb || !hist_on)) hflags = kFlagHistBad;
-  int ncand = 0;
-  if (mode != 0) {
+    cbar();
     const int need = min(total, nkeep);
-    if (need > 0) {
-      // rank of each key (distinct keys: the count of greater ones), one key
-      // per thread; the first need go to sm.top in order
-      for (int t = tid; t < total; t += kConsumers) {
-        const uint64_t key = flat[t];
-        int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
-        int j = 0;
-        for (; j + 4 <= total; j += 4) {
-          r0 += flat[j] > key ? 1 : 0;
-          r1 += flat[j + 1] > key ? 1 : 0;
-          r2 += flat[j + 2] > key ? 1 : 0;
-          r3 += flat[j + 3] > key ? 1 : 0;
-        }
-        for (; j < total; ++j) r0 += flat[j] > key ? 1 : 0;
-        const int rank = (r0 + r1) + (r2 + r3);
-        if (rank < need) sm.top[rank] = key;
-      }
+    if (need > 0 && total <= kN) {
+      // few keys: sorted in registers, in place
+      csort_desc(flat, total, pow2_at_least(total));
+      for (int t = tid; t < need; t += kConsumers) sm.top[t] = flat[t];
       cbar();
       ncand = need;
+    } else if (need > 0) {
+      // the need-th largest by a radix select over the kept keys, then
+      // only the keys at or above it sorted
+      if (tid == 0) sm.segn[0] = total;
+      cbar();
+      const uint64_t T = block_select<false>(flat, 1, total, sm.segn, need, reinterpret_cast<uint32_t*>(sm.wbuf),
+                                             rs, sm.ctl);
+      ncand = gather_sorted<false>(flat, 1, total, sm.segn, T, sm.top, sm.ctl);
     }
   }
   ItemSum is;
@@ -2582,16 +2672,18 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
         if (mt.need_count) gk[i] = sm.hcnt[i];
       }
     }
-    __threadfence();
+    // the CTA's writes are ordered before the barrier; one thread's fence
+    // then publishes them at device scope before the arrival
     cbar();
     if (tid == 0) {
+      __threadfence();
       const int prev = atomicAdd(&a.ws.row_done[row], 1);
+      __threadfence();
       sm.ctl->is_last = (prev == a.nseg - 1) ? 1 : 0;
     }
     cbar();
     run_finisher = sm.ctl->is_last != 0;
     if (run_finisher) {
-      __threadfence();
       for (int s2 = tid; s2 < a.nseg; s2 += kConsumers) {
         const ItemSum* src = a.ws.sums + first_item + s2;
         ItemSum t;
@@ -2701,8 +2793,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   if constexpr (MODE != 0 && es == 4) {
     // bound from the item's first chunk (f32, whole in the stage, no mask):
     // its nkeep-th largest penalised value over all kCE logits, so that the
-    // item appends about nkeep ln(n / kCE) keys in all (the loop below has
-    // no calls)
+    // item appends about nkeep ln(n / kCE) keys in all
     const int start = mt.c0 * kCE;
     const int len = min(kCE, V - start);
     const int nfast = row_al ? ((len * es) & ~15) / es : 0;
@@ -2730,7 +2821,8 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       const float t0 = block_kth_stage(f, nkeep, sm.radix, sm.red, sm.ctl);
       if (t0 > tau_v) {
         tau_v = t0;
-        tau = static_cast<uint64_t>(ord_key(t0)) << 32;  // every logit equal to t0 is kept
+        // every logit equal to t0 is kept (the key of +0.0 for a zero bound)
+        tau = static_cast<uint64_t>(ord_key(__fadd_rn(t0, 0.0f))) << 32;
         if (tid == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
       }
     }
@@ -2932,26 +3024,38 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
         tau_v = key_val(ts);
       }
       if (__any_sync(0xffffffffu, lm > RL_NEG_INF && lm >= tau_v)) {
-        // every slot statically indexed (no register-array indexing); the
-        // takers reserve buffer places with a per-warp shared counter
-        int* wc = sm.wcnt + warp;
+        // the lane's takers as a 16-bit mask (every slot statically
+        // indexed), their places in the warp's buffer from a warp scan of
+        // the counts: no atomics
+        unsigned hm = 0u;
 #pragma unroll
         for (int q = 0; q < 4; ++q)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const float x = v[q][k];
-            if (x > RL_NEG_INF && x >= tau_v) {
-              const uint32_t id = static_cast<uint32_t>(start + base + (q * 32 + lane) * 4 + k);
-              const uint64_t key = cand_key(x, id);
-              if (x > tau_v || key >= tau) {
-                const int idx = atomicAdd(wc, 1);
-                if (idx < kWcap) wbuf[idx] = key;
-                else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
-              }
-            }
+            bool take = x > RL_NEG_INF && x >= tau_v;
+            if (take && !(x > tau_v))
+              take = cand_key(x, static_cast<uint32_t>(start + base + (q * 32 + lane) * 4 + k)) >= tau;
+            hm |= take ? (1u << (q * 4 + k)) : 0u;
           }
+        const int nh = __popc(hm);
+        int inc = nh;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int t = __shfl_up_sync(0xffffffffu, inc, o);
+          if (lane >= o) inc += t;
+        }
+        int idx = wcnt + inc - nh;
+        wcnt += __shfl_sync(0xffffffffu, inc, 31);
+        while (hm) {
+          const int b = __ffs(hm) - 1;
+          hm &= hm - 1u;
+          const uint64_t key = cand_key(pick16(v, b), static_cast<uint32_t>(start + base + ((b >> 2) * 32 + lane) * 4 + (b & 3)));
+          if (idx < kWcap) wbuf[idx] = key;
+          else __stcg(reinterpret_cast<unsigned long long*>(gov + (idx - kWcap)), key);
+          ++idx;
+        }
         __syncwarp();
-        wcnt = *reinterpret_cast<volatile int*>(wc);
       }
     }
     // ---- windowed histogram ----
@@ -3028,8 +3132,10 @@ template <typename E, bool SPLIT>
 __device__ __noinline__ void consumer_loop(const SpecArgs& a) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x;
-  int cseq = 0, mseq = 0;
-  for (int item = blockIdx.x; item < a.nitems; item += gridDim.x, ++mseq) {
+  int cseq = 0;
+  for (int mseq = 0;; ++mseq) {
+    const int item = blockIdx.x + mseq * gridDim.x;
+    if (item >= a.nitems) return;
     const int slot = mseq & 1;
     const bool timeout = !mbar_wait(&sm.mfull[slot], static_cast<uint32_t>((mseq >> 1) & 1), kWaitBudget);
     if (cor_i(timeout || *reinterpret_cast<volatile int*>(&sm.ctl->abort), sm.red)) {
@@ -3169,20 +3275,22 @@ void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas) {
   *nctas = max(1, min(B * ns, slots));
 }
 
-int spec_max_ws_items(int num_sms) { return 2 * (2 * num_sms); }
+int spec_max_ws_items(int num_sms, int max_batch) { return max(2 * (2 * num_sms), max_batch); }
 
 template <typename E, bool SPLIT>
 static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t stream) {
-  static int configured[64] = {0};
+  // the kernels' shared-memory limit, set once per device (a per-device
+  // flag read and written atomically: several host threads may launch)
+  static std::atomic<int> configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  if (dev < 0 || dev >= 64 || !configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e =
         cudaFuncSetAttribute(spec_pipe_kernel<E, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (e == cudaSuccess && SPLIT)
       e = cudaFuncSetAttribute(spec_finish_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, kOffStage);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) configured[dev] = 1;
+    if (dev >= 0 && dev < 64) configured[dev].store(1, std::memory_order_release);
   }
   spec_pipe_kernel<E, SPLIT><<<nctas, kThreads, kSmemBytes, stream>>>(a);
   if (SPLIT) {

@@ -96,6 +96,7 @@ struct SpecArgs {
   float* list_probs;
   int32_t* list_len;
   int list_cap;
+  int32_t* list_cut;  // [B, 3] debug: K, position of the last kept entry, its id
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
   uint64_t* part_keys;   // non-null: partial launch, no draw (see PartStats)
   PartStats* part_stats;
@@ -146,10 +147,11 @@ __host__ __device__ inline int spec_chunks(int V) { return (V + kCE - 1) / kCE; 
 // Segments per row, chunks per segment and CTAs for a batch (host side).
 void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas);
 // Items of the largest launch that uses the workspace (more than one segment).
-int spec_max_ws_items(int num_sms);
+int spec_max_ws_items(int num_sms, int max_batch);
 // CTAs of the largest launch (the per-warp overflow areas).
 inline int spec_max_ctas(int num_sms) { return 2 * num_sms; }
 cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream);
+
 // One segment per row (no per-item workspace: only ws.wovf is used), at most
 // max_ctas CTAs (the persistent CTAs loop over the rows).
 cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream);

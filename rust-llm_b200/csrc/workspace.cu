@@ -26,7 +26,7 @@ rl_status alloc_workspace(rl_sampler* h) {
   // spec kernel workspace: per-item summaries, candidate lists and
   // histograms that the streaming kernel hands to the finish kernel (one
   // item per row, or up to spec_max_ws_items segments of small batches)
-  const size_t items = static_cast<size_t>(max(spec_max_ws_items(h->num_sms), h->max_batch));
+  const size_t items = static_cast<size_t>(spec_max_ws_items(h->num_sms, h->max_batch));
   h->ws.max_items = static_cast<int>(items);
   ok = ok && dalloc(&h->ws.row_done, B) && dalloc(&h->ws.sums, items) && dalloc(&h->ws.cands, items * kN) &&
        dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&

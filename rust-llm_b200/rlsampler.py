@@ -94,7 +94,7 @@ def lib():
         L.rl_sample_batch.argtypes = [P, P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P]
         L.rl_sample_batch_debug.restype = I
         L.rl_sample_batch_debug.argtypes = [P, P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P,
-                                            P, P, I, P]
+                                            P, P, I, P, P]
         L.rl_sample_batch_static.restype = I
         L.rl_sample_batch_static.argtypes = [P, I, I, I, I64, P, P, I, P, I64, P, P, P, P, P, P]
         L.rl_sample_host.restype = I
@@ -198,14 +198,15 @@ class Sampler:
         list_ids = torch.full((B, list_cap), -1, dtype=torch.int32, device=dev)
         list_probs = torch.zeros((B, list_cap), dtype=torch.float32, device=dev)
         list_len = torch.zeros(B, dtype=torch.int32, device=dev)
+        cut = torch.full((B, 3), -3, dtype=torch.int32, device=dev)
         hs = hist.shape[1] if hist is not None else 0
         ms = mask.shape[1] if mask is not None else 0
         check(lib().rl_sample_batch_debug(self.h, _ptr(logits), dtype, B, V, logits.stride(0), _ptr(hist),
                                           _ptr(hist_len), hs, _ptr(mask), ms, _ptr(params), _ptr(uniforms),
                                           _ptr(out_tok), _ptr(out_prob), _ptr(row_status), _ptr(list_ids),
-                                          _ptr(list_probs), _ptr(list_len), list_cap, _stream(stream)),
+                                          _ptr(list_probs), _ptr(list_len), list_cap, _ptr(cut), _stream(stream)),
               "rl_sample_batch_debug")
-        return out_tok, out_prob, row_status, list_ids, list_probs, list_len
+        return out_tok, out_prob, row_status, list_ids, list_probs, list_len, cut
 
     # -- vocabulary shards -------------------------------------------------------
     def sample_partial(self, logits, vocab_offset, params, hist=None, hist_len=None, mask=None, out_keys=None,

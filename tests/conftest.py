@@ -1,3 +1,4 @@
+import json
 import os
 import sys
 
@@ -32,3 +33,23 @@ def pytest_collection_modifyitems(config, items):
     for it in items:
         if "gpu" in it.keywords:
             it.add_marker(skip)
+
+
+# Parity counters of the -m gpu tests, per workload: rows compared, tokens
+# equal, boundary cases (the oracle's draw or cutoff within 1e-6 of a CDF
+# boundary, where the token may differ), kept-set checks. Written as JSON to
+# $RL_PARITY_OUT at the end of the session when that variable is set.
+PARITY = {}
+
+
+def parity_add(key, **counts):
+    d = PARITY.setdefault(key, {})
+    for k, v in counts.items():
+        d[k] = d.get(k, 0) + int(v)
+
+
+def pytest_sessionfinish(session, exitstatus):
+    out = os.environ.get("RL_PARITY_OUT")
+    if out and PARITY:
+        with open(out, "w") as f:
+            json.dump({"exitstatus": int(exitstatus), "workloads": PARITY}, f, indent=1, sort_keys=True)

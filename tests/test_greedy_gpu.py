@@ -64,3 +64,20 @@ def test_grammar_greedy_config3(sampler):
     got = _run(sampler, b.logits, b.mask)
     want = [oracle.grammar_greedy(b.logits[i], b.mask[i]) for i in range(b.logits.shape[0])]
     assert list(got) == want
+
+
+def test_signed_zero_ties(sampler):
+    """-0.0 and +0.0 tie (Rust's partial_cmp); greedy keeps the last of them,
+    the grammar path the lowest allowed id."""
+    V = 4099
+    rng = np.random.default_rng(99)
+    x = -np.abs(rng.normal(1.0, 1.0, (8, V))).astype(np.float32) - np.float32(0.5)
+    for b in range(8):
+        pos = rng.choice(V, 6, replace=False)
+        x[b, pos[:3]] = np.float32(0.0)
+        x[b, pos[3:]] = np.float32(-0.0)
+    got = _run(sampler, x)
+    assert list(got) == [oracle.greedy(x[b]) for b in range(8)]
+    mask = workloads.mask_from_allowed(V, [np.arange(V)] * 8)
+    got = _run(sampler, x, mask)
+    assert list(got) == [oracle.grammar_greedy(x[b], mask[b]) for b in range(8)]

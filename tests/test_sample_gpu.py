@@ -1,23 +1,31 @@
-"""Parity of the CUDA spec sampler (rl_sample_batch, through the C ABI) with
-the CPU oracle on identical seeded inputs.
+"""Parity of the CUDA spec sampler (rl_sample_batch_debug, through the C ABI)
+with the CPU oracle on identical seeded inputs.
 
-Bar: status equal; top-k id lists bit-exact; probabilities within 1e-5
-relative; sampled tokens identical except where the oracle reports the draw
-(or the top-p cutoff) within 1e-6 of a CDF boundary -- those are counted and
-reported, not failed.
+Bar: status equal; top-k id lists bit-exact; the kept set of every row bit
+exact (the list size K, the position of the last kept entry in (logit desc,
+id asc) order and that entry's id); probabilities within 1e-5 relative;
+sampled tokens identical except where the oracle reports the draw (or the
+top-p cutoff) within 1e-6 of a CDF boundary -- those are counted (see
+conftest.PARITY) and reported, not failed.
 """
+import concurrent.futures as cf
+import os
+
 import numpy as np
 import pytest
 
 import oracle
 import rlsampler
 import workloads
+from conftest import parity_add
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
 
 PROB_RTOL = 1e-5
 BOUNDARY = 1e-6
+NTHREADS = max(1, min(32, os.cpu_count() or 1))
+PARITY_STEPS = int(os.environ.get("RL_PARITY_STEPS", "20"))
 
 
 @pytest.fixture(scope="module")
@@ -43,34 +51,58 @@ def run_gpu(s, batch, list_cap=1024, bf16=False):
     return [t.cpu().numpy() for t in out]
 
 
-def compare(batch, gpu, list_cap=1024, label=""):
-    tok, prob, st, lids, lps, llen = gpu
+def oracle_rows(batch, list_cap):
+    """The oracle on every row, rows spread over host threads (the ctypes
+    call releases the GIL)."""
     B = batch.logits.shape[0]
-    boundary_cases = 0
-    for b in range(B):
+
+    def one(b):
         prm = {k: batch.params[b][k].item() for k in batch.params.dtype.names}
         h = batch.hist[b][: batch.hist_len[b]] if batch.hist is not None else None
         m = batch.mask[b] if batch.mask is not None else None
-        r = oracle.spec_sample_row(batch.logits[b], h, m, prm, batch.uniforms[b], list_cap=list_cap)
+        return oracle.spec_sample_row(batch.logits[b], h, m, prm, batch.uniforms[b], list_cap=list_cap)
+
+    with cf.ThreadPoolExecutor(NTHREADS) as ex:
+        return list(ex.map(one, range(B)))
+
+
+def compare(batch, gpu, list_cap=1024, label="", key=None):
+    tok, prob, st, lids, lps, llen, cut = gpu
+    refs = oracle_rows(batch, list_cap)
+    n = dict(rows=0, tokens_equal=0, boundary=0, kept_set_checked=0, cut_boundary=0, lists_checked=0)
+    for b, r in enumerate(refs):
         exp_st = 0 if r.status == 0 else rlsampler.RL_ERR_NONFINITE
         assert st[b] == exp_st, f"{label} row {b}: status {st[b]} vs {exp_st}"
+        n["rows"] += 1
         if r.status:
             continue
-        n = llen[b]
-        if n >= 0:
+        # the kept set: K, the last kept position and its id
+        assert cut[b, 0] == r.K, f"{label} row {b}: K {cut[b, 0]} vs {r.K}"
+        if r.cut_margin < BOUNDARY:
+            n["cut_boundary"] += 1
+        else:
+            assert cut[b, 1] == r.cutoff, f"{label} row {b}: cutoff position {cut[b, 1]} vs {r.cutoff}"
+            if cut[b, 2] != -2:
+                assert cut[b, 2] == r.cut_id, f"{label} row {b}: cutoff id {cut[b, 2]} vs {r.cut_id}"
+            n["kept_set_checked"] += 1
+        m = llen[b]
+        if m >= 0:
             want = min(r.K, list_cap)
-            assert n == want, f"{label} row {b}: list length {n} vs {want}"
-            assert np.array_equal(lids[b, :n], r.list_ids[:n]), f"{label} row {b}: top-k ids differ"
-            np.testing.assert_allclose(lps[b, :n], r.list_p[:n], rtol=PROB_RTOL, atol=1e-30,
+            assert m == want, f"{label} row {b}: list length {m} vs {want}"
+            assert np.array_equal(lids[b, :m], r.list_ids[:m]), f"{label} row {b}: top-k ids differ"
+            np.testing.assert_allclose(lps[b, :m], r.list_p[:m], rtol=PROB_RTOL, atol=1e-30,
                                        err_msg=f"{label} row {b}: list probabilities")
+            n["lists_checked"] += 1
         if tok[b] != r.token:
             near = min(r.draw_margin, r.cut_margin) < BOUNDARY
             assert near, (f"{label} row {b}: token {tok[b]} vs oracle {r.token} "
                           f"(draw margin {r.draw_margin:.3g}, cut margin {r.cut_margin:.3g})")
-            boundary_cases += 1
+            n["boundary"] += 1
             continue
+        n["tokens_equal"] += 1
         np.testing.assert_allclose(prob[b], r.prob, rtol=PROB_RTOL, err_msg=f"{label} row {b}: prob")
-    return boundary_cases
+    parity_add(key or label, **n)
+    return n["boundary"]
 
 
 def make_batch(rng, B, V, T, top_k, top_p, hist_len=0, mask_density=None, rp=1.1, pres=0.2, freq=0.3,
@@ -121,7 +153,29 @@ def test_small_shapes(sampler, case):
     B, V, T, k, tp, hl, md, ties = case
     rng = np.random.default_rng(hash(case) & 0xFFFFFFFF)
     batch = make_batch(rng, B, V, T, k, tp, hl, md, ties=ties)
-    compare(batch, run_gpu(sampler, batch), label=str(case))
+    compare(batch, run_gpu(sampler, batch), label=str(case), key="small_shapes")
+
+
+BIG_K = [
+    # B, V, T, top_k, top_p, hist, mask_density: top-k lists longer than the
+    # kernel's 128-key list (kept set compared through the cutoff export),
+    # and masked rows whose allowed set exceeds 128 with top_k off
+    (4, 32000, 1.0, 129, 1.0, 64, None),
+    (4, 32000, 0.8, 500, 1.0, 64, None),
+    (4, 128256, 1.2, 1000, 1.0, 256, None),
+    (4, 32000, 1.1, 300, 0.97, 0, None),
+    (4, 32000, 0.9, 0, 1.0, 0, 0.02),
+    (4, 32000, 1.3, 0, 0.95, 64, 0.05),
+    (4, 32000, 1.0, 200, 0.9, 0, 0.2),
+]
+
+
+@pytest.mark.parametrize("case", BIG_K, ids=lambda c: f"B{c[0]}_V{c[1]}_k{c[3]}_p{c[4]}_m{c[6]}")
+def test_big_k_and_masked_sets(sampler, case):
+    B, V, T, k, tp, hl, md = case
+    rng = np.random.default_rng(hash(case) & 0xFFFFFFFF)
+    batch = make_batch(rng, B, V, T, k, tp, hl, md)
+    compare(batch, run_gpu(sampler, batch), label=str(case), key="big_k_and_masked")
 
 
 DEEP = [
@@ -142,33 +196,36 @@ def test_deep_top_p_rows(sampler, case):
     B, V, T, k, tp, hl, scale, ties = case
     rng = np.random.default_rng(hash(case) & 0xFFFFFFFF)
     batch = make_batch(rng, B, V, T, k, tp, hl, None, scale=scale, ties=ties)
-    compare(batch, run_gpu(sampler, batch), label=str(case))
+    compare(batch, run_gpu(sampler, batch), label=str(case), key="deep_top_p")
 
 
-def test_config2_rows(sampler):
-    rows = list(range(0, 256, 16))
+def test_config2_full_batches(sampler):
+    """Every row of the heterogeneous batch (B=256 x V=128256) over
+    PARITY_STEPS regenerated steps."""
     total = 0
-    for step in range(2):
-        batch = workloads.config2(step, rows=rows)
-        total += compare(batch, run_gpu(sampler, batch), label=f"config2 step {step}")
-    print(f"config2: {total} boundary cases")
+    for step in range(PARITY_STEPS):
+        batch = workloads.config2(step)
+        total += compare(batch, run_gpu(sampler, batch), label=f"config2 step {step}", key="config2")
+    print(f"config2: {total} boundary cases over {PARITY_STEPS} steps")
 
 
 def test_config3_full(sampler):
-    for step in range(2):
+    for step in range(PARITY_STEPS):
         batch = workloads.config3(step)
-        compare(batch, run_gpu(sampler, batch), label=f"config3 step {step}")
+        compare(batch, run_gpu(sampler, batch), label=f"config3 step {step}", key="config3")
 
 
 def test_config1_spec(sampler):
-    for step in range(5):
+    for step in range(PARITY_STEPS):
         batch = workloads.config1(step)
-        compare(batch, run_gpu(sampler, batch), label=f"config1 step {step}")
+        compare(batch, run_gpu(sampler, batch), label=f"config1 step {step}", key="config1_spec")
 
 
 def test_config5_rows_bf16(sampler):
-    batch = workloads.config5_rows(0, rows=list(range(0, 1024, 128)))
-    compare(batch, run_gpu(sampler, batch, bf16=True), label="config5 bf16")
+    rows = list(range(0, 1024, 8))
+    for step in range(max(1, PARITY_STEPS // 5)):
+        batch = workloads.config5_rows(step, rows=rows)
+        compare(batch, run_gpu(sampler, batch, bf16=True), label=f"config5 bf16 step {step}", key="config5_one_piece")
 
 
 def test_nonfinite_rows_flagged(sampler):
@@ -183,16 +240,28 @@ def test_nonfinite_rows_flagged(sampler):
 
 
 def test_full_size_config2_properties(sampler):
-    """Full B=256 x V=128256: every row OK, tokens inside the allowed range,
-    deterministic across runs, and greedy rows reproduce argmax."""
+    """Full B=256 x V=128256 through the production entry (rl_sample_batch):
+    every row OK, deterministic across runs, equal to the debug launch, and
+    top-k rows draw from their list."""
     batch = workloads.config2(0)
-    g1 = run_gpu(sampler, batch)
-    g2 = run_gpu(sampler, batch)
-    assert (g1[2] == 0).all()
-    assert np.array_equal(g1[0], g2[0]) and np.array_equal(g1[1], g2[1])
-    assert ((g1[0] >= 0) & (g1[0] < 128256)).all()
-    # top-k rows: the token is inside the row's top-k list
+    dev = "cuda:0"
+    lg = torch.from_numpy(batch.logits).to(dev)
+    p = rlsampler.params_tensor(batch.params, dev)
+    u = torch.from_numpy(batch.uniforms).to(dev)
+    hist = torch.from_numpy(batch.hist).to(dev)
+    hl = torch.from_numpy(batch.hist_len).to(dev)
+    runs = []
+    for _ in range(3):
+        t, pr, st = sampler.sample(lg, p, u, hist, hl)
+        torch.cuda.synchronize()
+        runs.append((t.cpu().numpy(), pr.cpu().numpy(), st.cpu().numpy()))
+    for t, pr, st in runs:
+        assert (st == 0).all()
+        assert np.array_equal(t, runs[0][0]) and np.array_equal(pr, runs[0][1])
+    g = run_gpu(sampler, batch)
+    assert np.array_equal(g[0], runs[0][0]) and np.array_equal(g[1], runs[0][1])
+    assert ((g[0] >= 0) & (g[0] < 128256)).all()
     for b in range(256):
         k = batch.params[b]["top_k"]
-        if k > 0 and g1[5][b] >= 0:
-            assert g1[0][b] in set(g1[3][b, : g1[5][b]].tolist())
+        if k > 0 and g[5][b] >= 0:
+            assert g[0][b] in set(g[3][b, : g[5][b]].tolist())
