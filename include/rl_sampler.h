@@ -61,7 +61,10 @@ typedef struct rl_sampler rl_sampler;
 /* Creates a sampler on `device`. The handle owns a small device workspace
  * sized by the limits (allocated here, never in a sampling call).
  * Replaces the per-call construction of Decoder / Sampler
- * (src/decoder.rs:19-29, :325-331). flags: reserved, pass 0. */
+ * (src/decoder.rs:19-29, :325-331). flags: 0, or RL_CREATE_SHARDED to also
+ * allocate the exchange buffers of rl_sample_sharded (1056 B per row for this
+ * rank and 16 x that for the gathered records). */
+#define RL_CREATE_SHARDED 1u
 rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max_vocab,
                             int max_history, uint32_t flags);
 rl_status rl_sampler_destroy(rl_sampler* h);
@@ -71,6 +74,30 @@ const char* rl_last_error(void);
 
 /* Library version string. */
 const char* rl_version(void);
+
+/*
+ * Debug switches of a handle (diagnostics; flags = 0 turns them off). No
+ * counterpart in the reference: they exercise this library's failure path.
+ * RL_DEBUG_EXPIRE_WAIT: every item of the spec sampler's streaming kernel
+ * first waits, with a budget of about two thousand cycles, on a device
+ * barrier that nothing completes; the wait runs out and every row of the call
+ * reports RL_ERR_TIMEOUT in row_status (token -1), as a device wait that ran
+ * out of its budget would, without a fault or a hang. Later calls with the
+ * switch off sample normally on the same handle.
+ */
+#define RL_DEBUG_EXPIRE_WAIT 1u
+rl_status rl_sampler_set_debug(rl_sampler* h, uint32_t flags);
+
+/*
+ * Self-check of the fixed-divisor division that the spec sampler uses for
+ * every logit / temperature (no counterpart in the reference). For each T[j]
+ * (device array, nT <= 65535) counts the a[i] (device array) whose quotient
+ * differs in any bit from IEEE division (__fdiv_rn) into mismatch[j], and sets
+ * fast[j] = 1 when the fixed-divisor path is in use for T[j] (device arrays
+ * [nT]). Asynchronous on `stream`.
+ */
+rl_status rl_selfcheck_div(const float* a, int n, const float* T, int nT, uint32_t* mismatch, uint32_t* fast,
+                           void* stream);
 
 /*
  * Batched spec sampling: penalties -> mask -> temperature -> softmax ->
@@ -131,13 +158,19 @@ rl_status rl_sample_host(rl_sampler* h, const float* logits, int B, int V, const
  * counterpart in the reference: it serves callers that cannot allocate where
  * they sample (inside CUDA-graph capture, allocator-free decode loops, FFI
  * callers with no place to keep a handle). Same arguments and results as
- * rl_sample_batch, on the current device. Its scratch is a fixed device array
- * of the library (9.7 MB, the candidate overflow of at most 296 CTAs); sizes
- * beyond V <= 2093056, hist_stride <= 1024, B <= 65535 return RL_ERR_SHAPE.
- * The first call on a device looks up the scratch's address and the SM count
- * (no allocation) -- make it before any stream capture. Nothing in the
- * scratch must start at zero. Calls that overlap in time on one device share
- * the scratch and race: serialise them.
+ * rl_sample_batch, on the current device; every buffer must be device memory
+ * of that device (else RL_ERR_INVALID_ARG). Its scratch is a fixed device
+ * array of the library (9.7 MB, the candidate overflow of at most 296 CTAs);
+ * sizes beyond V <= 2093056, hist_stride <= 1024, B <= 65535 return
+ * RL_ERR_SHAPE. The first call on a device reads the SM count and configures
+ * the kernels of both dtypes (no allocation); it must come before any stream
+ * capture (inside one it returns RL_ERR_UNSUPPORTED). The scratch's device
+ * address is looked up on every call made outside a capture, so a reset
+ * device (cudaDeviceReset, which reloads the module) is picked up there;
+ * calls inside a capture reuse the last address, so capture after a reset
+ * only once an uncaptured call has run. Nothing in the scratch must start at
+ * zero. Calls that overlap in time on one device share the scratch and race:
+ * serialise them.
  */
 rl_status rl_sample_batch_static(const void* logits, rl_dtype dtype, int B, int V, int64_t ld,
                                  const int32_t* hist, const int32_t* hist_len, int hist_stride,
@@ -158,12 +191,24 @@ rl_status rl_sample_batch_static(const void* logits, rl_dtype dtype, int B, int 
  * Every sum is the reference's left-to-right f32 accumulation, reproduced bit
  * for bit; exp is the correctly rounded f32 exponential. A row holding NaN or
  * +-inf gets token -1 and probability 0 (the reference's result there depends
- * on NaN ordering). V must be <= 53248 (the row is held in one CTA's shared
- * memory) and <= the handle's max_vocab; B <= max_batch.
+ * on NaN ordering). B <= max_batch, V <= max_vocab. A row is worked on in one
+ * CTA's shared memory when it fits (V <= 53248 on a B200), else in the
+ * handle's staging buffer (which rl_sample_host and rl_decoder_sample_host
+ * also use: one call at a time per handle).
  */
 rl_status rl_decoder_sample(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
                             const float* temperature, const float* top_p, const float* uniforms,
                             int32_t* out_tok, float* out_prob, void* stream);
+
+/*
+ * rl_decoder_sample on host buffers (synchronous): logits [B, V] row-major
+ * f32, temperature[B], top_p[B], uniforms[B] in host memory; out_tok[B] and
+ * out_prob[B] (nullable) written in host memory. Backs the &[f32] Rust
+ * signatures of Decoder::sample / Decoder::sample_with_params
+ * (src/decoder.rs:31-100) with the reference's own semantics.
+ */
+rl_status rl_decoder_sample_host(rl_sampler* h, const float* logits, int B, int V, const float* temperature,
+                                 const float* top_p, const float* uniforms, int32_t* out_tok, float* out_prob);
 
 /* Decoder::greedy_sample (src/decoder.rs:160-167): argmax, LAST maximum on ties. */
 rl_status rl_greedy(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
@@ -225,6 +270,42 @@ rl_status rl_sample_merge(rl_sampler* h, int G, int B, const uint64_t* keys,
                           const rl_part_stats* stats, const rl_row_params* params,
                           const float* uniforms, int32_t* out_tok, float* out_prob,
                           int32_t* row_status, void* stream);
+
+/*
+ * Vocabulary-sharded sampling in one call per rank, with the exchange over
+ * NCCL. No single reference function: it replaces sampling whole rows on one
+ * thread (ContinuousBatchingEngine::step, src/inference.rs:112-138 ->
+ * Model::sample_with_params) when a row's vocabulary is split across the G
+ * devices of an NCCL communicator (one rank per device, G <= 16). Every rank
+ * calls it with its own columns [vocab_offset, vocab_offset + V_local) of the
+ * same rows, in the same order; the rank streams them (rl_sample_partial),
+ * the ranks' packed records (the sorted top-min(top_k, 128) list and the
+ * softmax summary, 1056 bytes per row) are all-gathered with one
+ * ncclAllGather on `stream`, and every rank merges them (rl_sample_merge) into
+ * the same tokens. History ids are global; mask_shard bit i is the rank's
+ * column i. Rows with temperature <= 0 take the argmax; sampled rows need
+ * 1 <= top_k <= 128 (RL_ERR_UNSUPPORTED in row_status otherwise).
+ *  comm: an ncclComm_t (void*) of this device, e.g. from rl_nccl_comm_init.
+ *  The handle needs RL_CREATE_SHARDED. NCCL errors return RL_ERR_NCCL.
+ */
+rl_status rl_sample_sharded(rl_sampler* h, void* comm, const void* logits, rl_dtype dtype, int B, int V_local,
+                            int64_t ld, int vocab_offset, int V_global, const int32_t* hist,
+                            const int32_t* hist_len, int hist_stride, const uint32_t* mask_shard,
+                            int64_t mask_stride, const rl_row_params* params, const float* uniforms,
+                            int32_t* out_tok, float* out_prob, int32_t* row_status, void* stream);
+
+/*
+ * NCCL communicators for rl_sample_sharded (NCCL is loaded at run time: the
+ * one already in the process, else libnccl.so.2, or the file named by the
+ * RL_NCCL_LIBRARY environment variable; RL_ERR_UNSUPPORTED without it).
+ * Rank 0 makes an id (RL_NCCL_ID_BYTES bytes), the caller hands it to every
+ * rank by its own means, and each rank creates its communicator with its
+ * device current (ncclGetUniqueId / ncclCommInitRank / ncclCommDestroy).
+ */
+#define RL_NCCL_ID_BYTES 128
+rl_status rl_nccl_unique_id(void* id_out);
+rl_status rl_nccl_comm_init(void** comm_out, int nranks, const void* id, int rank);
+rl_status rl_nccl_comm_destroy(void* comm);
 
 /*
  * One beam-search step for `items` independent searches of `beams` beams

@@ -46,7 +46,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             subprocess.run(cmd, check=True)
     if force or _newer(LIB, objs):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB] + objs + [
-            "-Xlinker", "--version-script=" + os.path.join(CSRC, "exports.map")]
+            "-Xlinker", "--version-script=" + os.path.join(CSRC, "exports.map"), "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

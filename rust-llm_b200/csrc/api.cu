@@ -75,6 +75,7 @@ rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max
     return fail(RL_ERR_SHAPE, "rl_sampler_create: max_vocab %d > %d", max_vocab, (1 << 21) - rl::kCE);
   if (max_history > rl::kHmax)
     return fail(RL_ERR_SHAPE, "rl_sampler_create: max_history %d > %d", max_history, rl::kHmax);
+  if (flags & ~RL_CREATE_SHARDED) return fail(RL_ERR_INVALID_ARG, "rl_sampler_create: unknown flags 0x%x", flags);
   int ndev = 0;
   cudaError_t e = cudaGetDeviceCount(&ndev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
@@ -107,6 +108,13 @@ rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max
   return RL_OK;
 }
 
+rl_status rl_sampler_set_debug(rl_sampler* h, uint32_t flags) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sampler_set_debug: handle is NULL");
+  if (flags & ~RL_DEBUG_EXPIRE_WAIT) return fail(RL_ERR_INVALID_ARG, "rl_sampler_set_debug: unknown flags 0x%x", flags);
+  h->debug = flags;
+  return RL_OK;
+}
+
 rl_status rl_sampler_destroy(rl_sampler* h) {
   if (!h) return RL_OK;
   DeviceGuard g(h->device);
@@ -122,7 +130,8 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
                                float* out_prob, int32_t* row_status, int32_t* list_ids,
                                float* list_probs, int32_t* list_len, int list_cap, void* stream,
                                int vocab_offset, uint64_t* part_keys = nullptr,
-                               rl::PartStats* part_stats = nullptr, int32_t* list_cut = nullptr) {
+                               rl::PartStats* part_stats = nullptr, int32_t* list_cut = nullptr,
+                               int part_packed = 0) {
   if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: handle is NULL");
   if (B < 0 || V <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_batch: B=%d V=%d", B, V);
   if (B == 0) return RL_OK;
@@ -166,8 +175,10 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.list_cap = list_cap;
   a.list_cut = list_cut;
   a.vocab_offset = vocab_offset;
+  a.debug_flags = static_cast<int>(h->debug);
   a.part_keys = part_keys;
   a.part_stats = part_stats;
+  a.part_packed = part_packed;
   a.ws = h->ws;
   cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
@@ -233,6 +244,49 @@ rl_status rl_sample_merge(rl_sampler* h, int G, int B, const uint64_t* keys, con
   m.row_status = row_status;
   cudaError_t e = rl::launch_shard_merge(m, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_merge launch");
+  return RL_OK;
+}
+
+rl_status rl_sample_sharded(rl_sampler* h, void* comm, const void* logits, rl_dtype dtype, int B, int V_local,
+                            int64_t ld, int vocab_offset, int V_global, const int32_t* hist, const int32_t* hist_len,
+                            int hist_stride, const uint32_t* mask, int64_t mask_stride, const rl_row_params* params,
+                            const float* uniforms, int32_t* out_tok, float* out_prob, int32_t* row_status,
+                            void* stream) {
+  if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sample_sharded: handle is NULL");
+  if (!comm) return fail(RL_ERR_INVALID_ARG, "rl_sample_sharded: comm is NULL");
+  if (!h->shard_send) return fail(RL_ERR_UNSUPPORTED, "rl_sample_sharded: handle created without RL_CREATE_SHARDED");
+  if (B < 0 || V_local <= 0) return fail(RL_ERR_INVALID_ARG, "rl_sample_sharded: B=%d V_local=%d", B, V_local);
+  if (vocab_offset < 0 || static_cast<int64_t>(vocab_offset) + V_local > V_global)
+    return fail(RL_ERR_INVALID_ARG, "rl_sample_sharded: columns [%d, %lld) outside the vocabulary of %d", vocab_offset,
+                static_cast<long long>(vocab_offset) + V_local, V_global);
+  if (B > h->max_batch) return fail(RL_ERR_SHAPE, "rl_sample_sharded: B=%d > max_batch %d", B, h->max_batch);
+  if (B == 0) return RL_OK;
+  if (!out_tok || !uniforms || !params) return fail(RL_ERR_INVALID_ARG, "rl_sample_sharded: a required pointer is NULL");
+  DeviceGuard g(h->device);
+  if (!g.ok) return fail(RL_ERR_CUDA, "cudaSetDevice(%d) failed", h->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 1. this rank's columns -> its packed records
+  rl_status st = sample_common(h, logits, dtype, B, V_local, ld, hist, hist_len, hist_stride, mask, mask_stride,
+                               params, h->zero_u, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0, stream,
+                               vocab_offset, h->shard_send, nullptr, nullptr, 1);
+  if (st != RL_OK) return st;
+  // 2. one all-gather of the records of every rank
+  int G = 0;
+  st = rl::nccl_gather_records(comm, h->shard_send, h->shard_recv, B, &G, s);
+  if (st != RL_OK) return st;
+  // 3. the same merge and draw on every rank
+  rl::MergeArgs m = {};
+  m.keys = h->shard_recv;
+  m.stats = nullptr;  // packed records
+  m.G = G;
+  m.B = B;
+  m.params = params;
+  m.uniforms = uniforms;
+  m.out_tok = out_tok;
+  m.out_prob = out_prob;
+  m.row_status = row_status;
+  cudaError_t e = rl::launch_shard_merge(m, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rl_sample_sharded: merge launch");
   return RL_OK;
 }
 

@@ -27,13 +27,25 @@ __device__ __forceinline__ float div_rn(float a, float b) { return __fdiv_rn(a, 
 // FMA-based refinement (P. Markstein, "Computation of elementary functions on
 // the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990):
 // y = RN(1/b), q = RN(a*y), r = a - b*q (exact with one FMA), RN(q + r*y).
-// The caller guarantees normal-range operands (|a| >= 2^-90 or a == 0,
-// 2^-20 <= |b| <= 2^20); outside that range it uses div_rn. Checked
-// bit-for-bit against __fdiv_rn by tests/test_kernels_gpu.py.
+// The caller keeps the operands where that holds and the quotient is a
+// finite normal number: 2^-90 <= |a| < 2^100 and 2^-20 <= b <= 2^20 (an
+// overflowing quotient would come out NaN, a zero numerator without its
+// sign); elsewhere it uses IEEE division. Checked bit for bit against
+// __fdiv_rn on the device by rl_selfcheck_div (the library's self-check
+// entry point, run by the GPU tests).
 __device__ __forceinline__ float div_fixed(float a, float b, float y) {
   float q = __fmul_rn(a, y);
   float r = __fmaf_rn(-q, b, a);
   return __fmaf_rn(r, y, q);
+}
+// The divisor range in which div_fixed is used (2^-20 <= b <= 2^20).
+__device__ __forceinline__ bool fixed_div_ok(float b) { return b >= 9.5367431640625e-07f && b <= 1048576.0f; }
+// a / b correctly rounded, by div_fixed where its preconditions hold
+// (fast: fixed_div_ok(b); yb = RN(1/b)), else by IEEE division.
+__device__ __forceinline__ float div_by(float a, float b, float yb, bool fast) {
+  const float m = fabsf(a);
+  if (fast && m >= 8.077935669e-28f && m < 1.2676506002282294e30f) return div_fixed(a, b, yb);
+  return __fdiv_rn(a, b);
 }
 
 // Order-preserving map float -> uint32 (larger float -> larger key).

@@ -1,6 +1,7 @@
 // ref_exact profile on the device: Decoder::sample_with_params
 // (src/decoder.rs:35-100), quirk for quirk, one CTA per row with the row in
-// shared memory.
+// shared memory -- or, for a row too long for it, in a global scratch row
+// (the handle's staging buffer), read and written through L1/L2.
 //
 //   decoder.rs:44-55  T > 0: max (f32::max, NaN-ignoring), (x - max) / T,
 //                     exp, sequential f32 sum, divide by the sum if > 0
@@ -25,9 +26,12 @@
 // Deviation (documented in the header): a row holding NaN or +-inf returns
 // token -1 and probability 0.
 #include <climits>
+#include <cstdio>
 
 #include "common.cuh"
 #include "internal.h"
+
+static thread_local char g_xerr[256];
 
 namespace rl {
 namespace {
@@ -425,6 +429,8 @@ struct XArgs {
   int64_t ld;
   int V;
   int cap;  // keys of a sorted batch (power of two)
+  float* scratch;      // non-null: the row's working copy lives here (row r at r * scratch_ld)
+  int64_t scratch_ld;
   const float* temperature;
   const float* top_p;
   const float* uniforms;
@@ -436,9 +442,12 @@ __global__ void __launch_bounds__(kXT, 1) decoder_exact_kernel(const __grid_cons
   extern __shared__ __align__(16) unsigned char xsm[];
   __shared__ XShared sh;
   const int V = a.V;
-  float* vals = reinterpret_cast<float*>(xsm);
-  uint64_t* list = reinterpret_cast<uint64_t*>(xsm + ((static_cast<size_t>(V) * 4 + 15) & ~static_cast<size_t>(15)));
   const int row = blockIdx.x, tid = threadIdx.x;
+  // the working copy of the row: shared memory, or the global scratch row
+  // (then the sorted batches take the start of shared memory)
+  float* vals = a.scratch ? a.scratch + static_cast<int64_t>(row) * a.scratch_ld : reinterpret_cast<float*>(xsm);
+  uint64_t* list = reinterpret_cast<uint64_t*>(
+      a.scratch ? xsm : xsm + ((static_cast<size_t>(V) * 4 + 15) & ~static_cast<size_t>(15)));
   int par = 0;
   const float* x = a.logits + static_cast<int64_t>(row) * a.ld;
   // ---- load, max (f32::max from f32::MIN), finiteness ----
@@ -589,8 +598,10 @@ __global__ void __launch_bounds__(kXT, 1) decoder_exact_kernel(const __grid_cons
 
 }  // namespace
 
-int decoder_exact_smem(int V, int max_optin, int* cap) {
-  const size_t base = (static_cast<size_t>(V) * 4 + 15) & ~static_cast<size_t>(15);
+// Dynamic shared memory of a launch (-1: does not fit); in_global: the row
+// lives in a global scratch row, only the sorted batches in shared memory.
+int decoder_exact_smem(int V, int max_optin, int* cap, bool in_global) {
+  const size_t base = in_global ? 0 : (static_cast<size_t>(V) * 4 + 15) & ~static_cast<size_t>(15);
   const size_t fixed = sizeof(XShared) + 1024;  // static shared memory and reserve
   for (int c = 2048; c >= 1024; c >>= 1)
     if (base + static_cast<size_t>(c) * 8 + fixed <= static_cast<size_t>(max_optin)) {
@@ -602,7 +613,7 @@ int decoder_exact_smem(int V, int max_optin, int* cap) {
 
 cudaError_t launch_decoder_exact(const float* logits, int B, int V, int64_t ld, const float* temperature,
                                  const float* top_p, const float* uniforms, int32_t* out_tok, float* out_prob,
-                                 int smem, int cap, cudaStream_t stream) {
+                                 int smem, int cap, float* scratch, int64_t scratch_ld, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(decoder_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   XArgs a;
@@ -615,6 +626,8 @@ cudaError_t launch_decoder_exact(const float* logits, int B, int V, int64_t ld, 
   a.uniforms = uniforms;
   a.out_tok = out_tok;
   a.out_prob = out_prob;
+  a.scratch = scratch;
+  a.scratch_ld = scratch_ld;
   decoder_exact_kernel<<<B, kXT, smem, stream>>>(a);
   return cudaGetLastError();
 }
@@ -624,9 +637,52 @@ cudaError_t launch_decoder_exact(const float* logits, int B, int V, int64_t ld, 
 extern "C" {
 #pragma GCC visibility push(default)
 
+// The launch behind rl_decoder_sample and rl_decoder_sample_host (the
+// handle's device is current). A row that does not fit in shared memory is
+// worked on in the handle's staging buffer (row r at r * max_vocab), which
+// may be the logits themselves (the host entry copies them there first).
+static rl_status decoder_sample_dev(rl_sampler* h, const float* logits, int B, int V, int64_t ld,
+                                   const float* temperature, const float* top_p, const float* uniforms,
+                                   int32_t* out_tok, float* out_prob, cudaStream_t stream, const char* who) {
+  int optin = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, h->device);
+  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, cudaGetErrorString(e));
+  int cap = 0;
+  int smem = rl::decoder_exact_smem(V, optin, &cap, false);
+  float* scratch = nullptr;
+  if (smem <= 0) {
+    if (!h->stage_logits) {
+      std::snprintf(g_xerr, sizeof(g_xerr), "%s: V=%d exceeds shared memory and the handle has no staging buffer", who, V);
+      return rl::set_error(RL_ERR_SHAPE, g_xerr);
+    }
+    smem = rl::decoder_exact_smem(V, optin, &cap, true);
+    scratch = h->stage_logits;
+    if (smem <= 0) return rl::set_error(RL_ERR_SHAPE, "rl_decoder_sample: shared memory too small");
+  }
+  e = rl::launch_decoder_exact(logits, B, V, ld, temperature, top_p, uniforms, out_tok, out_prob, smem, cap, scratch,
+                               h->max_vocab, stream);
+  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, cudaGetErrorString(e));
+  return RL_OK;
+}
+
+// Makes the handle's device current for the scope of a call.
+struct XDeviceGuard {
+  int prev = -1;
+  bool ok = true;
+  explicit XDeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~XDeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
 rl_status rl_decoder_sample(rl_sampler* h, const float* logits, int B, int V, int64_t ld, const float* temperature,
                             const float* top_p, const float* uniforms, int32_t* out_tok, float* out_prob,
                             void* stream) {
+  rl::clear_error();
   if (!h) return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample: handle is NULL");
   if (B < 0 || V <= 0) return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample: bad B or V");
   if (B == 0) return RL_OK;
@@ -635,22 +691,45 @@ rl_status rl_decoder_sample(rl_sampler* h, const float* logits, int B, int V, in
   if (ld < V) return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample: ld < V");
   if (B > h->max_batch || V > h->max_vocab)
     return rl::set_error(RL_ERR_SHAPE, "rl_decoder_sample: B or V beyond the handle's limits");
-  if (V > 53248) return rl::set_error(RL_ERR_SHAPE, "rl_decoder_sample: V > 53248 (one row per CTA's shared memory)");
-  int cur = -1;
-  if (cudaGetDevice(&cur) != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample: cudaGetDevice failed");
-  if (cur != h->device && cudaSetDevice(h->device) != cudaSuccess)
-    return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample: cudaSetDevice failed");
-  int optin = 0;
-  cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, h->device);
-  int cap = 0;
-  const int smem = e == cudaSuccess ? rl::decoder_exact_smem(V, optin, &cap) : -1;
-  if (e == cudaSuccess && smem > 0)
-    e = rl::launch_decoder_exact(logits, B, V, ld, temperature, top_p, uniforms, out_tok, out_prob, smem, cap,
-                                 static_cast<cudaStream_t>(stream));
-  if (cur != h->device) cudaSetDevice(cur);
-  if (smem <= 0 && e == cudaSuccess)
-    return rl::set_error(RL_ERR_SHAPE, "rl_decoder_sample: the row does not fit in shared memory");
-  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, cudaGetErrorString(e));
+  XDeviceGuard g(h->device);
+  if (!g.ok) return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample: cudaSetDevice failed");
+  return decoder_sample_dev(h, logits, B, V, ld, temperature, top_p, uniforms, out_tok, out_prob,
+                            static_cast<cudaStream_t>(stream), "rl_decoder_sample");
+}
+
+rl_status rl_decoder_sample_host(rl_sampler* h, const float* logits, int B, int V, const float* temperature,
+                                 const float* top_p, const float* uniforms, int32_t* out_tok, float* out_prob) {
+  rl::clear_error();
+  if (!h) return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample_host: handle is NULL");
+  if (B < 0 || V <= 0) return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample_host: bad B or V");
+  if (B == 0) return RL_OK;
+  if (!logits || !temperature || !top_p || !uniforms || !out_tok)
+    return rl::set_error(RL_ERR_INVALID_ARG, "rl_decoder_sample_host: a required pointer is NULL");
+  if (B > h->max_batch || V > h->max_vocab)
+    return rl::set_error(RL_ERR_SHAPE, "rl_decoder_sample_host: B or V beyond the handle's limits");
+  if (!h->stage_logits) return rl::set_error(RL_ERR_UNSUPPORTED, "rl_decoder_sample_host: no staging buffers");
+  XDeviceGuard g(h->device);
+  if (!g.ok) return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample_host: cudaSetDevice failed");
+  cudaStream_t s = h->stream;
+  // the rows are staged at stride max_vocab, where a long row is also worked on
+  const int64_t ld = h->max_vocab;
+  cudaError_t e = cudaMemcpy2DAsync(h->stage_logits, sizeof(float) * ld, logits, sizeof(float) * V,
+                                    sizeof(float) * V, B, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h->stage_T, temperature, sizeof(float) * B, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h->stage_p, top_p, sizeof(float) * B, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(h->stage_u, uniforms, sizeof(float) * B, cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample_host: copy to the device failed");
+  rl_status st = decoder_sample_dev(h, h->stage_logits, B, V, ld, h->stage_T, h->stage_p, h->stage_u, h->stage_tok,
+                                    h->stage_prob, s, "rl_decoder_sample_host");
+  if (st != RL_OK) return st;
+  e = cudaMemcpyAsync(out_tok, h->stage_tok, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess && out_prob)
+    e = cudaMemcpyAsync(out_prob, h->stage_prob, sizeof(float) * B, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_decoder_sample_host: copy back failed");
   return RL_OK;
 }
 

@@ -14,6 +14,7 @@ struct rl_sampler {
   int max_history = 0;
   int num_sms = 0;
   uint32_t flags = 0;
+  uint32_t debug = 0;             // rl_sampler_set_debug switches
   cudaStream_t stream = nullptr;  // used by the host-buffer entry points
   // device staging buffers of rl_sample_host (allocated at create)
   float* stage_logits = nullptr;
@@ -23,6 +24,8 @@ struct rl_sampler {
   int mask_words = 0;
   rl_row_params* stage_params = nullptr;
   float* stage_u = nullptr;
+  float* stage_T = nullptr;       // rl_decoder_sample_host: temperatures and top_p
+  float* stage_p = nullptr;
   int32_t* stage_tok = nullptr;
   float* stage_prob = nullptr;
   int32_t* stage_status = nullptr;
@@ -32,6 +35,10 @@ struct rl_sampler {
   uint64_t* part_keys = nullptr;      // [max_batch * kN]
   rl::PartStats* part_stats = nullptr;
   rl_row_params* beam_params = nullptr;
+  // rl_sample_sharded (RL_CREATE_SHARDED): this rank's packed records and the
+  // gathered records of all ranks
+  uint64_t* shard_send = nullptr;  // [max_batch * kRec]
+  uint64_t* shard_recv = nullptr;  // [kMergeMaxShards * max_batch * kRec]
   float* zero_u = nullptr;            // uniforms of partial launches (unused, zero)
 };
 
@@ -39,5 +46,6 @@ namespace rl {
 rl_status alloc_workspace(rl_sampler* h);
 void free_workspace(rl_sampler* h);
 rl_status set_error(rl_status st, const char* msg);
+rl_status nccl_gather_records(void* comm, const uint64_t* send, uint64_t* recv, int B, int* G, cudaStream_t stream);
 void clear_error();
 }  // namespace rl

@@ -40,31 +40,65 @@ struct DevState {
 DevState g_dev[kMaxDevices];
 std::mutex g_mu;
 
-// Per-device set-up on the first call: the scratch's device address (with
-// the device current) and the SM count. Neither allocates.
-rl_status device_state(DevState** out) {
+// Per-device set-up on the first call (the SM count; both dtypes' kernels
+// configured, so that no later call does it inside a capture), and the
+// scratch's device address with that device current. The address is looked
+// up again on every call made outside a stream capture -- a reset device
+// reloads the module, and the address may move -- and taken from the cache
+// inside a capture. Nothing here allocates.
+rl_status device_state(cudaStream_t stream, DevState** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: cudaGetDevice failed");
   if (dev < 0 || dev >= kMaxDevices) return rl::set_error(RL_ERR_UNSUPPORTED, "rl_sample_batch_static: device index too large");
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: cudaStreamIsCapturing failed");
+  }
   std::lock_guard<std::mutex> lock(g_mu);
   DevState& d = g_dev[dev];
   if (!d.ready) {
+    if (cap != cudaStreamCaptureStatusNone)
+      return rl::set_error(RL_ERR_UNSUPPORTED,
+                           "rl_sample_batch_static: the first call on a device must come before any stream capture");
     int major = 0;
     e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: device query failed");
     if (major < 10) return rl::set_error(RL_ERR_UNSUPPORTED, "rl_sample_batch_static: this library is built for sm_100a");
     e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: device query failed");
+    e = rl::spec_configure_single();
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: kernel configuration failed");
+    }
+  }
+  if (!d.ready || cap == cudaStreamCaptureStatusNone) {
     e = cudaGetSymbolAddress(&d.ovf, g_static_ovf);
     if (e != cudaSuccess) {
       cudaGetLastError();
+      d.ready = 0;
       return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: cudaGetSymbolAddress of the scratch failed");
     }
     d.ready = 1;
   }
   *out = &d;
   return RL_OK;
+}
+
+// Whether device pointer p lives on device dev (or is managed memory that
+// dev can use); queried without allocating.
+bool on_device(const void* p, int dev) {
+  if (!p) return true;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (at.type == cudaMemoryTypeManaged) return true;
+  return at.type == cudaMemoryTypeDevice && at.device == dev;
 }
 
 }  // namespace
@@ -93,8 +127,17 @@ rl_status rl_sample_batch_static(const void* logits, rl_dtype dtype, int B, int 
   if (mask && mask_stride < (V + 31) / 32)
     return rl::set_error(RL_ERR_INVALID_ARG, "rl_sample_batch_static: mask_stride < ceil(V/32)");
   DevState* d = nullptr;
-  rl_status st = device_state(&d);
+  rl_status st = device_state(static_cast<cudaStream_t>(stream), &d);
   if (st != RL_OK) return st;
+  // the kernel runs on the current device with that device's scratch: its
+  // buffers must be there too (a peer's memory would fault without peer access)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return rl::set_error(RL_ERR_CUDA, "rl_sample_batch_static: cudaGetDevice failed");
+  if (!on_device(logits, dev) || !on_device(out_tok, dev) || !on_device(params, dev) || !on_device(uniforms, dev) ||
+      !on_device(out_prob, dev) || !on_device(row_status, dev) || !on_device(hist, dev) || !on_device(hist_len, dev) ||
+      !on_device(mask, dev))
+    return rl::set_error(RL_ERR_INVALID_ARG,
+                         "rl_sample_batch_static: every buffer must be device memory of the current device");
   rl::SpecArgs a = {};
   a.logits = logits;
   a.ld = ld;

@@ -57,7 +57,7 @@ __device__ __forceinline__ RowT make_rowt(float T) {
   RowT r;
   r.T = T;
   r.rT = __frcp_rn(T);
-  r.fast_div = (T >= 9.5367431640625e-07f) && (T <= 1048576.0f);
+  r.fast_div = fixed_div_ok(T);
   r.c = static_cast<float>(kLog2e / static_cast<double>(T));
   const double cb = static_cast<double>(kRbin) / static_cast<double>(T);
   r.cb_hi = static_cast<float>(cb);
@@ -67,9 +67,7 @@ __device__ __forceinline__ RowT make_rowt(float T) {
 }
 // l = (x - m) / T with IEEE rounding, as the CPU restatement computes it.
 __device__ __forceinline__ float exact_l(float x, float m, const RowT& r) {
-  const float d = sub_rn(x, m);
-  if (r.fast_div && (d == 0.0f || fabsf(d) >= 8.077935669e-28f)) return div_fixed(d, r.T, r.rT);
-  return div_rn(d, r.T);
+  return div_by(sub_rn(x, m), r.T, r.rT, r.fast_div != 0);
 }
 __device__ __forceinline__ float exact_e(float x, float m, const RowT& r) { return expf(exact_l(x, m, r)); }
 __device__ __forceinline__ float ex2_approx(float t) {
@@ -165,7 +163,7 @@ static_assert(256 * (4 + 8 + 8) <= kCW * 256 * 4, "radix walk bins");
 static_assert(kCW * kWcap >= 2 * kNB + 8 * kConsumers && kCollect <= 8 * kConsumers, "sort scratch");
 static_assert(kCW * kN <= 4 * kConsumers && kCW * kN * 8 <= kCW * 256 * 4, "item-end sort of the kept keys");
 static_assert(sizeof(ItemMeta) <= 128 && sizeof(Ctl) <= 128 && sizeof(Red) <= 256, "smem header");
-static_assert(3 * kNS + 4 <= 16, "mbarriers");
+static_assert(3 * kNS + 5 <= 16, "mbarriers");
 static_assert(kOffMeta + 2 * 128 <= kOffTopE, "meta");
 static_assert(kOffWcnt + 32 + kCW * 8 <= kOffMeta && (kOffWcnt + 32) % 8 == 0, "per-warp counts and histogram totals");
 static_assert(kOffStage % 128 == 0 && kOffMask % 16 == 0 && kOffSumS % 8 == 0 && kOffHist % 16 == 0, "alignment");
@@ -179,6 +177,7 @@ struct Smem {
   uint64_t* mfull;   // [2]
   uint64_t* mempty;  // [2]
   uint64_t* ready;   // [kNS] split kernel: the chunk in the stage is patched
+  uint64_t* never;   // a barrier nothing completes (RL_DEBUG_EXPIRE_WAIT)
   Ctl* ctl;
   Red* red;
   int* wcnt;
@@ -205,6 +204,7 @@ __device__ __forceinline__ Smem smem_map() {
   m.mfull = m.empty + kNS;
   m.mempty = m.mfull + 2;
   m.ready = m.mempty + 2;
+  m.never = m.ready + kNS;
   m.ctl = reinterpret_cast<Ctl*>(s + kOffCtl);
   m.red = reinterpret_cast<Red*>(s + kOffRed);
   m.wcnt = reinterpret_cast<int*>(s + kOffWcnt);
@@ -1614,6 +1614,14 @@ __device__ __forceinline__ void stream_row(const SpecArgs& a, const ItemMeta& mt
 // ---------------------------------------------------------------------------
 // Finisher
 // ---------------------------------------------------------------------------
+// Where a partial launch puts row r's sorted keys and its summary.
+__device__ __forceinline__ uint64_t* part_keys_of(const SpecArgs& a, int row) {
+  return a.part_keys + static_cast<int64_t>(row) * (a.part_packed ? kRec : kN);
+}
+__device__ __forceinline__ PartStats* part_stats_of(const SpecArgs& a, int row) {
+  return a.part_packed ? reinterpret_cast<PartStats*>(part_keys_of(a, row) + kN) : a.part_stats + row;
+}
+
 __device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status, int token, float prob) {
   if (a.part_keys) {
     // partial launch: an unfinished row is reported through its summary
@@ -1625,7 +1633,7 @@ __device__ __forceinline__ void write_row(const SpecArgs& a, int row, int status
     ps.z = 0.0;
     ps.nt = 0;
     ps.pad = 0;
-    a.part_stats[row] = ps;
+    *part_stats_of(a, row) = ps;
     return;
   }
   const bool ok = status == 0;
@@ -1978,7 +1986,7 @@ __device__ __forceinline__ void write_part(const SpecArgs& a, int row, float M, 
   ps.z = Z;
   ps.nt = nt;
   ps.pad = 0;
-  a.part_stats[row] = ps;
+  *part_stats_of(a, row) = ps;
 }
 
 // The finisher of a row (consumer threads). On entry sm.sums[0..nseg) hold
@@ -2094,7 +2102,7 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
     // partial launch: the row's (shard's) sorted list with global ids
     for (int i = tid; i < nt; i += kConsumers) {
       const uint64_t k = sm.top[i];
-      a.part_keys[static_cast<int64_t>(row) * kN + i] =
+      part_keys_of(a, row)[i] =
           cand_key(key_val(k), key_id(k) + static_cast<uint32_t>(a.vocab_offset));
     }
     if (tid == 0) write_part(a, row, M, argmax, nallow, flags, Z, nt);
@@ -2789,6 +2797,9 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   if (tid == 0) sm.ctl->tau_shared = 0ull;
   if (lane == 0) sm.wcnt[warp] = 0;
   cbar();
+  // RL_DEBUG_EXPIRE_WAIT: a bounded wait on a barrier that nothing
+  // completes runs out, and the item reports a timeout like any wait would
+  if ((a.debug_flags & 1) && !mbar_wait(sm.never, 0u, 2000)) tmo = 1;
   bool pre_patched = false;
   if constexpr (MODE != 0 && es == 4) {
     // bound from the item's first chunk (f32, whole in the stage, no mask):
@@ -3197,6 +3208,7 @@ __global__ void __launch_bounds__(kThreads, 2) spec_pipe_kernel(const __grid_con
       mbar_init(&sm.mempty[s], kCW);
     }
     for (int s = 0; s < kNS; ++s) mbar_init(&sm.ready[s], 1);
+    mbar_init(sm.never, 1);
     sm.ctl->abort = 0;
     sm.ctl->tab_seq = 0;
     fence_mbar_init();
@@ -3316,6 +3328,15 @@ static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t strea
   return cudaGetLastError();
 }
 
+cudaError_t spec_configure_single() {
+  cudaError_t e = cudaFuncSetAttribute(spec_pipe_kernel<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(spec_pipe_kernel<uint16_t, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+  return e;
+}
+
 cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream) {
   if (args.B == 0) return cudaSuccess;
   SpecArgs a = args;
@@ -3418,6 +3439,16 @@ cudaError_t launch_beam_combine(const BeamArgs& b, cudaStream_t stream) {
 // Vocabulary shards: the G partial results of each row merged, then the
 // finisher's cutoff and draw. One CTA of kConsumers threads per row.
 // ---------------------------------------------------------------------------
+// Shard g's keys and summary of row r (separate arrays, or packed records
+// as one all-gather lays them out).
+__device__ __forceinline__ const uint64_t* merge_keys(const MergeArgs& m, int g, int row) {
+  return m.keys + (static_cast<int64_t>(g) * m.B + row) * (m.stats ? kN : kRec);
+}
+__device__ __forceinline__ PartStats merge_stats(const MergeArgs& m, int g, int row) {
+  if (m.stats) return m.stats[static_cast<int64_t>(g) * m.B + row];
+  return *reinterpret_cast<const PartStats*>(merge_keys(m, g, row) + kN);
+}
+
 __global__ void __launch_bounds__(kConsumers) shard_merge_kernel(const __grid_constant__ MergeArgs m) {
   __shared__ uint64_t keys[kMergeMax];
   __shared__ uint64_t top[kN];
@@ -3432,7 +3463,7 @@ __global__ void __launch_bounds__(kConsumers) shard_merge_kernel(const __grid_co
   float M = RL_NEG_INF;
   int argmax = INT_MAX, nallow = 0, flags = 0;
   for (int g = 0; g < m.G; ++g) {
-    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    const PartStats ps = merge_stats(m, g, row);
     nallow += ps.nallow;
     flags |= ps.flags;
     if (ps.nallow == 0) continue;
@@ -3460,16 +3491,16 @@ __global__ void __launch_bounds__(kConsumers) shard_merge_kernel(const __grid_co
   const double cd = kLog2e / static_cast<double>(T);
   double Z = 0.0;
   for (int g = 0; g < m.G; ++g) {
-    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    const PartStats ps = merge_stats(m, g, row);
     if (ps.nallow > 0 && ps.m > RL_NEG_INF) Z += ps.z * exp2((static_cast<double>(ps.m) - static_cast<double>(M)) * cd);
   }
   const int K = min(prm.top_k, nallow);
   // a shard list holding K keys bounds the row's K-th key by its K-th one
   uint64_t bound = 0ull;
   for (int g = 0; g < m.G; ++g) {
-    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    const PartStats ps = merge_stats(m, g, row);
     if (ps.nt >= K) {
-      const uint64_t kk = m.keys[(static_cast<int64_t>(g) * m.B + row) * kN + K - 1];
+      const uint64_t kk = merge_keys(m, g, row)[K - 1];
       bound = kk > bound ? kk : bound;
     }
   }
@@ -3477,9 +3508,9 @@ __global__ void __launch_bounds__(kConsumers) shard_merge_kernel(const __grid_co
   __syncthreads();
   for (int f = tid; f < m.G * kN; f += blockDim.x) {
     const int g = f / kN, j = f - g * kN;
-    const PartStats ps = m.stats[static_cast<int64_t>(g) * m.B + row];
+    const PartStats ps = merge_stats(m, g, row);
     if (j >= ps.nt) continue;
-    const uint64_t kk = m.keys[(static_cast<int64_t>(g) * m.B + row) * kN + j];
+    const uint64_t kk = merge_keys(m, g, row)[j];
     if (kk >= bound) keys[atomicAdd(&cnt, 1)] = kk;  // at most G * kN keys
   }
   __syncthreads();

@@ -98,8 +98,10 @@ struct SpecArgs {
   int list_cap;
   int32_t* list_cut;  // [B, 3] debug: K, position of the last kept entry, its id
   int vocab_offset;  // global id of local id 0 (vocabulary shards)
+  int debug_flags;   // RL_DEBUG_* switches of the handle
   uint64_t* part_keys;   // non-null: partial launch, no draw (see PartStats)
   PartStats* part_stats;
+  int part_packed;       // 1: row r's keys at part_keys + r * kRec, its stats right after them
   int nseg;          // segments per row
   int cps;           // chunks per segment
   int nitems;        // B * nseg
@@ -129,9 +131,11 @@ cudaError_t launch_fill_params(rl_row_params* p, int n, int top_k, cudaStream_t 
 
 // Vocabulary shards: the G partial results of each row merged and drawn.
 constexpr int kMergeMaxShards = 16;
+// A packed partial record: kN keys then the 32-byte PartStats (u64 units).
+constexpr int kRec = kN + 4;
 constexpr int kMergeMax = kMergeMaxShards * kN;
 struct MergeArgs {
-  const uint64_t* keys;    // [G, B, kN]
+  const uint64_t* keys;    // [G, B, kN], or packed records [G, B, kRec] (stats == nullptr)
   const PartStats* stats;  // [G, B]
   int G, B;
   const rl_row_params* params;
@@ -155,5 +159,8 @@ cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream
 // One segment per row (no per-item workspace: only ws.wovf is used), at most
 // max_ctas CTAs (the persistent CTAs loop over the rows).
 cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream);
+// Sets the single-kernel launch's shared-memory limit for both dtypes on the
+// current device (what its first launch per dtype would do otherwise).
+cudaError_t spec_configure_single();
 
 }  // namespace rl

@@ -21,7 +21,8 @@ rl_status alloc_workspace(rl_sampler* h) {
   bool ok = dalloc(&h->stage_logits, B * static_cast<size_t>(h->max_vocab)) &&
             dalloc(&h->stage_hist, B * static_cast<size_t>(h->max_history)) &&
             dalloc(&h->stage_hist_len, B) && dalloc(&h->stage_mask, B * h->mask_words) &&
-            dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_tok, B) &&
+            dalloc(&h->stage_params, B) && dalloc(&h->stage_u, B) && dalloc(&h->stage_T, B) &&
+            dalloc(&h->stage_p, B) && dalloc(&h->stage_tok, B) &&
             dalloc(&h->stage_prob, B) && dalloc(&h->stage_status, B);
   // spec kernel workspace: per-item summaries, candidate lists and
   // histograms that the streaming kernel hands to the finish kernel (one
@@ -32,6 +33,8 @@ rl_status alloc_workspace(rl_sampler* h) {
        dalloc(&h->ws.hcnt, items * kNB) && dalloc(&h->ws.hmass, items * kNB) &&
        dalloc(&h->ws.tabs, items * kHmax) && dalloc(&h->ws.tabn, items) &&
        dalloc(&h->ws.wovf, static_cast<size_t>(spec_max_ctas(h->num_sms)) * kCW * kWovf);
+  if (h->flags & RL_CREATE_SHARDED)
+    ok = ok && dalloc(&h->shard_send, B * kRec) && dalloc(&h->shard_recv, static_cast<size_t>(kMergeMaxShards) * B * kRec);
   ok = ok && dalloc(&h->part_keys, B * kN) && dalloc(&h->part_stats, B) && dalloc(&h->beam_params, B) &&
        dalloc(&h->zero_u, B);
   if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
@@ -51,6 +54,8 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->stage_mask);
   cudaFree(h->stage_params);
   cudaFree(h->stage_u);
+  cudaFree(h->stage_T);
+  cudaFree(h->stage_p);
   cudaFree(h->stage_tok);
   cudaFree(h->stage_prob);
   cudaFree(h->stage_status);
@@ -63,6 +68,10 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->ws.tabs);
   cudaFree(h->ws.tabn);
   h->ws = {};
+  cudaFree(h->shard_send);
+  cudaFree(h->shard_recv);
+  h->shard_send = nullptr;
+  h->shard_recv = nullptr;
   cudaFree(h->part_keys);
   cudaFree(h->part_stats);
   cudaFree(h->beam_params);

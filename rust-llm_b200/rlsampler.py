@@ -28,8 +28,12 @@ RL_ERR_UNSUPPORTED = 7
 RL_ERR_NONFINITE = 8
 RL_F32 = 0
 RL_BF16 = 1
+RL_DEBUG_EXPIRE_WAIT = 1
+RL_CREATE_SHARDED = 1
+NCCL_ID_BYTES = 128  # RL_NCCL_ID_BYTES
 
 PART_KEYS = 128  # RL_PART_KEYS
+PART_REC = PART_KEYS + 4  # u64 words of a packed partial record (keys, then rl_part_stats)
 PART_STATS_DTYPE = np.dtype(
     [
         ("m", np.float32),
@@ -101,6 +105,8 @@ def lib():
         L.rl_sample_host.argtypes = [P, P, I, I, P, P, I, P, I64, P, P, P, P]
         L.rl_decoder_sample.restype = I
         L.rl_decoder_sample.argtypes = [P, P, I, I, I64, P, P, P, P, P, P]
+        L.rl_decoder_sample_host.restype = I
+        L.rl_decoder_sample_host.argtypes = [P, P, I, I, P, P, P, P, P]
         L.rl_greedy.restype = I
         L.rl_greedy.argtypes = [P, P, I, I, I64, P, P]
         L.rl_grammar_greedy.restype = I
@@ -111,6 +117,18 @@ def lib():
         L.rl_sample_partial.argtypes = [P, P, I, I, I, I64, I, P, P, I, P, I64, P, P, P, P]
         L.rl_sample_merge.restype = I
         L.rl_sample_merge.argtypes = [P, I, I, P, P, P, P, P, P, P, P]
+        L.rl_sample_sharded.restype = I
+        L.rl_sample_sharded.argtypes = [P, P, P, I, I, I, I64, I, I, P, P, I, P, I64, P, P, P, P, P, P]
+        L.rl_nccl_unique_id.restype = I
+        L.rl_nccl_unique_id.argtypes = [P]
+        L.rl_nccl_comm_init.restype = I
+        L.rl_nccl_comm_init.argtypes = [ctypes.POINTER(P), I, P, I]
+        L.rl_nccl_comm_destroy.restype = I
+        L.rl_nccl_comm_destroy.argtypes = [P]
+        L.rl_sampler_set_debug.restype = I
+        L.rl_sampler_set_debug.argtypes = [P, ctypes.c_uint32]
+        L.rl_selfcheck_div.restype = I
+        L.rl_selfcheck_div.argtypes = [P, I, P, I, P, P, P]
         _lib = L
     return _lib
 
@@ -150,6 +168,10 @@ class Sampler:
               "rl_sampler_create")
         self.h = h
         self.device = device
+
+    def set_debug(self, flags):
+        """rl_sampler_set_debug: RL_DEBUG_* switches (0 = off)."""
+        check(lib().rl_sampler_set_debug(self.h, int(flags)), "rl_sampler_set_debug")
 
     def close(self):
         if self.h:
@@ -249,6 +271,31 @@ class Sampler:
               "rl_sample_merge")
         return out_tok, out_prob, row_status
 
+    def sample_sharded(self, comm, logits_shard, vocab_offset, V_global, params, uniforms, hist=None, hist_len=None,
+                       mask_shard=None, out_tok=None, out_prob=None, row_status=None, stream=None):
+        """rl_sample_sharded: this rank's columns [vocab_offset, + width) of
+        the rows, one NCCL all-gather on `comm`, the merged draw (global ids).
+        The handle needs flags=RL_CREATE_SHARDED."""
+        import torch
+
+        B, W = logits_shard.shape
+        dtype = RL_BF16 if logits_shard.dtype == torch.bfloat16 else RL_F32
+        dev = logits_shard.device
+        if out_tok is None:
+            out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+        if out_prob is None:
+            out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        if row_status is None:
+            row_status = torch.empty(B, dtype=torch.int32, device=dev)
+        hs = hist.shape[1] if hist is not None else 0
+        ms = mask_shard.shape[1] if mask_shard is not None else 0
+        check(lib().rl_sample_sharded(self.h, ctypes.c_void_p(comm), _ptr(logits_shard), dtype, B, W,
+                                      logits_shard.stride(0), int(vocab_offset), int(V_global), _ptr(hist),
+                                      _ptr(hist_len), hs, _ptr(mask_shard), ms, _ptr(params), _ptr(uniforms),
+                                      _ptr(out_tok), _ptr(out_prob), _ptr(row_status), _stream(stream)),
+              "rl_sample_sharded")
+        return out_tok, out_prob, row_status
+
     # -- beam search ----------------------------------------------------------------
     def beam_step(self, logits, items, beams, scores, done, lens=None, alpha=1.0, eos=2, log_softmax=1,
                   n_out=None, stream=None):
@@ -317,8 +364,56 @@ def sample_static(logits, params, uniforms, hist=None, hist_len=None, mask=None,
         row_status = torch.empty(B, dtype=torch.int32, device=dev)
     hs = hist.shape[1] if hist is not None else 0
     ms = mask.shape[1] if mask is not None else 0
+    # the entry point runs on the current device with that device's scratch:
+    # make the tensors' device current, and use its stream
+    with torch.cuda.device(dev):
+        if stream is None:
+            stream = torch.cuda.current_stream(dev)
+        _call_static(logits, dtype, B, V, hist, hist_len, hs, mask, ms, params, uniforms, out_tok, out_prob,
+                     row_status, stream)
+    return out_tok, out_prob, row_status
+
+
+def _call_static(logits, dtype, B, V, hist, hist_len, hs, mask, ms, params, uniforms, out_tok, out_prob, row_status,
+                 stream):
     check(lib().rl_sample_batch_static(_ptr(logits), dtype, B, V, logits.stride(0), _ptr(hist), _ptr(hist_len), hs,
                                        _ptr(mask), ms, _ptr(params), _ptr(uniforms), _ptr(out_tok), _ptr(out_prob),
                                        _ptr(row_status), _stream(stream)),
           "rl_sample_batch_static")
-    return out_tok, out_prob, row_status
+
+
+def selfcheck_div(a, T, stream=None):
+    """rl_selfcheck_div over device float32 tensors a [n] and T [nT]: per T the
+    count of quotients that differ in any bit from IEEE division, and whether
+    the fixed-divisor path is in use for it. Returns two cpu numpy arrays."""
+    import torch
+
+    nT = T.numel()
+    mism = torch.zeros(nT, dtype=torch.int32, device=a.device)
+    fast = torch.zeros(nT, dtype=torch.int32, device=a.device)
+    check(lib().rl_selfcheck_div(_ptr(a), a.numel(), _ptr(T), nT, _ptr(mism), _ptr(fast), _stream(stream)),
+          "rl_selfcheck_div")
+    torch.cuda.synchronize(a.device)
+    return mism.cpu().numpy().astype(np.uint32), fast.cpu().numpy()
+
+
+def nccl_unique_id() -> bytes:
+    """rl_nccl_unique_id: a new NCCL communicator id (made on one rank)."""
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    check(lib().rl_nccl_unique_id(ctypes.cast(buf, ctypes.c_void_p)), "rl_nccl_unique_id")
+    return buf.raw
+
+
+def nccl_comm_init(nranks: int, id_bytes: bytes, rank: int) -> int:
+    """rl_nccl_comm_init on the current device: returns the ncclComm_t as an int."""
+    if len(id_bytes) != NCCL_ID_BYTES:
+        raise ValueError("an NCCL id has 128 bytes")
+    buf = ctypes.create_string_buffer(bytes(id_bytes), NCCL_ID_BYTES)
+    c = ctypes.c_void_p()
+    check(lib().rl_nccl_comm_init(ctypes.byref(c), int(nranks), ctypes.cast(buf, ctypes.c_void_p), int(rank)),
+          "rl_nccl_comm_init")
+    return c.value
+
+
+def nccl_comm_destroy(comm: int) -> None:
+    check(lib().rl_nccl_comm_destroy(ctypes.c_void_p(comm)), "rl_nccl_comm_destroy")

@@ -185,3 +185,65 @@ def test_shard_merge_rejects_unsupported_rows(sampler):
         stats.append(s)
     tok, prob, st = [t.cpu().numpy() for t in sampler.sample_merge(torch.stack(keys), torch.stack(stats), p, u)]
     assert st[0] == 0 and st[1] == rlsampler.RL_ERR_UNSUPPORTED and tok[1] == -1
+
+
+def test_beam_config4_steps(sampler):
+    """Config 4 over 10 seeded steps (16 items x 8 beams x V 151936), against
+    the oracle; near-tie swaps counted into the parity record."""
+    from conftest import parity_add
+
+    steps = 10
+    swaps = 0
+    for step in range(steps):
+        bb = workloads.config4(step)
+        n_out = 2 * bb.beams
+        got = _beam_gpu(sampler, bb, n_out)
+        ref = oracle.beam_step(bb.logits, bb.items, bb.beams, bb.scores, bb.done, bb.lens, bb.alpha, bb.eos, 1,
+                               n_out)
+        swaps += _beam_agree(got, ref)
+    assert swaps <= steps
+    parity_add("config4_beam", steps=steps, candidates=steps * 16 * 16, near_tie_swaps=swaps)
+
+
+def test_shard_config5_steps(sampler):
+    """Config 5 (vocabulary shards, bf16, top_k 64, top_p 0.95) over 20
+    seeded steps with G = 8 shards merged on one device, 64 rows a step,
+    against the oracle on the whole row."""
+    from conftest import parity_add
+
+    steps = 20
+    G = 8
+    dev = "cuda:0"
+    n = dict(rows=0, tokens_equal=0, boundary=0, prob_on_cut_boundary=0)
+    for step in range(steps):
+        rows = list(range(step % 16, 1024, 16))
+        batch = workloads.config5_rows(step, rows=rows)
+        lg = torch.from_numpy(batch.bf16_bits.view(np.int16)).to(dev).view(torch.bfloat16)
+        p = rlsampler.params_tensor(batch.params, dev)
+        u = torch.from_numpy(batch.uniforms).to(dev)
+        hist = torch.from_numpy(batch.hist).to(dev)
+        hl = torch.from_numpy(batch.hist_len).to(dev)
+        V = lg.shape[1]
+        keys, stats = [], []
+        for off, w in sharded.shard_bounds(V, G):
+            k, s = sampler.sample_partial(lg[:, off:off + w], off, p, hist, hl)
+            keys.append(k)
+            stats.append(s)
+        tok, prob, st = [t.cpu().numpy() for t in sampler.sample_merge(torch.stack(keys), torch.stack(stats), p, u)]
+        for b in range(len(rows)):
+            prm = {k: batch.params[b][k].item() for k in batch.params.dtype.names}
+            r = oracle.spec_sample_row(batch.logits[b], batch.hist[b], None, prm, batch.uniforms[b])
+            assert st[b] == r.status == 0
+            n["rows"] += 1
+            if tok[b] != r.token:
+                assert min(r.draw_margin, r.cut_margin) < BOUNDARY, f"step {step} row {rows[b]}"
+                n["boundary"] += 1
+                continue
+            n["tokens_equal"] += 1
+            if r.cut_margin < BOUNDARY and abs(prob[b] - r.prob) > PROB_RTOL * abs(r.prob):
+                # same token, but the cutoff (and so the renormalising mass)
+                # sits on a CDF boundary
+                n["prob_on_cut_boundary"] = n.get("prob_on_cut_boundary", 0) + 1
+                continue
+            np.testing.assert_allclose(prob[b], r.prob, rtol=PROB_RTOL)
+    parity_add("config5_sharded_G8", **n)

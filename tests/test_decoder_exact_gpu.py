@@ -155,11 +155,98 @@ def test_nonfinite_rows_return_minus_one(sampler):
     assert 0 <= tok[2] < V
 
 
-def test_rejects_oversized_rows(sampler):
-    big = rlsampler.Sampler(0, max_batch=1, max_vocab=60000, max_history=0)
+def test_rejects_rows_beyond_the_handle(sampler):
+    small = rlsampler.Sampler(0, max_batch=1, max_vocab=60000, max_history=0)
     try:
         P = None
-        st = rlsampler.lib().rl_decoder_sample(big.h, 1, 1, 60000, 60000, 1, 1, 1, 1, P, P)
+        st = rlsampler.lib().rl_decoder_sample(small.h, 1, 1, 60001, 60001, 1, 1, 1, 1, P, P)
         assert st == rlsampler.RL_ERR_SHAPE
     finally:
-        big.close()
+        small.close()
+
+
+@pytest.fixture(scope="module")
+def wide():
+    s = rlsampler.Sampler(0, max_batch=1024, max_vocab=151936, max_history=0)
+    yield s
+    s.close()
+
+
+@pytest.mark.parametrize("V", [53249, 128256, 151936])
+def test_rows_longer_than_shared_memory(wide, V):
+    """Rows beyond one CTA's shared memory run on the handle's staging buffer."""
+    r = np.random.default_rng(V + 3)
+    B = 6
+    lg = r.normal(0.0, 3.0, (B, V)).astype(np.float32)
+    lg[:, r.integers(0, V, 5)] += np.float32(8.0)
+    U = r.random(B).astype(np.float32)
+    T = np.array([1.0, 0.7, 1.3, 0.0, 1.0, 2.0], np.float32)
+    P = np.array([0.9, 0.95, 0.5, 1.0, 1.0, 0.99], np.float32)
+    tok, prob = run(wide, lg, T, P, U, ld=V + 5)
+    compare(lg, T, P, U, tok, prob, max_boundary=1)
+
+
+def _host(s, lg, T, P, U):
+    B, V = lg.shape
+    tok = np.empty(B, np.int32)
+    prob = np.empty(B, np.float32)
+    x = np.ascontiguousarray(lg, np.float32)
+    rlsampler.check(rlsampler.lib().rl_decoder_sample_host(
+        s.h, rlsampler._ptr(x), B, V, rlsampler._ptr(np.ascontiguousarray(T, np.float32)),
+        rlsampler._ptr(np.ascontiguousarray(P, np.float32)), rlsampler._ptr(np.ascontiguousarray(U, np.float32)),
+        rlsampler._ptr(tok), rlsampler._ptr(prob)), "rl_decoder_sample_host")
+    return tok, prob
+
+
+@pytest.mark.parametrize("V", [32000, 151936])
+def test_host_entry_matches_oracle(wide, V):
+    """rl_decoder_sample_host: host slices in, host tokens out (the &[f32]
+    Decoder::sample_with_params signature)."""
+    r = np.random.default_rng(V + 11)
+    B = 16
+    lg = r.normal(0.0, 3.0, (B, V)).astype(np.float32)
+    U = r.random(B).astype(np.float32)
+    T = r.uniform(0.5, 1.5, B).astype(np.float32)
+    P = r.uniform(0.5, 1.0, B).astype(np.float32)
+    tok, prob = _host(wide, lg, T, P, U)
+    compare(lg, T, P, U, tok, prob, max_boundary=1)
+    # the device entry on the same rows gives the same results
+    dtok, dprob = run(wide, lg, T, P, U)
+    assert np.array_equal(tok, dtok) and np.array_equal(prob, dprob)
+
+
+def test_config1_all_steps(wide):
+    """Config 1 (Decoder::sample at the CLI defaults: T 1.0, top_p 0.9) over all
+    of its 10,000 seeded steps, batched as rows, against the oracle; boundary
+    cases counted into the parity record."""
+    from conftest import parity_add
+
+    steps = 10000
+    lg = np.empty((steps, 32000), np.float32)
+    U = np.empty(steps, np.float32)
+    for st in range(steps):
+        b = workloads.config1(st)
+        lg[st] = b.logits[0]
+        U[st] = b.uniforms[0]
+    T = np.full(steps, 1.0, np.float32)
+    P = np.full(steps, 0.9, np.float32)
+    tok = np.empty(steps, np.int32)
+    prob = np.empty(steps, np.float32)
+    for b0 in range(0, steps, 1000):
+        sl = slice(b0, b0 + 1000)
+        tok[sl], prob[sl] = run(wide, lg[sl], T[sl], P[sl], U[sl])
+    import os
+
+    ref_tok, ref_prob = oracle.decoder_sample_batch(lg, T, P, U, nthreads=max(1, min(32, os.cpu_count() or 1)))
+    diff = np.nonzero(tok != ref_tok)[0]
+    boundary = 0
+    for b in diff:
+        r = oracle.decoder_sample(lg[b], T[b], P[b], U[b])
+        assert min(r["draw_margin"], r["cut_margin"]) < BOUNDARY, f"step {b}: {tok[b]} vs {ref_tok[b]}"
+        boundary += 1
+    same = tok == ref_tok
+    np.testing.assert_allclose(prob[same], ref_prob[same], rtol=PROB_RTOL)
+    exact = int((prob[same].view(np.uint32) == ref_prob[same].view(np.uint32)).sum())
+    assert exact >= 0.99 * same.sum()
+    parity_add("config1_ref_exact", rows=steps, tokens_equal=int(same.sum()), boundary=boundary,
+               probs_bit_identical=exact)

@@ -69,7 +69,8 @@ def oracle_rows(batch, list_cap):
 def compare(batch, gpu, list_cap=1024, label="", key=None):
     tok, prob, st, lids, lps, llen, cut = gpu
     refs = oracle_rows(batch, list_cap)
-    n = dict(rows=0, tokens_equal=0, boundary=0, kept_set_checked=0, cut_boundary=0, lists_checked=0)
+    n = dict(rows=0, tokens_equal=0, boundary=0, kept_set_checked=0, cut_boundary=0, lists_checked=0,
+             prob_on_cut_boundary=0)
     for b, r in enumerate(refs):
         exp_st = 0 if r.status == 0 else rlsampler.RL_ERR_NONFINITE
         assert st[b] == exp_st, f"{label} row {b}: status {st[b]} vs {exp_st}"
@@ -100,6 +101,11 @@ def compare(batch, gpu, list_cap=1024, label="", key=None):
             n["boundary"] += 1
             continue
         n["tokens_equal"] += 1
+        if r.cut_margin < BOUNDARY and abs(prob[b] - r.prob) > PROB_RTOL * abs(r.prob):
+            # same token, but the cutoff (and so the renormalising mass) sits
+            # on a CDF boundary
+            n["prob_on_cut_boundary"] = n.get("prob_on_cut_boundary", 0) + 1
+            continue
         np.testing.assert_allclose(prob[b], r.prob, rtol=PROB_RTOL, err_msg=f"{label} row {b}: prob")
     parity_add(key or label, **n)
     return n["boundary"]

@@ -1,6 +1,8 @@
 """Host side of vocabulary-sharded sampling, on CPU: the shard split, the
-all-gather layout over two gloo ranks, and the merge identity (the G
-partial results determine the one-piece result) checked against the oracle.
+packed records and their single all-gather over two gloo ranks (the layout
+rl_sample_sharded's NCCL all-gather produces), the communicator-id exchange
+of ShardedSampler, and the merge identity (the G partial results determine
+the one-piece result) checked against the oracle.
 
 The partial results here are computed with numpy from each rank's columns,
 in the layout rl_sample_partial writes (sorted uint64 keys, rl_part_stats).
@@ -115,12 +117,19 @@ def _rank_main(rank, world, port, V, B, out_dir):
             keys[b], stats[b] = k, st[0]
         kt = torch.from_numpy(keys.view(np.int64).copy())
         stt = torch.from_numpy(stats.view(np.uint8).reshape(B, -1).copy())
-        kall, sall = sharded.gather_partials(kt, stt)
+        rec = sharded.pack_records(kt, stt)
+        assert tuple(rec.shape) == (B, rlsampler.PART_REC)
+        gathered = sharded.gather_records(rec)  # one collective for keys and stats
+        assert tuple(gathered.shape) == (world, B, rlsampler.PART_REC)
+        kall, sall = sharded.unpack_records(gathered)
         assert tuple(kall.shape) == (world, B, rlsampler.PART_KEYS)
         assert tuple(sall.shape) == (world, B, rlsampler.PART_STATS_DTYPE.itemsize)
         np.save(os.path.join(out_dir, f"k{rank}.npy"), kall.numpy())
         np.save(os.path.join(out_dir, f"s{rank}.npy"), sall.numpy())
         np.save(os.path.join(out_dir, f"own{rank}.npy"), keys.view(np.int64))
+        # the communicator id made on rank 0 reaches every rank
+        uid = sharded.exchange_id(make_id=lambda: bytes(range(128)))
+        np.save(os.path.join(out_dir, f"id{rank}.npy"), np.frombuffer(uid, np.uint8))
     finally:
         dist.destroy_process_group()
 
@@ -133,6 +142,8 @@ def test_gather_layout_and_merge_identity_two_gloo_ranks(tmp_path):
                        start_method="spawn")
     k0, k1 = np.load(tmp_path / "k0.npy"), np.load(tmp_path / "k1.npy")
     assert np.array_equal(k0, k1)  # every rank holds the same gathered results
+    for g in range(world):
+        assert np.array_equal(np.load(tmp_path / f"id{g}.npy"), np.arange(128, dtype=np.uint8))
     for g in range(world):
         assert np.array_equal(k0[g], np.load(tmp_path / f"own{g}.npy"))  # rank g's result at index g
     stats = sharded.stats_view(np.load(tmp_path / "s0.npy"))
@@ -151,3 +162,20 @@ def test_gather_layout_and_merge_identity_two_gloo_ranks(tmp_path):
         else:
             np.testing.assert_allclose(prob, r.prob, rtol=1e-5)
     assert boundary <= 1
+
+
+def test_packed_records_round_trip():
+    """The packed record keeps the keys and the 32-byte summary of a row."""
+    B = 3
+    keys = torch.arange(B * rlsampler.PART_KEYS, dtype=torch.int64).view(B, -1) * 7919
+    st = np.zeros(B, rlsampler.PART_STATS_DTYPE)
+    st["m"] = [1.5, -2.0, 3.25]
+    st["argmax"] = [4, 5, 6]
+    st["z"] = [0.5, 1.25, 9.0]
+    st["n"] = [128, 3, 0]
+    stats = torch.from_numpy(st.view(np.uint8).reshape(B, -1).copy())
+    rec = sharded.pack_records(keys, stats)
+    k2, s2 = sharded.unpack_records(rec)
+    assert torch.equal(k2, keys) and torch.equal(s2, stats)
+    back = sharded.stats_view(s2)
+    assert np.array_equal(back, st)

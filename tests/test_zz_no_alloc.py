@@ -101,3 +101,82 @@ def test_static_bf16_and_greedy_rows():
         got = [t.cpu().numpy() for t in rlsampler.sample_static(lg, p, u, hist, hl)]
         assert got[0][0] == ref[0][0]  # greedy row: argmax
         _agree(batch, got, ref)
+
+
+@pytest.mark.gpu
+def test_static_masked_rows_match_handle_path():
+    """Grammar masks through the entry that allocates nothing (config 3)."""
+    import torch
+
+    dev = "cuda:0"
+    batch = workloads.config3(4)
+    lg = torch.from_numpy(batch.logits).to(dev)
+    p = rlsampler.params_tensor(batch.params, dev)
+    u = torch.from_numpy(batch.uniforms).to(dev)
+    mask = torch.from_numpy(batch.mask.view(np.int32)).to(dev)
+    s = rlsampler.Sampler(0, max_batch=64, max_vocab=batch.logits.shape[1], max_history=0)
+    try:
+        ref = [t.cpu().numpy() for t in s.sample(lg, p, u, mask=mask)]
+    finally:
+        s.close()
+    for _ in range(2):
+        got = [t.cpu().numpy() for t in rlsampler.sample_static(lg, p, u, mask=mask)]
+        _agree(batch, got, ref)
+
+
+@pytest.mark.gpu
+def test_static_allocates_nothing_and_replays_in_a_graph():
+    """No device memory is taken by a call (free memory unchanged), and a
+    call captured into a CUDA graph after a warm call replays to the eager
+    results, twice."""
+    import torch
+
+    dev = "cuda:0"
+    batch = workloads.config2(5, rows=list(range(0, 256, 16)))
+    lg = torch.from_numpy(batch.logits).to(dev)
+    p = rlsampler.params_tensor(batch.params, dev)
+    u = torch.from_numpy(batch.uniforms).to(dev)
+    hist = torch.from_numpy(batch.hist).to(dev)
+    hl = torch.from_numpy(batch.hist_len).to(dev)
+    B = lg.shape[0]
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+    rlsampler.sample_static(lg, p, u, hist, hl, out_tok=tok, out_prob=prob, row_status=st)  # warm
+    torch.cuda.synchronize()
+    eager = (tok.cpu().numpy().copy(), prob.cpu().numpy().copy(), st.cpu().numpy().copy())
+    free0, _ = torch.cuda.mem_get_info()
+    rlsampler.sample_static(lg, p, u, hist, hl, out_tok=tok, out_prob=prob, row_status=st)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            rlsampler.sample_static(lg, p, u, hist, hl, out_tok=tok, out_prob=prob, row_status=st)
+    for _ in range(2):
+        tok.fill_(-7)
+        g.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(tok.cpu().numpy(), eager[0])
+        assert np.array_equal(prob.cpu().numpy(), eager[1])
+        assert np.array_equal(st.cpu().numpy(), eager[2])
+    del g
+
+
+@pytest.mark.gpu
+def test_static_rejects_host_buffers():
+    """Buffers that are not device memory of the current device are refused
+    before any launch."""
+    import torch
+
+    dev = "cuda:0"
+    lg = torch.zeros((2, 64), device=dev)
+    p = rlsampler.params_tensor(np.zeros(2, rlsampler.ROW_PARAMS_DTYPE), dev)
+    u = torch.zeros(2, device=dev)
+    host_tok = torch.empty(2, dtype=torch.int32, pin_memory=True)
+    with pytest.raises(rlsampler.RLError) as e:
+        rlsampler.sample_static(lg, p, u, out_tok=host_tok)
+    assert e.value.status == rlsampler.RL_ERR_INVALID_ARG
