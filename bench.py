@@ -1,21 +1,31 @@
-"""Benchmark of the B200 sampler on the heterogeneous continuous-batch
-workload: batch 256 x vocab 128256 fp32 logits per step, per-row temperature,
-top-k, top-p and repetition / presence / frequency penalties over a 512-token
-history (the reference's serial per-sequence sampling loop,
-src/inference.rs:112-138 -> src/decoder.rs:35-100, batched).
+"""Benchmark of the B200 sampler (rust-llm's logits -> token path,
+src/decoder.rs, batched) on the five workloads:
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  1  single sequence at the CLI defaults: B 1 x V 32000, top_k 40, top_p 0.9,
+     repetition penalty over a 64-token history (microseconds per token)
+  2  heterogeneous continuous batch: B 256 x V 128256 f32, per-row T, top_k,
+     top_p and penalties over a 512-token history (the headline; tokens/s)
+  3  grammar-constrained: B 64 x V 32000 with bit-packed allowed masks
+  4  beam step: 16 items x 8 beams x V 151936 (beam extensions/s)
+  5  vocabulary shards: B 1024 x V 256000 bf16 split across the ranks,
+     merged by one NCCL all-gather (tokens/s, strong scaling)
 
-One process per GPU (torchrun for N > 1). Batch rows are independent, so each
-rank samples its own 256-row batch with no collective on the data path
-(weak scaling); the time is the max over ranks of the device-timed region.
-Prints one JSON line on rank 0.
+    python bench.py [--config C] [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU (torchrun for N > 1); rank 0 prints one JSON line. For
+configs 1-4 every rank samples its own batch with no collective (weak
+scaling); config 5 splits one batch's vocabulary across the ranks. The
+default (config 2) line also carries the config-5 step at the same N under
+"vocab_shards", so a scaling run measures both.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
+import datetime
 import json
 import os
+import platform
 import statistics
 import subprocess
 import sys
@@ -27,15 +37,36 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "rust-llm_b200"))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
-B, V, H = 256, 128256, 512
-METRIC = "sampled tokens/s at batch 256 x vocab 128256 fp32"
-UNIT = "tokens/s"
-POOL = 8  # distinct step buffers cycled through (8 x 131 MB > L2)
+POOL = 8  # distinct step buffers cycled through (inputs larger than L2 for config 2)
+
+CONFIGS = {
+    1: dict(workload="single_seq_cli_defaults_b1_v32000", B=1, V=32000, H=64,
+            metric="microseconds per sampled token at batch 1 x vocab 32000 (CLI defaults)", unit="us/token",
+            higher=False),
+    2: dict(workload="hetero_batch_b256_v128256_f32", B=256, V=128256, H=512,
+            metric="sampled tokens/s at batch 256 x vocab 128256 fp32", unit="tokens/s", higher=True),
+    3: dict(workload="grammar_b64_v32000", B=64, V=32000, H=0,
+            metric="sampled tokens/s at batch 64 x vocab 32000 with grammar masks", unit="tokens/s", higher=True),
+    4: dict(workload="beam_16x8_v151936", B=128, V=151936, H=0,
+            metric="beam extensions/s at 16 items x 8 beams x vocab 151936", unit="beam extensions/s", higher=True),
+    5: dict(workload="vocab_shard_b1024_v256000_bf16", B=1024, V=256000, H=256,
+            metric="sampled tokens/s at batch 1024 x vocab 256000 bf16, vocabulary split across the GPUs",
+            unit="tokens/s", higher=True),
+}
 
 
-def algorithmic_bytes(b=B, v=V, h=H):
-    # logits + history + hist_len + params + uniforms + token + prob + status
-    return b * v * 4 + b * h * 4 + b * 4 + b * 24 + b * 4 + b * 4 + b * 4 + b * 4
+def algorithmic_bytes(cfg, n_ranks=1):
+    """Bytes one step must move at least (logits once, history, params,
+    masks, outputs), per GPU."""
+    c = CONFIGS[cfg]
+    B, V, H = c["B"], c["V"], c["H"]
+    if cfg == 4:
+        return B * V * 4 + B * (4 + 1 + 4) + 16 * 16 * (4 + 4 + 4 + 1)
+    if cfg == 5:
+        w = -(-V // n_ranks)
+        return B * w * 2 + B * H * 4 + B * 4 + B * 24 + B * 4 + B * 12 + (B * 1056 * n_ranks if n_ranks > 1 else 0)
+    mask = B * ((V + 31) // 32) * 4 if cfg == 3 else 0
+    return B * V * 4 + B * H * 4 + B * 4 + B * 24 + B * 4 + B * 12 + mask
 
 
 def measured_peak():
@@ -52,6 +83,17 @@ def committed_traffic():
             return json.load(f)
     except Exception:
         return {}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return platform.processor() or "unknown"
 
 
 class ClockSampler:
@@ -99,16 +141,17 @@ class ClockSampler:
                     reasons.add(n)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_params(step, rng_seed=2000):
+# ---------------------------------------------------------------------------
+# Step inputs (seeded, synthetic: the reference publishes no data set)
+# ---------------------------------------------------------------------------
+def config2_params(step, B, V, H):
     import workloads
-
-    r = np.random.Generator(np.random.PCG64(rng_seed + step))
     from rlsampler import ROW_PARAMS_DTYPE
 
+    r = np.random.Generator(np.random.PCG64(2000 + step))
     p = np.zeros(B, ROW_PARAMS_DTYPE)
     p["temperature"] = r.uniform(0.5, 1.5, B)
     p["top_k"] = r.choice(np.array([0, 20, 50, 100]), B)
@@ -121,77 +164,273 @@ def make_params(step, rng_seed=2000):
     return p, hist, u
 
 
-def cpu_baseline(max_seconds=10.0, max_steps=400, distinct=2):
-    """The CPU restatement of the sampler (oracle/, a port: the Rust
-    reference cannot be built here) on this host's cores, over a bounded
-    sample of config-2 steps (about max_seconds of timed sampling, cycling
-    over `distinct` generated step batches)."""
-    import oracle
+def make_pool(cfg, dev, rank, n_ranks, count=POOL):
+    """`count` device-resident steps of the configuration (this rank's part:
+    its own rows for configs 1-4, its own columns of shared rows for 5)."""
+    import torch
+
+    import rlsampler
     import workloads
 
-    nthreads = os.cpu_count() or 1
-    batches = [workloads.config2(i) for i in range(distinct)]
-    hl = np.full(B, H, np.int32)
-    rows = 0
-    elapsed = 0.0
-    steps = 0
-    while steps < max_steps and elapsed < max_seconds:
-        batch = batches[steps % distinct]
-        t0 = time.perf_counter()
-        oracle.spec_sample_batch(batch.logits, batch.hist, hl, None, batch.params, batch.uniforms,
-                                 nthreads=nthreads)
-        elapsed += time.perf_counter() - t0
-        rows += B
-        steps += 1
-    return {"value": rows / elapsed, "unit": UNIT, "cores": nthreads, "kind": "port",
-            "sample": f"{steps} steps x {B} rows x {V} vocab of the same workload ({distinct} distinct step "
-                      f"batches cycled), {nthreads} threads, {elapsed:.1f} s of sampling"}
+    c = CONFIGS[cfg]
+    B, V, H = c["B"], c["V"], c["H"]
+    gen = torch.Generator(device=dev)
+    pool = []
+    for i in range(count):
+        gen.manual_seed(1000 * cfg + i + (7919 * rank if cfg != 5 else 0))
+        d = {}
+        if cfg == 2:
+            prior = (-1.1 * torch.log(torch.arange(V, device=dev, dtype=torch.float64) + 1.0)).float()
+            d["logits"] = torch.randn((B, V), generator=gen, device=dev, dtype=torch.float32) * 4.0 + prior
+            p, hist, u = config2_params(i + 100 * rank, B, V, H)
+        elif cfg in (1, 3):
+            b = workloads.config1(i + 100 * rank) if cfg == 1 else workloads.config3(i + 100 * rank)
+            d["logits"] = torch.from_numpy(b.logits).to(dev)
+            p, u = b.params, b.uniforms
+            hist = b.hist
+            if b.mask is not None:
+                d["mask"] = torch.from_numpy(b.mask.view(np.int32)).to(dev)
+        elif cfg == 4:
+            bb = workloads.config4(i + 100 * rank)
+            d["logits"] = torch.from_numpy(bb.logits).to(dev)
+            d["scores"] = torch.from_numpy(bb.scores).to(dev)
+            d["done"] = torch.from_numpy(bb.done).to(dev)
+            d["lens"] = torch.from_numpy(bb.lens).to(dev)
+            pool.append(d)
+            continue
+        else:  # 5: the full rows, bf16; each rank keeps its own columns
+            import sharded
+
+            off, w = sharded.shard_bounds(V, n_ranks)[rank] if n_ranks > 1 else (0, V)
+            full = (torch.randn((B, V), generator=gen, device=dev, dtype=torch.float32) * 4.0).to(torch.bfloat16)
+            d["logits"] = full[:, off:off + w].contiguous()
+            del full
+            r = np.random.Generator(np.random.PCG64(5000 + i))
+            from rlsampler import ROW_PARAMS_DTYPE
+
+            p = np.zeros(B, ROW_PARAMS_DTYPE)
+            p["temperature"] = 0.8
+            p["top_k"] = 64
+            p["top_p"] = 0.95
+            p["repeat_penalty"] = 1.2
+            hist = r.integers(0, V, (B, H)).astype(np.int32)
+            u = workloads.uniforms(5, i, B)
+        d["params"] = rlsampler.params_tensor(p, dev)
+        d["u"] = torch.from_numpy(np.ascontiguousarray(u)).to(dev)
+        if hist is not None:
+            d["hist"] = torch.from_numpy(np.ascontiguousarray(hist)).to(dev)
+            d["hl"] = torch.full((B,), hist.shape[1], dtype=torch.int32, device=dev)
+        pool.append(d)
+    return pool
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle (a C++ restatement of src/decoder.rs; the Rust
+# reference cannot be built here) on this host's cores
+# ---------------------------------------------------------------------------
+def _host_step(d):
+    """A pool step's inputs on the host, in the oracle's layout."""
+    B = d["logits"].shape[0]
+    lg = d["logits"].float().cpu().numpy()
+    from rlsampler import ROW_PARAMS_DTYPE
+
+    p = d["params"].cpu().numpy().view(ROW_PARAMS_DTYPE)
+    hist = d["hist"].cpu().numpy() if "hist" in d else None
+    hl = d["hl"].cpu().numpy() if "hl" in d else None
+    mask = d["mask"].cpu().numpy().view(np.uint32) if "mask" in d else None
+    return lg, p, d["u"].cpu().numpy(), hist, hl, mask, B
+
+
+def _oracle_step(step, nthreads):
+    import oracle
+
+    lg, p, u, hist, hl, mask, B = step
+    tok, prob, bad = oracle.spec_sample_batch(lg, hist, hl, mask, p, u, nthreads=nthreads)
+    return tok, prob
+
+
+def cpu_baseline(cfg, host_steps, gpu_tokens, seconds=5.0):
+    """The oracle timed over a bounded sample of the same steps, on one
+    core and on all cores; its tokens are compared with the device's for
+    the same steps (parity counter)."""
+    nall = os.cpu_count() or 1
+    unit_per_step = CONFIGS[cfg]["B"]
+    out = {}
+    parity = None
+    for label, nth in (("1core", 1), ("all", nall)):
+        elapsed, steps = 0.0, 0
+        toks = []
+        while elapsed < seconds and steps < 100000:
+            st = host_steps[steps % len(host_steps)]
+            t0 = time.perf_counter()
+            tok, _ = _oracle_step(st, nth)
+            elapsed += time.perf_counter() - t0
+            if steps < len(host_steps):
+                toks.append(tok)
+            steps += 1
+        v = steps * unit_per_step / elapsed
+        out[label] = dict(value=(1e6 / v if cfg == 1 else v), steps=steps, seconds=round(elapsed, 2), threads=nth)
+        if parity is None and gpu_tokens is not None:
+            n = sum(len(t) for t in toks)
+            eq = sum(int((t == g).sum()) for t, g in zip(toks, gpu_tokens))
+            parity = {"rows_checked": n, "tokens_equal": eq,
+                      "note": "device tokens of timed steps vs the oracle on the same inputs; rows may differ only "
+                              "where a draw or cutoff is within 1e-6 of a CDF boundary"}
+    c = CONFIGS[cfg]
+    line = {"value": out["all"]["value"], "unit": c["unit"], "cores": nall, "kind": "port",
+            "cpu_model": cpu_model(), "one_core": out["1core"]["value"], "all_cores": out["all"]["value"],
+            "sample": f"{out['all']['steps']} steps of the same workload on {nall} threads "
+                      f"({out['all']['seconds']} s) and {out['1core']['steps']} on one thread "
+                      f"({out['1core']['seconds']} s), cycling over {len(host_steps)} distinct steps"}
+    return line, parity
 
 
 def run_reference(args, rank, world):
-    line = {"impl": "reference", "metric": METRIC, "unit": UNIT, "higher_is_better": True}
+    """--impl reference: the CPU sampler (the oracle port of src/decoder.rs;
+    the Rust crate cannot be built here) on this host's cores, on whole
+    distinct batches of the same configuration. Rank 0 only."""
+    c = CONFIGS[args.config]
+    line = {"impl": "reference", "metric": c["metric"], "unit": c["unit"], "higher_is_better": c["higher"]}
     if rank != 0:
         return
     import oracle
     import workloads
 
     nthreads = os.cpu_count() or 1
-    batch = workloads.config2(0)
-    hl = np.full(B, H, np.int32)
-    # each step samples a bounded slice of the 256-row batch (full V)
-    rows_per_step = max(8, min(B, 4 * nthreads))
-    sl = slice(0, rows_per_step)
-    for _ in range(args.warmup):
-        oracle.spec_sample_batch(batch.logits[sl], batch.hist[sl], hl[sl], None, batch.params[sl],
-                                 batch.uniforms[sl], nthreads=nthreads)
+    cfg = args.config
+    B = c["B"]
+
+    def batch(i):
+        if cfg == 1:
+            b = workloads.config1(i)
+        elif cfg == 2:
+            b = workloads.config2(i)
+        elif cfg == 3:
+            b = workloads.config3(i)
+        elif cfg == 5:
+            b = workloads.config5_rows(i, rows=list(range(0, 1024, 16)))
+        else:
+            return workloads.config4(i)
+        return b
+
+    steps = [batch(i) for i in range(min(args.steps, 4))]
+
+    def run(b):
+        if cfg == 4:
+            oracle.beam_step(b.logits, b.items, b.beams, b.scores, b.done, b.lens, b.alpha, b.eos, 1, 2 * b.beams)
+            return b.items * b.beams
+        hl = b.hist_len
+        oracle.spec_sample_batch(b.logits, b.hist, hl, b.mask, b.params, b.uniforms, nthreads=nthreads)
+        return b.logits.shape[0]
+
+    for i in range(min(args.warmup, 3)):
+        run(steps[i % len(steps)])
+    # whole steps until K are done or the time budget runs out (the line
+    # reports the steps actually timed)
+    units, done = 0, 0
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        oracle.spec_sample_batch(batch.logits[sl], batch.hist[sl], hl[sl], None, batch.params[sl],
-                                 batch.uniforms[sl], nthreads=nthreads)
+    while done < args.steps:
+        units += run(steps[done % len(steps)])
+        done += 1
+        if time.perf_counter() - t0 > args.ref_seconds:
+            break
     dt = time.perf_counter() - t0
-    val = rows_per_step * args.steps / dt
+    v = units / dt
+    value = 1e6 / v if cfg == 1 else v
+    rows = (steps[0].items * steps[0].beams) if cfg == 4 else steps[0].logits.shape[0]
     line.update({
-        "value": val, "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": dt / args.steps * 1e3, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "hetero_batch_b256_v128256_f32", "global_batch": B,
-                                        "vocab": V, "history": H, "rows_per_step_timed": rows_per_step},
-        "cpu_baseline": {"value": val, "unit": UNIT, "cores": nthreads, "kind": "port",
-                         "sample": f"{rows_per_step} of the {B} rows per step, full vocab, {nthreads} threads"},
-        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "value": value, "n_gpus": args.gpus, "steps": done, "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / done * 1e3, "scaling": "weak" if cfg != 5 else "strong", "vs_baseline": None,
+        "dtype": "bf16" if cfg == 5 else "f32", "data": "synthetic",
+        "config": {"workload": c["workload"], "rows_per_step": rows, "vocab": c["V"],
+                   "distinct_steps": len(steps), "same_config": cfg != 5},
+        "cpu_baseline": {"value": value, "unit": c["unit"], "cores": nthreads, "kind": "port", "cpu_model": cpu_model(),
+                         "sample": f"{done} steps of {rows} rows (whole batches, {len(steps)} distinct), "
+                                   f"{nthreads} threads, {dt:.1f} s"},
+        "e2e": {"value": value, "unit": c["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# Device legs
+# ---------------------------------------------------------------------------
+def timed_loop(step_fn, steps, warmup, stream, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    for i in range(warmup):
+        step_fn(i)
+    torch.cuda.synchronize()
+    clk = ClockSampler(dev.index)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clk.start()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for i in range(steps):
+        step_fn(i)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clocks = clk.stop()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    return ms / steps, clocks
+
+
+def shard_step_line(steps, warmup, dev, rank, world, stream):
+    """The config-5 step (vocabulary split across the ranks, one NCCL
+    all-gather inside rl_sample_sharded) at this N: returned on rank 0."""
+    import torch
+
+    import rlsampler
+    import sharded
+
+    c = CONFIGS[5]
+    B, V = c["B"], c["V"]
+    pool = make_pool(5, dev, rank, world, count=2)
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+    if world > 1:
+        ss = sharded.ShardedSampler(V, max_batch=B, device=dev, max_history=c["H"])
+        fn = lambda i: ss.sample(pool[i % 2]["logits"], pool[i % 2]["params"], pool[i % 2]["u"], pool[i % 2]["hist"],
+                                 pool[i % 2]["hl"], out_tok=tok, out_prob=prob, row_status=st, stream=stream)
+    else:
+        ss = rlsampler.Sampler(dev.index, max_batch=B, max_vocab=V, max_history=c["H"])
+        fn = lambda i: ss.sample(pool[i % 2]["logits"], pool[i % 2]["params"], pool[i % 2]["u"], pool[i % 2]["hist"],
+                                 pool[i % 2]["hl"], None, tok, prob, st, stream=stream)
+    ms, _ = timed_loop(fn, steps, warmup, stream, world, dev)
+    bad = int((st != 0).sum().item())
+    ss.close()
+    return {"metric": c["metric"], "value": B * steps / (ms * steps / 1e3), "unit": c["unit"], "ms_per_step": ms,
+            "ranks": world, "scaling": "strong", "dtype": "bf16", "rows_not_ok": bad,
+            "exchange": "one ncclAllGather of 1056 B per row and rank inside rl_sample_sharded" if world > 1
+            else "one piece (rl_sample_batch)",
+            "algorithmic_bytes_per_gpu": algorithmic_bytes(5, world)}
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-shards", action="store_true", help="config 2: leave out the config-5 step")
+    ap.add_argument("--ref-seconds", type=float, default=120.0, help="--impl reference: time budget of the loop")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.steps is None:
+        args.steps = {1: 2000, 2: 200, 3: 500, 4: 200, 5: 50}[args.config]
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -208,124 +447,188 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-
-    s = rlsampler.Sampler(local, max_batch=B, max_vocab=V, max_history=H)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = args.config
+    c = CONFIGS[cfg]
+    B, V, H = c["B"], c["V"], c["H"]
     stream = torch.cuda.current_stream(dev)
+    pool = make_pool(cfg, dev, rank, world) if cfg != 5 else None
 
-    # ---- device-resident pool of step inputs (inputs > L2) ----
-    gen = torch.Generator(device=dev)
-    prior = (-1.1 * torch.log(torch.arange(V, device=dev, dtype=torch.float64) + 1.0)).float()
-    pool = []
-    for i in range(POOL):
-        gen.manual_seed(1000 * 2 + i + 7919 * rank)
-        lg = torch.randn((B, V), generator=gen, device=dev, dtype=torch.float32) * 4.0 + prior
-        p, hist, u = make_params(i + 100 * rank)
-        pool.append(dict(logits=lg, params=rlsampler.params_tensor(p, dev),
-                         hist=torch.from_numpy(hist).to(dev), hl=torch.full((B,), H, dtype=torch.int32, device=dev),
-                         u=torch.from_numpy(u).to(dev)))
     out_tok = torch.empty(B, dtype=torch.int32, device=dev)
     out_prob = torch.empty(B, dtype=torch.float32, device=dev)
     row_st = torch.empty(B, dtype=torch.int32, device=dev)
+    kernel_ms = None
+    launches_per_step = 2
+    s = None
+    if cfg in (1, 2, 3):
+        s = rlsampler.Sampler(local, max_batch=B, max_vocab=V, max_history=max(H, 1))
 
-    def step(i):
-        d = pool[i % POOL]
-        s.sample(d["logits"], d["params"], d["u"], d["hist"], d["hl"], None, out_tok, out_prob, row_st,
-                 stream=stream)
+        def step(i):
+            d = pool[i % POOL]
+            s.sample(d["logits"], d["params"], d["u"], d.get("hist"), d.get("hl"), d.get("mask"), out_tok, out_prob,
+                     row_st, stream=stream)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize()
-    bad = int((row_st != 0).sum().item())
+        ms, clocks = timed_loop(step, args.steps, args.warmup, stream, world, dev)
+        # per-kernel device times over a few extra (untimed) steps
+        s.set_debug(rlsampler.RL_DEBUG_TIMING)
+        per = []
+        for i in range(8):
+            step(i)
+            per.append(s.kernel_times())
+        s.set_debug(0)
+        kernel_ms = [float(np.mean([p[k] for p in per])) for k in range(len(per[0]))]
+        units = B
+    elif cfg == 4:
+        s = rlsampler.Sampler(local, max_batch=B, max_vocab=V, max_history=1)
+        launches_per_step = 4  # params fill, streaming, finish, beam combine
 
-    clk = ClockSampler(local)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    clk.start()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    clocks = clk.stop()
-    ms = ev0.elapsed_time(ev1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-        dist.barrier()
-    ms_per_step = ms / args.steps
-    value = world * B * args.steps / (ms / 1e3)
+        def step(i):
+            d = pool[i % POOL]
+            s.beam_step(d["logits"], 16, 8, d["scores"], d["done"], d["lens"], 1.0, 2, 1, 16, stream=stream)
+
+        ms, clocks = timed_loop(step, args.steps, args.warmup, stream, world, dev)
+        units = 128
+        row_st.zero_()
+    else:
+        line5 = shard_step_line(args.steps, args.warmup, dev, rank, world, stream)
+        ms, clocks, units = line5["ms_per_step"], None, B
+        launches_per_step = 3 if world > 1 else 2
+    bad = int((row_st != 0).sum().item()) if cfg != 5 else line5["rows_not_ok"]
+    value_units_per_s = (world if cfg != 5 else 1) * units / (ms / 1e3)
 
     # ---- end to end through the host-buffer entry point (pinned memory) ----
-    hp = pool[0]
-    h_logits = torch.empty((B, V), dtype=torch.float32, pin_memory=True)
-    h_logits.copy_(hp["logits"].cpu())
-    p0, hist0, u0 = make_params(0)
-    h_params = np.ascontiguousarray(p0)
-    h_hist = np.ascontiguousarray(hist0)
-    h_hl = np.full(B, H, np.int32)
-    h_u = np.ascontiguousarray(u0)
-    h_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
-    h_prob = torch.empty(B, dtype=torch.float32, pin_memory=True)
-    import ctypes
+    e2e = None
+    if cfg in (2, 3):
+        d = pool[0]
+        h_logits = torch.empty((B, V), dtype=torch.float32, pin_memory=True)
+        h_logits.copy_(d["logits"].cpu())
+        h_params = d["params"].cpu().numpy().copy()
+        h_u = d["u"].cpu().numpy().copy()
+        h_hist = d["hist"].cpu().numpy().copy() if "hist" in d else None
+        h_hl = d["hl"].cpu().numpy().copy() if "hl" in d else None
+        h_mask = d["mask"].cpu().numpy().copy() if "mask" in d else None
+        h_tok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+        h_prob = torch.empty(B, dtype=torch.float32, pin_memory=True)
+        cp = lambda a: a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+        tp = lambda t: ctypes.c_void_p(t.data_ptr())
 
-    cp = lambda a: a.ctypes.data_as(ctypes.c_void_p)
-    tp = lambda t: ctypes.c_void_p(t.data_ptr())
+        def e2e_step():
+            s.sample_host_ptrs(tp(h_logits), B, V, cp(h_params), cp(h_u), tp(h_tok), tp(h_prob), cp(h_hist),
+                               cp(h_hl), H, cp(h_mask), h_mask.shape[1] if h_mask is not None else 0)
 
-    def e2e_step():
-        s.sample_host_ptrs(tp(h_logits), B, V, cp(h_params), cp(h_u), tp(h_tok), tp(h_prob), cp(h_hist),
-                           cp(h_hl), H, None, 0)
+        for _ in range(3):
+            e2e_step()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e2e_s = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e_s = float(t.item())
+        h2d = B * V * 4 + (B * H * 4 + B * 4 if H else 0) + B * 24 + B * 4 + (h_mask.nbytes if h_mask is not None else 0)
+        copy_ms = (B * V * 4) / 40e9 * 1e3
+        e2e = {"value": world * B * args.e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": B * 8, "ms_per_step": e2e_s / args.e2e_steps * 1e3,
+               "device_ms_per_step": ms,
+               "path": "rl_sample_host (pinned host buffers, H2D + kernels + D2H + sync per step)"}
+    elif cfg == 1:
+        # one host call per token through the host-buffer entry point
+        d = pool[0]
+        h = {k: (d[k].cpu().numpy().copy() if k != "logits" else None) for k in ("params", "u", "hist", "hl")}
+        h_logits = torch.empty((1, V), dtype=torch.float32, pin_memory=True)
+        h_logits.copy_(d["logits"].cpu())
+        h_tok = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        h_prob = torch.empty(1, dtype=torch.float32, pin_memory=True)
+        cp = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+        tp = lambda t: ctypes.c_void_p(t.data_ptr())
+        fn = lambda: s.sample_host_ptrs(tp(h_logits), 1, V, cp(h["params"]), cp(h["u"]), tp(h_tok), tp(h_prob),
+                                        cp(h["hist"]), cp(h["hl"]), H, None, 0)
+        for _ in range(10):
+            fn()
+        t0 = time.perf_counter()
+        n = 500
+        for _ in range(n):
+            fn()
+        e2e_us = (time.perf_counter() - t0) / n * 1e6
+        e2e = {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": V * 4 + H * 4 + 4 + 24 + 4,
+               "d2h_bytes_per_step": 8, "path": "rl_sample_host, one call per token (host logits in, token out)"}
 
-    for _ in range(3):
-        e2e_step()
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
-        e2e_step()
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_val = world * B * args.e2e_steps / e2e_s
-    h2d = B * V * 4 + B * H * 4 + B * 4 + B * 24 + B * 4
-    d2h = B * 4 + B * 4
+    shards = None
+    if cfg == 2 and not args.no_shards:
+        shards = shard_step_line(20, 3, dev, rank, world, stream)
 
     if rank == 0:
         peak, peak_kind = measured_peak()
-        alg = algorithmic_bytes()
-        achieved = alg / (ms_per_step * 1e-3) / 1e9
-        traffic = committed_traffic().get("spec_step_f32_config2")
+        alg = algorithmic_bytes(cfg, world)
+        step_gbs = alg / (ms * 1e-3) / 1e9
+        if kernel_ms:
+            dom_ms = kernel_ms[0]
+            achieved = alg / (dom_ms * 1e-3) / 1e9
+            kern = "spec_pipe_kernel (the streaming kernel: reads every logit once), CUDA events around it"
+        else:
+            dom_ms = ms
+            achieved = step_gbs
+            kern = "the whole step (its kernels timed together)"
+        # config 1 samples one token per step and rank: microseconds per token
+        value = ms * 1e3 if cfg == 1 else value_units_per_s
+        traffic = committed_traffic().get(f"spec_step_f32_config{cfg}") if cfg == 2 else None
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "hetero_batch_b256_v128256_f32", "global_batch": world * B, "per_gpu_batch": B,
-                       "vocab": V, "history": H, "parallelism": f"rows{world}",
-                       "l2": f"inputs larger than L2: {POOL} distinct {B}x{V} f32 step buffers cycled"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "kernel": "one step: spec_pipe_kernel (stream) + spec_finish_kernel, timed together",
-                         "algorithmic_bytes_per_launch": alg, "traffic": traffic},
-            # two of this library's kernels per step: the streaming kernel and the finish kernel
-            "gpu_launches": 2 * args.steps,
+            "metric": c["metric"], "value": value, "unit": c["unit"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": c["higher"],
+            "scaling": "strong" if cfg == 5 else "weak", "vs_baseline": None, "dtype": "bf16" if cfg == 5 else "f32",
+            "data": "synthetic (seeded; the reference publishes no data set)",
+            "config": {"workload": c["workload"], "global_batch": B * (world if cfg != 5 else 1), "per_gpu_batch": B,
+                       "vocab": V, "history": H, "parallelism": (f"vocab{world}" if cfg == 5 else f"rows{world}"),
+                       "l2": ("inputs larger than L2: 8 distinct 256x128256 f32 step buffers cycled" if cfg == 2 else
+                              f"{POOL} distinct step buffers cycled (a step's inputs fit in L2)")},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "kernel": kern, "algorithmic_bytes_per_launch": alg,
+                         "kernel_ms": dom_ms, "step_gbs": step_gbs, "step_frac": step_gbs / peak, "traffic": traffic,
+                         "traffic_source": "profiles/traffic.json (ncu dram__bytes of one launch)" if traffic else None},
+            "kernel_ms": ({"spec_pipe_kernel": kernel_ms[0], "spec_finish_kernel": kernel_ms[1]}
+                          if kernel_ms and len(kernel_ms) > 1 else None),
+            "gpu_launches": launches_per_step * args.steps,
             "rows_not_ok": bad,
-            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "rl_sample_host (pinned host buffers, H2D + kernel + D2H + sync per step)"},
+            "e2e": e2e,
             "clocks": clocks,
         }
-        if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+        if shards:
+            line["vocab_shards"] = shards
+        if not args.no_cpu_baseline and world == 1 and cfg != 5:
+            if cfg == 4:
+                import oracle
+
+                steps_h = [pool[i] for i in range(2)]
+                t0 = time.perf_counter()
+                n = 0
+                while time.perf_counter() - t0 < 5.0:
+                    d = steps_h[n % 2]
+                    lg = d["logits"].cpu().numpy()
+                    oracle.beam_step(lg, 16, 8, d["scores"].cpu().numpy(), d["done"].cpu().numpy(),
+                                     d["lens"].cpu().numpy(), 1.0, 2, 1, 16)
+                    n += 1
+                dt = time.perf_counter() - t0
+                line["cpu_baseline"] = {"value": n * 128 / dt, "unit": c["unit"], "cores": 1, "kind": "port",
+                                        "cpu_model": cpu_model(), "sample": f"{n} beam steps, one thread, {dt:.1f} s"}
+            else:
+                host_steps = [_host_step(pool[i]) for i in range(2)]
+                # the device's tokens for the same two steps
+                gtoks = []
+                for i in range(2):
+                    d = pool[i]
+                    s.sample(d["logits"], d["params"], d["u"], d.get("hist"), d.get("hl"), d.get("mask"), out_tok,
+                             out_prob, row_st, stream=stream)
+                    torch.cuda.synchronize()
+                    gtoks.append(out_tok.cpu().numpy().copy())
+                cb, parity = cpu_baseline(cfg, host_steps, gtoks)
+                line["cpu_baseline"] = cb
+                line["parity_sample"] = parity
         print(json.dumps(line), flush=True)
-    s.close()
+    if s is not None:
+        s.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

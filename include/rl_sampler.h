@@ -86,7 +86,17 @@ const char* rl_version(void);
  * switch off sample normally on the same handle.
  */
 #define RL_DEBUG_EXPIRE_WAIT 1u
+/* RL_DEBUG_TIMING: each spec sampling call (rl_sample_batch and the entries
+ * built on it) records CUDA events around each of its kernels on the call's
+ * stream; rl_sampler_kernel_times returns the last call's per-kernel device
+ * times in launch order (the streaming kernel, then the finish kernel). The
+ * events between the two kernels keep the finish kernel from starting early,
+ * so a timed step can run a little longer than an untimed one. */
+#define RL_DEBUG_TIMING 2u
 rl_status rl_sampler_set_debug(rl_sampler* h, uint32_t flags);
+/* Waits for the last timed call and writes up to cap kernel times (ms) to
+ * ms[]; *n gets their count (0 when no call was timed). */
+rl_status rl_sampler_kernel_times(rl_sampler* h, float* ms, int cap, int* n);
 
 /*
  * Self-check of the fixed-divisor division that the spec sampler uses for

@@ -110,8 +110,25 @@ rl_status rl_sampler_create(rl_sampler** out, int device, int max_batch, int max
 
 rl_status rl_sampler_set_debug(rl_sampler* h, uint32_t flags) {
   if (!h) return fail(RL_ERR_INVALID_ARG, "rl_sampler_set_debug: handle is NULL");
-  if (flags & ~RL_DEBUG_EXPIRE_WAIT) return fail(RL_ERR_INVALID_ARG, "rl_sampler_set_debug: unknown flags 0x%x", flags);
+  if (flags & ~(RL_DEBUG_EXPIRE_WAIT | RL_DEBUG_TIMING))
+    return fail(RL_ERR_INVALID_ARG, "rl_sampler_set_debug: unknown flags 0x%x", flags);
   h->debug = flags;
+  return RL_OK;
+}
+
+rl_status rl_sampler_kernel_times(rl_sampler* h, float* ms, int cap, int* n) {
+  if (!h || !n || (cap > 0 && !ms)) return fail(RL_ERR_INVALID_ARG, "rl_sampler_kernel_times: NULL pointer");
+  *n = 0;
+  if (h->ev_n == 0) return RL_OK;
+  DeviceGuard g(h->device);
+  cudaError_t e = cudaEventSynchronize(h->ev[h->ev_n]);
+  if (e != cudaSuccess) return cuda_fail(e, "rl_sampler_kernel_times");
+  const int k = h->ev_n < cap ? h->ev_n : cap;
+  for (int i = 0; i < k; ++i) {
+    e = cudaEventElapsedTime(&ms[i], h->ev[i], h->ev[i + 1]);
+    if (e != cudaSuccess) return cuda_fail(e, "rl_sampler_kernel_times");
+  }
+  *n = k;
   return RL_OK;
 }
 
@@ -180,7 +197,9 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.part_stats = part_stats;
   a.part_packed = part_packed;
   a.ws = h->ws;
-  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream));
+  const bool timed = (h->debug & RL_DEBUG_TIMING) != 0;
+  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream), timed ? h->ev : nullptr);
+  h->ev_n = timed ? 2 : 0;
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
   return RL_OK;
 }

@@ -15,6 +15,8 @@ struct rl_sampler {
   int num_sms = 0;
   uint32_t flags = 0;
   uint32_t debug = 0;             // rl_sampler_set_debug switches
+  cudaEvent_t ev[3] = {};         // RL_DEBUG_TIMING: around the last call's kernels
+  int ev_n = 0;                   // kernels timed by the last call
   cudaStream_t stream = nullptr;  // used by the host-buffer entry points
   // device staging buffers of rl_sample_host (allocated at create)
   float* stage_logits = nullptr;

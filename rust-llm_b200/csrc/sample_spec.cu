@@ -3290,7 +3290,7 @@ void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas) {
 int spec_max_ws_items(int num_sms, int max_batch) { return max(2 * (2 * num_sms), max_batch); }
 
 template <typename E, bool SPLIT>
-static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t stream) {
+static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t stream, cudaEvent_t* ev = nullptr) {
   // the kernels' shared-memory limit, set once per device (a per-device
   // flag read and written atomically: several host threads may launch)
   static std::atomic<int> configured[64];
@@ -3304,7 +3304,9 @@ static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t strea
     if (e != cudaSuccess) return e;
     if (dev >= 0 && dev < 64) configured[dev].store(1, std::memory_order_release);
   }
+  if (ev) cudaEventRecord(ev[0], stream);
   spec_pipe_kernel<E, SPLIT><<<nctas, kThreads, kSmemBytes, stream>>>(a);
+  if (ev) cudaEventRecord(ev[1], stream);
   if (SPLIT) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -3324,6 +3326,7 @@ static cudaError_t launch_typed(const SpecArgs& a, int nctas, cudaStream_t strea
     cfg.numAttrs = 1;
     e = cudaLaunchKernelEx(&cfg, spec_finish_kernel<E>, a);
     if (e != cudaSuccess) return e;
+    if (ev) cudaEventRecord(ev[2], stream);
   }
   return cudaGetLastError();
 }
@@ -3337,14 +3340,15 @@ cudaError_t spec_configure_single() {
   return e;
 }
 
-cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream) {
+cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream, cudaEvent_t* ev) {
   if (args.B == 0) return cudaSuccess;
   SpecArgs a = args;
   int nctas = 0;
   spec_plan(a.B, a.V, num_sms, &a.nseg, &a.cps, &nctas);
   a.nitems = a.B * a.nseg;
   if (a.nitems > a.ws.max_items) return cudaErrorInvalidValue;
-  return dtype == RL_BF16 ? launch_typed<uint16_t, true>(a, nctas, stream) : launch_typed<float, true>(a, nctas, stream);
+  return dtype == RL_BF16 ? launch_typed<uint16_t, true>(a, nctas, stream, ev)
+                          : launch_typed<float, true>(a, nctas, stream, ev);
 }
 
 cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int max_ctas, cudaStream_t stream) {

@@ -154,7 +154,10 @@ void spec_plan(int B, int V, int num_sms, int* nseg, int* cps, int* nctas);
 int spec_max_ws_items(int num_sms, int max_batch);
 // CTAs of the largest launch (the per-warp overflow areas).
 inline int spec_max_ctas(int num_sms) { return 2 * num_sms; }
-cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream);
+// ev (nullable): three events recorded before the streaming kernel, between
+// it and the finish kernel, and after the finish kernel.
+cudaError_t launch_spec(const SpecArgs& args, int dtype, int num_sms, cudaStream_t stream,
+                        cudaEvent_t* ev = nullptr);
 
 // One segment per row (no per-item workspace: only ws.wovf is used), at most
 // max_ctas CTAs (the persistent CTAs loop over the rows).

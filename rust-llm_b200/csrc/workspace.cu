@@ -37,6 +37,7 @@ rl_status alloc_workspace(rl_sampler* h) {
     ok = ok && dalloc(&h->shard_send, B * kRec) && dalloc(&h->shard_recv, static_cast<size_t>(kMergeMaxShards) * B * kRec);
   ok = ok && dalloc(&h->part_keys, B * kN) && dalloc(&h->part_stats, B) && dalloc(&h->beam_params, B) &&
        dalloc(&h->zero_u, B);
+  for (int i = 0; i < 3 && ok; ++i) ok = cudaEventCreate(&h->ev[i]) == cudaSuccess;
   if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
                cudaMemset(h->zero_u, 0, sizeof(float) * B) == cudaSuccess &&
                cudaDeviceSynchronize() == cudaSuccess;
@@ -80,6 +81,8 @@ void free_workspace(rl_sampler* h) {
   h->part_stats = nullptr;
   h->beam_params = nullptr;
   h->zero_u = nullptr;
+  for (int i = 0; i < 3; ++i)
+    if (h->ev[i]) cudaEventDestroy(h->ev[i]);
   if (h->stream) cudaStreamDestroy(h->stream);
   h->stage_logits = nullptr;
   h->stream = nullptr;

@@ -29,6 +29,7 @@ RL_ERR_NONFINITE = 8
 RL_F32 = 0
 RL_BF16 = 1
 RL_DEBUG_EXPIRE_WAIT = 1
+RL_DEBUG_TIMING = 2
 RL_CREATE_SHARDED = 1
 NCCL_ID_BYTES = 128  # RL_NCCL_ID_BYTES
 
@@ -125,6 +126,8 @@ def lib():
         L.rl_nccl_comm_init.argtypes = [ctypes.POINTER(P), I, P, I]
         L.rl_nccl_comm_destroy.restype = I
         L.rl_nccl_comm_destroy.argtypes = [P]
+        L.rl_sampler_kernel_times.restype = I
+        L.rl_sampler_kernel_times.argtypes = [P, P, I, P]
         L.rl_sampler_set_debug.restype = I
         L.rl_sampler_set_debug.argtypes = [P, ctypes.c_uint32]
         L.rl_selfcheck_div.restype = I
@@ -172,6 +175,13 @@ class Sampler:
     def set_debug(self, flags):
         """rl_sampler_set_debug: RL_DEBUG_* switches (0 = off)."""
         check(lib().rl_sampler_set_debug(self.h, int(flags)), "rl_sampler_set_debug")
+
+    def kernel_times(self):
+        """rl_sampler_kernel_times: the last timed call's kernel times (ms)."""
+        buf = (ctypes.c_float * 4)()
+        n = ctypes.c_int()
+        check(lib().rl_sampler_kernel_times(self.h, buf, 4, ctypes.byref(n)), "rl_sampler_kernel_times")
+        return [buf[i] for i in range(n.value)]
 
     def close(self):
         if self.h:

@@ -101,3 +101,31 @@ def test_debug_flags_rejected_when_unknown():
             s.set_debug(0x80)
     finally:
         s.close()
+
+
+def test_kernel_times_after_a_timed_call():
+    """RL_DEBUG_TIMING: rl_sampler_kernel_times returns the streaming and
+    finish kernels' device times of the last call; off again, it returns none."""
+    import workloads
+
+    b = workloads.config3(0)
+    dev = torch.device("cuda", 0)
+    s = rlsampler.Sampler(0, max_batch=64, max_vocab=32000, max_history=0)
+    try:
+        assert s.kernel_times() == []
+        lg = torch.from_numpy(b.logits).to(dev)
+        mask = torch.from_numpy(b.mask.view(np.int32)).to(dev)
+        prm = rlsampler.params_tensor(b.params, dev)
+        u = torch.from_numpy(b.uniforms).to(dev)
+        s.set_debug(rlsampler.RL_DEBUG_TIMING)
+        tok, _, st = s.sample(lg, prm, u, mask=mask)
+        t = s.kernel_times()
+        assert len(t) == 2 and all(0.0 < x < 1000.0 for x in t)
+        ref, _, _ = oracle.spec_sample_batch(b.logits, None, None, b.mask, b.params, b.uniforms)
+        assert (st.cpu().numpy() == 0).all()
+        assert (tok.cpu().numpy() == ref).mean() > 0.98
+        s.set_debug(0)
+        s.sample(lg, prm, u, mask=mask)
+        assert s.kernel_times() == []
+    finally:
+        s.close()
