@@ -231,6 +231,16 @@ rl_status rl_grammar_greedy(rl_sampler* h, const float* logits, int B, int V, in
                             const uint32_t* mask, int64_t mask_stride, int32_t* out_tok,
                             void* stream);
 
+/* rl_greedy and rl_grammar_greedy on host buffers (synchronous): logits
+ * [B, V] row-major f32 and mask [B, mask_stride] u32 in host memory, out_tok[B]
+ * written in host memory. They back the &[f32] signatures of
+ * Sampler::sample_with_grammar (src/decoder.rs:359-376) and the error
+ * fallback of the infallible (-> Token) wrappers. B <= max_batch and
+ * V <= max_vocab of the handle. */
+rl_status rl_greedy_host(rl_sampler* h, const float* logits, int B, int V, int32_t* out_tok);
+rl_status rl_grammar_greedy_host(rl_sampler* h, const float* logits, int B, int V, const uint32_t* mask,
+                                 int64_t mask_stride, int32_t* out_tok);
+
 /*
  * Vocabulary-sharded sampling (a row's logits split by vocabulary across
  * devices). No single reference function: it splits the spec pipeline above

@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t key_id(uint64_t k) {
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h16) { return __uint_as_float(h16 << 16); }
 
 // ---------------------------------------------------------------------------
-// mbarrier + bulk async copy (TMA, non-tensor form). No multicast anywhere.
+// mbarrier + bulk async copy (TMA, non-tensor form): each copy lands in the issuing CTA only.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -146,4 +146,51 @@ rl_status rl_grammar_greedy(rl_sampler* h, const float* logits, int B, int V, in
   return RL_OK;
 }
 
+// Host-buffer forms (synchronous, on the handle's stream): the rows are
+// copied into the handle's staging buffers (logits at stride max_vocab, mask
+// rows at stride ceil(max_vocab / 32)), reduced, and the tokens copied back.
+static rl_status greedy_host(rl_sampler* h, const float* logits, int B, int V, const uint32_t* mask,
+                             int64_t mask_stride, int lastmax, int32_t* out_tok, const char* who) {
+  rl::clear_error();
+  if (!h) return rl::set_error(RL_ERR_INVALID_ARG, "greedy (host): handle is NULL");
+  if (B < 0 || V <= 0) return rl::set_error(RL_ERR_INVALID_ARG, "greedy (host): bad B or V");
+  if (B == 0) return RL_OK;
+  if (!logits || !out_tok) return rl::set_error(RL_ERR_INVALID_ARG, "greedy (host): logits and out_tok are required");
+  if (B > h->max_batch || V > h->max_vocab) return rl::set_error(RL_ERR_SHAPE, "greedy (host): B or V beyond the handle");
+  const int64_t words = (V + 31) / 32;
+  if (mask && mask_stride < words) return rl::set_error(RL_ERR_INVALID_ARG, "greedy (host): mask_stride < ceil(V/32)");
+  if (!h->stage_logits || (mask && !h->stage_mask))
+    return rl::set_error(RL_ERR_UNSUPPORTED, "greedy (host): no staging buffers");
+  int prev = -1;
+  cudaGetDevice(&prev);
+  if (prev != h->device && cudaSetDevice(h->device) != cudaSuccess)
+    return rl::set_error(RL_ERR_CUDA, "greedy (host): cudaSetDevice failed");
+  cudaStream_t s = h->stream;
+  const int64_t ld = h->max_vocab;
+  cudaError_t e = cudaMemcpy2DAsync(h->stage_logits, sizeof(float) * ld, logits, sizeof(float) * V, sizeof(float) * V,
+                                    B, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess && mask)
+    e = cudaMemcpy2DAsync(h->stage_mask, sizeof(uint32_t) * h->mask_words, mask, sizeof(uint32_t) * mask_stride,
+                          sizeof(uint32_t) * words, B, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) {
+    rl::greedy_kernel<<<B, rl::kGNT, 0, s>>>(h->stage_logits, V, ld, mask ? h->stage_mask : nullptr,
+                                             mask ? h->mask_words : 0, lastmax, h->stage_tok);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpyAsync(out_tok, h->stage_tok, sizeof(int32_t) * B, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (prev >= 0 && prev != h->device) cudaSetDevice(prev);
+  if (e != cudaSuccess) return rl::set_error(RL_ERR_CUDA, who);
+  return RL_OK;
+}
+
+rl_status rl_greedy_host(rl_sampler* h, const float* logits, int B, int V, int32_t* out_tok) {
+  return greedy_host(h, logits, B, V, nullptr, 0, 1, out_tok, "rl_greedy_host: CUDA error");
+}
+
+rl_status rl_grammar_greedy_host(rl_sampler* h, const float* logits, int B, int V, const uint32_t* mask,
+                                 int64_t mask_stride, int32_t* out_tok) {
+  return greedy_host(h, logits, B, V, mask, mask_stride, 0, out_tok, "rl_grammar_greedy_host: CUDA error");
+}
+
 }  // extern "C"

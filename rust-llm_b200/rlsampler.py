@@ -112,6 +112,10 @@ def lib():
         L.rl_greedy.argtypes = [P, P, I, I, I64, P, P]
         L.rl_grammar_greedy.restype = I
         L.rl_grammar_greedy.argtypes = [P, P, I, I, I64, P, I64, P, P]
+        L.rl_greedy_host.restype = I
+        L.rl_greedy_host.argtypes = [P, P, I, I, P]
+        L.rl_grammar_greedy_host.restype = I
+        L.rl_grammar_greedy_host.argtypes = [P, P, I, I, P, I64, P]
         L.rl_beam_step.restype = I
         L.rl_beam_step.argtypes = [P, P, I, I, I, I64, P, P, P, F, I, I, I, P, P, P, P, P]
         L.rl_sample_partial.restype = I
@@ -340,6 +344,44 @@ class Sampler:
                                    _ptr(out_tok), _ptr(out_prob)),
               "rl_sample_host")
         return out_tok, out_prob
+
+    def decoder_sample_host(self, logits, temperature, top_p, uniforms):
+        """rl_decoder_sample_host: Decoder::sample_with_params semantics on host
+        rows [B, V] f32 with per-row temperature / top_p / uniform; returns
+        (tokens, probs) as numpy arrays."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        if lg.ndim == 1:
+            lg = lg[None, :]
+        B, V = lg.shape
+        t = np.ascontiguousarray(np.broadcast_to(np.asarray(temperature, np.float32), (B,)))
+        p = np.ascontiguousarray(np.broadcast_to(np.asarray(top_p, np.float32), (B,)))
+        u = np.ascontiguousarray(np.broadcast_to(np.asarray(uniforms, np.float32), (B,)))
+        tok = np.empty(B, np.int32)
+        prob = np.empty(B, np.float32)
+        check(lib().rl_decoder_sample_host(self.h, _ptr(lg), B, V, _ptr(t), _ptr(p), _ptr(u), _ptr(tok), _ptr(prob)),
+              "rl_decoder_sample_host")
+        return tok, prob
+
+    def greedy_host(self, logits):
+        """rl_greedy_host: argmax (last maximum on ties) of host rows."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        if lg.ndim == 1:
+            lg = lg[None, :]
+        tok = np.empty(lg.shape[0], np.int32)
+        check(lib().rl_greedy_host(self.h, _ptr(lg), lg.shape[0], lg.shape[1], _ptr(tok)), "rl_greedy_host")
+        return tok
+
+    def grammar_greedy_host(self, logits, mask):
+        """rl_grammar_greedy_host: argmax over the allowed ids of the bit-packed
+        mask rows (lowest id on ties; an all-zero row allows every id)."""
+        lg = np.ascontiguousarray(logits, np.float32)
+        m = np.ascontiguousarray(mask, np.uint32)
+        if lg.ndim == 1:
+            lg, m = lg[None, :], m[None, :]
+        tok = np.empty(lg.shape[0], np.int32)
+        check(lib().rl_grammar_greedy_host(self.h, _ptr(lg), lg.shape[0], lg.shape[1], _ptr(m), m.shape[1], _ptr(tok)),
+              "rl_grammar_greedy_host")
+        return tok
 
     def sample_host_ptrs(self, logits_p, B, V, params_p, u_p, tok_p, prob_p, hist_p=None, hist_len_p=None,
                          hist_stride=0, mask_p=None, mask_stride=0):
