@@ -242,6 +242,41 @@ rl_status rl_grammar_greedy_host(rl_sampler* h, const float* logits, int B, int 
                                  int64_t mask_stride, int32_t* out_tok);
 
 /*
+ * Speculative decoding (SpeculativeDecoder, src/inference.rs:238-438): its
+ * sampling arithmetic on device buffers, bit-exact with the reference for the
+ * same uniforms (the reference draws them with rand_simple(), :432-438). One
+ * CTA per row; logits [B, V] f32 at row stride ld.
+ *
+ * rl_specdec_sample -- SpeculativeDecoder::sample (:376-414) per row:
+ * temperature[b] <= 0 takes the argmax of the ids >= offset[b] (the LAST
+ * maximum; 0 when offset >= V); otherwise v / T, max from f32::MIN,
+ * exp(v - max), a left-to-right f32 sum divided out when > 0, and the id-order
+ * draw with uniforms[b] (first id with r <= cumsum, else V - 1). Token ids
+ * include the offset. The draft model's draws are (T 0.8, offset 1), the
+ * target's (T 1.0, offset = the number of drafts).
+ *
+ * rl_specdec_verify -- SpeculativeDecoder::verify_and_accept (:335-374) per
+ * request b: drafts[b, 0 .. n_draft[b]) (row stride draft_stride, 1 <=
+ * n_draft[b] <= draft_stride) against the target row. out_accepted[b] = the
+ * number of leading drafts whose softmax_at probability (:416-429) p > 0 has
+ * accept_u[b, i] < min(p / p, 1) (accept_u at row stride draft_stride). Then
+ * one draw of sample(target, 1.0, n_draft) with draw_u[b]: when every draft
+ * was accepted and room[b] > 0 (generated.len() < max_tokens) it is the bonus
+ * token, kept when > 0 and not the last draft; when none was accepted it is
+ * generate's fallback token (:293-300), kept when > 0. out_tok[b] = the kept
+ * token, else -1.
+ *
+ * Deviation: a row holding NaN or +inf gives out_tok -1 (and out_accepted -1);
+ * the reference panics or walks NaN sums there. n_draft outside [1,
+ * draft_stride] gives -1 / -1 (the reference never verifies an empty draft).
+ */
+rl_status rl_specdec_sample(rl_sampler* h, const float* logits, int B, int V, int64_t ld, const float* temperature,
+                            const int32_t* offset, const float* uniforms, int32_t* out_tok, void* stream);
+rl_status rl_specdec_verify(rl_sampler* h, const float* logits, int B, int V, int64_t ld, const int32_t* drafts,
+                            int draft_stride, const int32_t* n_draft, const float* accept_u, const int32_t* room,
+                            const float* draw_u, int32_t* out_accepted, int32_t* out_tok, void* stream);
+
+/*
  * Vocabulary-sharded sampling (a row's logits split by vocabulary across
  * devices). No single reference function: it splits the spec pipeline above
  * so that each device streams only its columns and the devices exchange 4 KB

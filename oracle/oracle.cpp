@@ -18,6 +18,8 @@
 //     Decoder::greedy_sample        src/decoder.rs:160-167  (orc_greedy)
 //     Sampler::sample_with_grammar  src/decoder.rs:359-376  (orc_grammar_greedy)
 //     BeamSearch::search, one step  src/decoder.rs:217-276  (orc_beam_step, raw logits)
+//     SpeculativeDecoder::sample, softmax_at, verify_and_accept
+//                                   src/inference.rs:335-429 (orc_specdec_*)
 //     with rand_secure() (src/decoder.rs:170-188) replaced by an injected
 //     uniform. All arithmetic is f32, sums are sequential left-to-right,
 //     exp is the platform libm expf (what Rust's f32::exp lowers to on Linux),
@@ -531,6 +533,84 @@ void orc_beam_step(const float* logits, int items, int beams, int V, int64_t ld,
       }
     }
   }
+}
+
+// ---------------------------------------------------------------------------
+// SpeculativeDecoder (src/inference.rs:238-438), with rand_simple()
+// (src/inference.rs:432-438) replaced by injected uniforms.
+// ---------------------------------------------------------------------------
+
+// SpeculativeDecoder::sample (src/inference.rs:376-414): ids below `offset`
+// are skipped (.skip(offset)); the token id includes the offset.
+int32_t orc_specdec_sample(const float* logits, int V, float temperature, int offset, float r) {
+  if (offset < 0) return -1;  // a usize in the reference
+  if (temperature <= 0.0f) {  // :379-387 argmax, max_by: the LAST maximum
+    int best = -1;
+    float bv = 0.0f;
+    for (int i = offset; i < V; ++i) {
+      if (logits[i] != logits[i]) return -1;  // partial_cmp(..).unwrap() panics on NaN
+      if (best < 0 || !(logits[i] < bv)) {
+        best = i;
+        bv = logits[i];
+      }
+    }
+    return best < 0 ? 0 : best;  // unwrap_or(0)
+  }
+  std::vector<float> adjusted;  // :389-395 v / temperature
+  for (int i = offset; i < V; ++i) adjusted.push_back(logits[i] / temperature);
+  float max_val = -FLT_MAX;  // :397 fold(f32::MIN, max)
+  for (float v : adjusted) max_val = rust_max(max_val, v);
+  for (float& v : adjusted) v = std::exp(v - max_val);  // :398
+  float sum = 0.0f;  // :400 sequential f32 sum
+  for (float v : adjusted) sum += v;
+  if (sum > 0.0f)
+    for (float& v : adjusted) v /= sum;
+  float cumsum = 0.0f;  // :405-411 id-order draw, r <= cumsum
+  for (size_t i = 0; i < adjusted.size(); ++i) {
+    cumsum += adjusted[i];
+    if (r <= cumsum) return static_cast<int32_t>(i) + offset;
+  }
+  return V - 1;  // :413
+}
+
+// SpeculativeDecoder::softmax_at (src/inference.rs:416-429).
+float orc_specdec_softmax_at(const float* logits, int V, int64_t idx) {
+  if (idx < 0 || idx >= V) return 0.0f;  // a negative Token cast to usize is out of range
+  float max_logit = -FLT_MAX;
+  for (int i = 0; i < V; ++i) max_logit = rust_max(max_logit, logits[i]);
+  float exp_sum = 0.0f;
+  for (int i = 0; i < V; ++i) exp_sum += std::exp(logits[i] - max_logit);
+  return exp_sum > 0.0f ? std::exp(logits[idx] - max_logit) / exp_sum : 0.0f;
+}
+
+// SpeculativeDecoder::verify_and_accept (src/inference.rs:335-374) for one
+// request: returns the accepted count; *out_token is the token the caller
+// appends after the accepted drafts (the bonus token when every draft is
+// accepted and room > 0, the fallback sample of generate (:293-300) when
+// none is), or -1. draw_u is the uniform of that one draw.
+int32_t orc_specdec_verify(const float* logits, int V, const int32_t* drafts, int D, const float* accept_u,
+                           int room, float draw_u, int32_t* out_token) {
+  int accepted = 0;
+  for (int i = 0; i < D; ++i) {
+    const float draft_prob = orc_specdec_softmax_at(logits, V, drafts[i]);
+    const float target_prob = orc_specdec_softmax_at(logits, V, drafts[i]);
+    const float acceptance = draft_prob > 0.0f ? std::fmin(target_prob / draft_prob, 1.0f) : 0.0f;
+    if (accept_u[i] < acceptance) {
+      accepted = i + 1;
+    } else {
+      break;
+    }
+  }
+  int32_t tok = -1;
+  if (accepted == D && room > 0) {  // :363-369 the bonus token
+    const int32_t bonus = orc_specdec_sample(logits, V, 1.0f, D, draw_u);
+    if (bonus > 0 && bonus != (D > 0 ? drafts[D - 1] : 0)) tok = bonus;
+  } else if (accepted == 0) {  // generate :293-300 the fallback token
+    const int32_t t = orc_specdec_sample(logits, V, 1.0f, D, draw_u);
+    if (t > 0) tok = t;
+  }
+  *out_token = tok;
+  return accepted;
 }
 
 }  // extern "C"

@@ -90,6 +90,12 @@ def lib():
         L.orc_beam_step.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int64,
                                     P, P, P, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                     ctypes.c_int, P, P, P, P]
+        L.orc_specdec_sample.restype = ctypes.c_int32
+        L.orc_specdec_sample.argtypes = [P, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_float]
+        L.orc_specdec_softmax_at.restype = ctypes.c_float
+        L.orc_specdec_softmax_at.argtypes = [P, ctypes.c_int, ctypes.c_int64]
+        L.orc_specdec_verify.restype = ctypes.c_int32
+        L.orc_specdec_verify.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, P]
         _lib = L
     return _lib
 
@@ -195,3 +201,26 @@ def beam_step(logits, items, beams, scores, done, lens, alpha, eos, log_softmax,
     lib().orc_beam_step(_p(lg), items, beams, V, V, _p(sc), _p(dn), _p(ln), float(alpha),
                         int(eos), int(log_softmax), n_out, _p(ob), _p(ot), _p(os_), _p(od))
     return ob, ot, os_, od
+
+
+def specdec_sample(logits, temperature, offset, r):
+    """SpeculativeDecoder::sample (src/inference.rs:376-414) on one f32 row."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().orc_specdec_sample(_p(x), x.size, float(temperature), int(offset), float(r)))
+
+
+def specdec_softmax_at(logits, idx):
+    """SpeculativeDecoder::softmax_at (src/inference.rs:416-429)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    return float(lib().orc_specdec_softmax_at(_p(x), x.size, int(idx)))
+
+
+def specdec_verify(logits, drafts, accept_u, room, draw_u):
+    """SpeculativeDecoder::verify_and_accept (src/inference.rs:335-374) for one
+    request -> (accepted count, appended token or -1)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    d = np.ascontiguousarray(drafts, dtype=np.int32)
+    a = np.ascontiguousarray(accept_u, dtype=np.float32)
+    tok = np.zeros(1, np.int32)
+    acc = lib().orc_specdec_verify(_p(x), x.size, _p(d), d.size, _p(a), int(room), float(draw_u), _p(tok))
+    return int(acc), int(tok[0])

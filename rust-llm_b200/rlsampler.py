@@ -112,6 +112,10 @@ def lib():
         L.rl_greedy.argtypes = [P, P, I, I, I64, P, P]
         L.rl_grammar_greedy.restype = I
         L.rl_grammar_greedy.argtypes = [P, P, I, I, I64, P, I64, P, P]
+        L.rl_specdec_sample.restype = I
+        L.rl_specdec_sample.argtypes = [P, P, I, I, I64, P, P, P, P, P]
+        L.rl_specdec_verify.restype = I
+        L.rl_specdec_verify.argtypes = [P, P, I, I, I64, P, I, P, P, P, P, P, P, P]
         L.rl_greedy_host.restype = I
         L.rl_greedy_host.argtypes = [P, P, I, I, P]
         L.rl_grammar_greedy_host.restype = I
@@ -382,6 +386,37 @@ class Sampler:
         check(lib().rl_grammar_greedy_host(self.h, _ptr(lg), lg.shape[0], lg.shape[1], _ptr(m), m.shape[1], _ptr(tok)),
               "rl_grammar_greedy_host")
         return tok
+
+    # -- speculative decoding ---------------------------------------------------
+    def specdec_sample(self, logits, temperature, offset, uniforms, stream=None):
+        """rl_specdec_sample: SpeculativeDecoder::sample per row of device
+        logits [B, V] f32; temperature / offset / uniforms are [B] device tensors."""
+        import torch
+
+        B, V = logits.shape
+        out = torch.empty(B, dtype=torch.int32, device=logits.device)
+        check(lib().rl_specdec_sample(self.h, _ptr(logits), B, V, logits.stride(0), _ptr(temperature), _ptr(offset),
+                                      _ptr(uniforms), _ptr(out), _stream(stream)),
+              "rl_specdec_sample")
+        return out
+
+    def specdec_verify(self, logits, drafts, n_draft, accept_u, room, draw_u, stream=None):
+        """rl_specdec_verify: SpeculativeDecoder::verify_and_accept per request;
+        drafts / accept_u [B, Dmax] (same row stride), n_draft / room / draw_u
+        [B] (device). Returns (accepted [B], token [B]) device tensors."""
+        import torch
+
+        B, V = logits.shape
+        if accept_u.stride(0) != drafts.stride(0):
+            raise ValueError("specdec_verify: drafts and accept_u need the same row stride")
+        dev = logits.device
+        acc = torch.empty(B, dtype=torch.int32, device=dev)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        check(lib().rl_specdec_verify(self.h, _ptr(logits), B, V, logits.stride(0), _ptr(drafts), drafts.stride(0),
+                                      _ptr(n_draft), _ptr(accept_u), _ptr(room), _ptr(draw_u), _ptr(acc), _ptr(tok),
+                                      _stream(stream)),
+              "rl_specdec_verify")
+        return acc, tok
 
     def sample_host_ptrs(self, logits_p, B, V, params_p, u_p, tok_p, prob_p, hist_p=None, hist_len_p=None,
                          hist_stride=0, mask_p=None, mask_stride=0):
