@@ -774,7 +774,11 @@ __device__ __forceinline__ void warp_sort_desc(uint64_t* buf, int n) {
 // The need-th largest value among the kCE f32 logits of a stage (NaN and
 // -inf ignored; -inf when fewer than need remain), by the consumer threads:
 // a radix select on the ordered bits; bins: 256 u32.
-__device__ __noinline__ float block_kth_stage(const float* stg, int need, uint32_t* bins, Red* rs, Ctl* ctl) {
+// E: f32 or bf16 stage; excl (nullable): kCE bits, set for the positions to
+// leave out (a bf16 stage holds raw values, so its history ids are skipped).
+template <typename E>
+__device__ __noinline__ float block_kth_stage(const E* stg, int need, uint32_t* bins, Red* rs, Ctl* ctl,
+                                              const uint32_t* excl) {
   const int tid = threadIdx.x;
   constexpr int R = kCE / kConsumers;
   uint32_t u[R];
@@ -782,8 +786,9 @@ __device__ __noinline__ float block_kth_stage(const float* stg, int need, uint32
   uint32_t kmin = 0xffffffffu, kmax = 0u;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const float x = stg[r * kConsumers + tid];
-    const bool ok = x > RL_NEG_INF;  // false for NaN
+    const int e = r * kConsumers + tid;
+    const float x = to_f32<E>(stg[e]);
+    const bool ok = x > RL_NEG_INF && !(excl && ((excl[e >> 5] >> (e & 31)) & 1u));  // false for NaN
     u[r] = ok ? ord_key(x) : 0u;
     if (ok) {
       ++cnt;
@@ -2829,12 +2834,47 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       }
       __syncwarp();
       cbar();  // every warp's penalties are in the stage
-      const float t0 = block_kth_stage(f, nkeep, sm.radix, sm.red, sm.ctl);
+      const float t0 = block_kth_stage<float>(f, nkeep, sm.radix, sm.red, sm.ctl, nullptr);
       if (t0 > tau_v) {
         tau_v = t0;
         // every logit equal to t0 is kept (the key of +0.0 for a zero bound)
         tau = static_cast<uint64_t>(ord_key(__fadd_rn(t0, 0.0f))) << 32;
         if (tid == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
+      }
+    }
+  }
+  if constexpr (MODE != 0 && es == 2) {
+    // the same bound for a bf16 item: the stage holds raw values (penalties
+    // are applied in registers), so the chunk's history ids are left out --
+    // the nkeep-th largest of the other logits, whose values are final, is
+    // still a lower bound on the row's nkeep-th largest penalised value
+    const int start = mt.c0 * kCE;
+    const int len = min(kCE, V - start);
+    const int nfast = row_al ? ((len * es) & ~15) / es : 0;
+    if (!mask_on && nfast == kCE) {
+      const int s = cseq % kNS;
+      uint32_t* excl = sm.radix + 256;  // kCE bits, past the 256 select bins
+      for (int i = tid; i < kCE / 32; i += kConsumers) excl[i] = 0u;
+      cbar();
+      if (ntab > 0) {
+        const int j0 = tab_lower_bound(tab, ntab, start);
+        for (int j = j0 + tid; j < ntab; j += kConsumers) {
+          const int id = static_cast<int>(tab[j] >> 11);
+          if (id >= start + kCE) break;  // the table is sorted by id
+          atomicOr(&excl[(id - start) >> 5], 1u << ((id - start) & 31));
+        }
+      }
+      cbar();
+      if (mbar_wait(SPLIT ? &sm.ready[s] : &sm.full[s], static_cast<uint32_t>((cseq / kNS) & 1), kWaitBudget)) {
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(sm.stage + s * kStageBytes);
+        const float t0 = block_kth_stage<uint16_t>(h, nkeep, sm.radix, sm.red, sm.ctl, excl);
+        if (t0 > tau_v) {
+          tau_v = t0;
+          tau = static_cast<uint64_t>(ord_key(__fadd_rn(t0, 0.0f))) << 32;
+          if (tid == 0) atomicMax(&sm.ctl->tau_shared, static_cast<unsigned long long>(tau));
+        }
+      } else {
+        tmo = 1;
       }
     }
   }
