@@ -477,6 +477,7 @@ def main():
             per.append(s.kernel_times())
         s.set_debug(0)
         kernel_ms = [float(np.mean([p[k] for p in per])) for k in range(len(per[0]))]
+        launches_per_step = len(kernel_ms)  # short rows: one kernel; long rows: streaming + finish
         units = B
     elif cfg == 4:
         s = rlsampler.Sampler(local, max_batch=B, max_vocab=V, max_history=1)
@@ -567,7 +568,9 @@ def main():
         if kernel_ms:
             dom_ms = kernel_ms[0]
             achieved = alg / (dom_ms * 1e-3) / 1e9
-            kern = "spec_pipe_kernel (the streaming kernel: reads every logit once), CUDA events around it"
+            kern = ("spec_pipe_kernel (the streaming kernel: reads every logit once), CUDA events around it"
+                    if len(kernel_ms) > 1 else
+                    "small_rows_kernel (one CTA per row, the row in shared memory), CUDA events around it")
         else:
             dom_ms = ms
             achieved = step_gbs
@@ -588,8 +591,8 @@ def main():
                          "peak_kind": peak_kind, "kernel": kern, "algorithmic_bytes_per_launch": alg,
                          "kernel_ms": dom_ms, "step_gbs": step_gbs, "step_frac": step_gbs / peak, "traffic": traffic,
                          "traffic_source": "profiles/traffic.json (ncu dram__bytes of one launch)" if traffic else None},
-            "kernel_ms": ({"spec_pipe_kernel": kernel_ms[0], "spec_finish_kernel": kernel_ms[1]}
-                          if kernel_ms and len(kernel_ms) > 1 else None),
+            "kernel_ms": (({"spec_pipe_kernel": kernel_ms[0], "spec_finish_kernel": kernel_ms[1]}
+                           if len(kernel_ms) > 1 else {"small_rows_kernel": kernel_ms[0]}) if kernel_ms else None),
             "gpu_launches": launches_per_step * args.steps,
             "rows_not_ok": bad,
             "e2e": e2e,

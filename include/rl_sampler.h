@@ -89,9 +89,11 @@ const char* rl_version(void);
 /* RL_DEBUG_TIMING: each spec sampling call (rl_sample_batch and the entries
  * built on it) records CUDA events around each of its kernels on the call's
  * stream; rl_sampler_kernel_times returns the last call's per-kernel device
- * times in launch order (the streaming kernel, then the finish kernel). The
- * events between the two kernels keep the finish kernel from starting early,
- * so a timed step can run a little longer than an untimed one. */
+ * times in launch order: for rows of more than 45056 logits the streaming
+ * kernel, then the finish kernel; for shorter rows without a mask the one
+ * short-row kernel.
+ * The events between the two kernels keep the finish kernel from starting
+ * early, so a timed step can run a little longer than an untimed one. */
 #define RL_DEBUG_TIMING 2u
 rl_status rl_sampler_set_debug(rl_sampler* h, uint32_t flags);
 /* Waits for the last timed call and writes up to cap kernel times (ms) to

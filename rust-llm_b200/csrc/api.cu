@@ -198,8 +198,22 @@ static rl_status sample_common(rl_sampler* h, const void* logits, rl_dtype dtype
   a.part_packed = part_packed;
   a.ws = h->ws;
   const bool timed = (h->debug & RL_DEBUG_TIMING) != 0;
-  cudaError_t e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream), timed ? h->ev : nullptr);
-  h->ev_n = timed ? 2 : 0;
+  cudaError_t e;
+  // short unmasked rows without inspection outputs: the one-kernel short-row
+  // sampler (measured faster there; masked rows stay on the streaming
+  // kernels, where a sparse allowed set makes the short-row threshold search
+  // slower than the two-kernel path)
+  const bool small = rl::small_rows_ok(V) && !mask && !list_len && !list_cut && !part_keys && vocab_offset == 0 &&
+                     (h->debug & RL_DEBUG_EXPIRE_WAIT) == 0;
+  if (small) {
+    if (timed) cudaEventRecord(h->ev[0], static_cast<cudaStream_t>(stream));
+    e = rl::launch_small_rows(a, dtype, static_cast<cudaStream_t>(stream));
+    if (timed) cudaEventRecord(h->ev[1], static_cast<cudaStream_t>(stream));
+    h->ev_n = timed ? 1 : 0;
+  } else {
+    e = rl::launch_spec(a, dtype, h->num_sms, static_cast<cudaStream_t>(stream), timed ? h->ev : nullptr);
+    h->ev_n = timed ? 2 : 0;
+  }
   if (e != cudaSuccess) return cuda_fail(e, "rl_sample_batch launch");
   return RL_OK;
 }

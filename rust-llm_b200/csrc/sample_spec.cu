@@ -37,39 +37,10 @@
 
 #include "common.cuh"
 #include "spec_kernel.cuh"
+#include "spec_row.cuh"
 
 namespace rl {
 
-constexpr double kLog2e = 1.4426950408889634074;
-
-// ---------------------------------------------------------------------------
-// Row arithmetic
-// ---------------------------------------------------------------------------
-struct RowT {
-  float T, rT;         // temperature, RN(1/T)
-  int fast_div;        // Markstein division valid for T
-  float c;             // log2(e)/T (bulk sums)
-  float cb_hi, cb_lo;  // kRbin / T split in two floats
-  float dlt;           // log2(e) / kRbin
-};
-
-__device__ __forceinline__ RowT make_rowt(float T) {
-  RowT r;
-  r.T = T;
-  r.rT = __frcp_rn(T);
-  r.fast_div = fixed_div_ok(T);
-  r.c = static_cast<float>(kLog2e / static_cast<double>(T));
-  const double cb = static_cast<double>(kRbin) / static_cast<double>(T);
-  r.cb_hi = static_cast<float>(cb);
-  r.cb_lo = static_cast<float>(cb - static_cast<double>(r.cb_hi));
-  r.dlt = static_cast<float>(kLog2e / static_cast<double>(kRbin));
-  return r;
-}
-// l = (x - m) / T with IEEE rounding, as the CPU restatement computes it.
-__device__ __forceinline__ float exact_l(float x, float m, const RowT& r) {
-  return div_by(sub_rn(x, m), r.T, r.rT, r.fast_div != 0);
-}
-__device__ __forceinline__ float exact_e(float x, float m, const RowT& r) { return expf(exact_l(x, m, r)); }
 __device__ __forceinline__ float ex2_approx(float t) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(t));
@@ -165,7 +136,8 @@ static_assert(kCW * kN <= 4 * kConsumers && kCW * kN * 8 <= kCW * 256 * 4, "item
 static_assert(sizeof(ItemMeta) <= 128 && sizeof(Ctl) <= 128 && sizeof(Red) <= 256, "smem header");
 static_assert(3 * kNS + 5 <= 16, "mbarriers");
 static_assert(kOffMeta + 2 * 128 <= kOffTopE, "meta");
-static_assert(kOffWcnt + 32 + kCW * 8 <= kOffMeta && (kOffWcnt + 32) % 8 == 0, "per-warp counts and histogram totals");
+static_assert(kOffWcnt + 32 + kCW * 8 + kCW * 4 <= kOffMeta && (kOffWcnt + 32) % 8 == 0,
+              "per-warp counts, histogram totals and published bounds");
 static_assert(kOffStage % 128 == 0 && kOffMask % 16 == 0 && kOffSumS % 8 == 0 && kOffHist % 16 == 0, "alignment");
 static_assert(kSmemBytes <= 113 * 1024, "two CTAs per SM");
 
@@ -196,6 +168,8 @@ struct Smem {
   unsigned char* stage;
 };
 extern __shared__ __align__(128) unsigned char g_smem[];
+struct Smem;
+__device__ __forceinline__ uint32_t* wk_of(const Smem& sm);
 __device__ __forceinline__ Smem smem_map() {
   unsigned char* s = g_smem;
   Smem m;
@@ -223,6 +197,9 @@ __device__ __forceinline__ Smem smem_map() {
   m.stage = s + kOffStage;
   return m;
 }
+// Per-warp published bounds of compact_warp_buf (kCW u32), after the
+// per-warp counts (kCW ints) and histogram totals (kCW u64).
+__device__ __forceinline__ uint32_t* wk_of(const Smem& sm) { return reinterpret_cast<uint32_t*>(sm.wcnt + kCW + 2 * kCW); }
 
 // ---------------------------------------------------------------------------
 // Small helpers
@@ -472,7 +449,7 @@ __device__ __forceinline__ void csort_kpt(uint64_t* a, int n, int P, uint64_t* x
 
 // Sorts a[0, n) descending (keys are > 0); positions [n, P) get 0. P is a
 // power of two <= kCollect. Consumer threads only.
-__device__ void csort_desc(uint64_t* a, int n, int P) {
+__device__ __noinline__ void csort_desc(uint64_t* a, int n, int P) {
   if (P <= 32) {
     // one warp, one key per lane
     if (threadIdx.x < 32) {
@@ -2726,9 +2703,18 @@ __device__ __noinline__ void item_end(const SpecArgs& a, int item, int slot, Ite
 // the top 16 value bits (two radix passes) keeps nkeep keys and the rest of
 // their bucket; exact only when that is too many. Returns the new bound,
 // shared through tau_shared.
+//
+// The warp also publishes a lower bound wk[warp] on the value key of its
+// kw-th largest key (kw = ceil(nkeep / kCW)); the warps' elements are
+// disjoint, so the union of every warp's top kw holds at least nkeep keys,
+// all at or above min over the warps of wk: a bound on the item's nkeep-th
+// largest key much closer to it than any one warp's nkeep-th (the warps see
+// an eighth of the item each). wk only grows; a warp that has not published
+// yet holds 0, which leaves the bound alone.
 __device__ __noinline__ uint64_t compact_warp_buf(uint64_t* wbuf, const uint64_t* gov, int* wcnt, int nkeep,
-                                                  uint32_t* bins_w, int* wc, unsigned long long* tau_shared) {
-  const int lane = threadIdx.x & 31;
+                                                  uint32_t* bins_w, int* wc, unsigned long long* tau_shared,
+                                                  uint32_t* wk) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int n = *wcnt;
   uint64_t tau = warp_select(wbuf, gov, n, nkeep, bins_w, 48);
   int kept = warp_count_ge(wbuf, gov, n, tau);
@@ -2738,9 +2724,19 @@ __device__ __noinline__ uint64_t compact_warp_buf(uint64_t* wbuf, const uint64_t
   }
   warp_keep_ge(wbuf, gov, n, tau);
   *wcnt = kept;
+  const int kw = (nkeep + kCW - 1) / kCW;
+  uint64_t bw = 0ull;
+  if (kept >= kw) bw = warp_select(wbuf, gov, kept, kw, bins_w, 48);  // <= the kw-th largest kept key
   if (lane == 0) {
     *wc = kept;
     atomicMax(tau_shared, static_cast<unsigned long long>(tau));
+    volatile uint32_t* w = wk;
+    const uint32_t v = static_cast<uint32_t>(bw >> 32);
+    if (v > w[warp]) w[warp] = v;
+    uint32_t u = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < kCW; ++i) u = min(u, w[i]);
+    if (u != 0u) atomicMax(tau_shared, static_cast<unsigned long long>(u) << 32);
   }
   __syncwarp();
   return tau;
@@ -2793,6 +2789,7 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   const uint32_t wb_u = static_cast<uint32_t>(mt.wbins);
   const int c0 = mt.c0, c1 = mt.c1;
   bool hist_on = MODE == 2;
+  const int wtrig = min(kWcompact, max(2 * nkeep + 32, 128));
   int hp = ntab > 0 ? tab_lower_bound(tab, ntab, mt.c0 * kCE) : 0;
   if (mode == 2)
     for (int i = tid; i < kNB; i += kConsumers) {
@@ -2800,7 +2797,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
       sm.hcnt[i] = 0u;
     }
   if (tid == 0) sm.ctl->tau_shared = 0ull;
-  if (lane == 0) sm.wcnt[warp] = 0;
+  if (lane == 0) {
+    sm.wcnt[warp] = 0;
+    wk_of(sm)[warp] = 0u;
+  }
   cbar();
   // RL_DEBUG_EXPIRE_WAIT: a bounded wait on a barrier that nothing
   // completes runs out, and the item reports a timeout like any wait would
@@ -2880,9 +2880,10 @@ __device__ __noinline__ ItemAcc run_item(const SpecArgs& a, int slot, int cseq) 
   }
 
   for (int c = c0; c < c1; ++c, ++cseq) {
-    if (MODE != 0 && wcnt > kWcompact) {
-      // room for a whole slice of appends (no logits are live here)
-      tau = compact_warp_buf(wbuf, gov, &wcnt, nkeep, bins_w, sm.wcnt + warp, &sm.ctl->tau_shared);
+    if (MODE != 0 && wcnt > wtrig) {
+      // room for a whole slice of appends (no logits are live here); small
+      // lists compact early, so that the union bound rises early
+      tau = compact_warp_buf(wbuf, gov, &wcnt, nkeep, bins_w, sm.wcnt + warp, &sm.ctl->tau_shared, wk_of(sm));
       tau_v = key_val(tau);
     }
     const int s = cseq % kNS;

@@ -166,4 +166,10 @@ cudaError_t launch_spec_single(const SpecArgs& args, int dtype, int num_sms, int
 // current device (what its first launch per dtype would do otherwise).
 cudaError_t spec_configure_single();
 
+// The short-row kernel (sample_small.cu): one CTA per row with the row in
+// shared memory, for rows of at most 45056 logits; plain unmasked
+// sampling calls only (no list, cutoff, partial or debug outputs).
+bool small_rows_ok(int V);
+cudaError_t launch_small_rows(const SpecArgs& args, int dtype, cudaStream_t stream);
+
 }  // namespace rl

@@ -271,3 +271,88 @@ def test_full_size_config2_properties(sampler):
         k = batch.params[b]["top_k"]
         if k > 0 and g[5][b] >= 0:
             assert g[0][b] in set(g[3][b, : g[5][b]].tolist())
+
+
+def run_plain(s, batch, bf16=False):
+    """rl_sample_batch itself (no inspection outputs): for rows of at most
+    45056 logits without a mask this is the short-row kernel."""
+    dev = "cuda:0"
+    if bf16:
+        lg = torch.from_numpy(batch.bf16_bits.view(np.int16)).to(dev).view(torch.bfloat16)
+    else:
+        lg = torch.from_numpy(batch.logits).to(dev)
+    p = rlsampler.params_tensor(batch.params, dev)
+    u = torch.from_numpy(batch.uniforms).to(dev)
+    hist = torch.from_numpy(batch.hist).to(dev) if batch.hist is not None else None
+    hl = torch.from_numpy(batch.hist_len).to(dev) if batch.hist_len is not None else None
+    mask = torch.from_numpy(batch.mask.view(np.int32)).to(dev) if batch.mask is not None else None
+    tok, prob, st = s.sample(lg, p, u, hist, hl, mask)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy(), prob.cpu().numpy(), st.cpu().numpy()
+
+
+def compare_plain(batch, got, label, key):
+    tok, prob, st = got
+    refs = oracle_rows(batch, 0)
+    n = dict(rows=0, tokens_equal=0, boundary=0, prob_on_cut_boundary=0)
+    for b, r in enumerate(refs):
+        exp_st = 0 if r.status == 0 else rlsampler.RL_ERR_NONFINITE
+        assert st[b] == exp_st, f"{label} row {b}: status {st[b]} vs {exp_st}"
+        n["rows"] += 1
+        if r.status:
+            continue
+        if tok[b] != r.token:
+            assert min(r.draw_margin, r.cut_margin) < BOUNDARY, (
+                f"{label} row {b}: token {tok[b]} vs oracle {r.token} "
+                f"(draw margin {r.draw_margin:.3g}, cut margin {r.cut_margin:.3g})")
+            n["boundary"] += 1
+            continue
+        n["tokens_equal"] += 1
+        if r.cut_margin < BOUNDARY and abs(prob[b] - r.prob) > PROB_RTOL * abs(r.prob):
+            n["prob_on_cut_boundary"] += 1
+            continue
+        np.testing.assert_allclose(prob[b], r.prob, rtol=PROB_RTOL, err_msg=f"{label} row {b}: prob")
+    parity_add(key, **n)
+
+
+SHORT = [c for c in SMALL if c[6] is None] + [
+    # B, V, T, top_k, top_p, hist, mask_density, ties: short unmasked rows
+    # whose ordered list spans several 1024-key batches, or a whole row
+    (4, 32000, 1.0, 129, 1.0, 64, None, False),
+    (4, 32000, 0.8, 500, 1.0, 64, None, False),
+    (4, 32000, 1.1, 3000, 0.97, 0, None, False),
+    (4, 45056, 1.3, 0, 0.999, 512, None, False),
+    (4, 20000, 1.0, 0, 0.9, 1024, None, True),
+    (64, 32000, 0.7, 50, 0.95, 0, None, False),
+]
+
+
+@pytest.mark.parametrize("case", SHORT, ids=lambda c: f"B{c[0]}_V{c[1]}_T{c[2]}_k{c[3]}_p{c[4]}_h{c[5]}")
+def test_short_rows_plain_entry(sampler, case):
+    B, V, T, k, tp, hl, md, ties = case
+    rng = np.random.default_rng((hash(case) + 1) & 0xFFFFFFFF)
+    batch = make_batch(rng, B, V, T, k, tp, hl, md, ties=ties)
+    compare_plain(batch, run_plain(sampler, batch), str(case), "short_rows_plain")
+
+
+def test_short_rows_config1_and_bf16(sampler):
+    for step in range(PARITY_STEPS):
+        batch = workloads.config1(step)
+        compare_plain(batch, run_plain(sampler, batch), f"config1 plain step {step}", "config1_plain")
+    rng = np.random.default_rng(99)
+    batch = make_batch(rng, 16, 32000, 0.9, 64, 0.95, 256, None)
+    bits = workloads.f32_to_bf16_bits(batch.logits)
+    batch.logits = workloads.bf16_bits_to_f32(bits)
+    batch.bf16_bits = bits
+    compare_plain(batch, run_plain(sampler, batch, bf16=True), "bf16 short rows", "short_rows_bf16")
+
+
+def test_short_rows_nonfinite(sampler):
+    rng = np.random.default_rng(8)
+    batch = make_batch(rng, 4, 300, 1.0, 0, 0.9)
+    batch.logits[1, 17] = np.nan
+    batch.logits[2, :] = -np.inf
+    batch.logits[3, 5] = np.inf
+    tok, prob, st = run_plain(sampler, batch)
+    assert list(st) == [0, rlsampler.RL_ERR_NONFINITE, rlsampler.RL_ERR_NONFINITE, rlsampler.RL_ERR_NONFINITE]
+    assert list(tok[1:]) == [-1, -1, -1]

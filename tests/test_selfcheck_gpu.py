@@ -104,15 +104,16 @@ def test_debug_flags_rejected_when_unknown():
 
 
 def test_kernel_times_after_a_timed_call():
-    """RL_DEBUG_TIMING: rl_sampler_kernel_times returns the streaming and
-    finish kernels' device times of the last call; off again, it returns none."""
+    """RL_DEBUG_TIMING: rl_sampler_kernel_times returns the device times of the
+    last call's kernels -- one for short unmasked rows (the short-row kernel),
+    two otherwise (the streaming and finish kernels); off again, none."""
     import workloads
 
-    b = workloads.config3(0)
     dev = torch.device("cuda", 0)
-    s = rlsampler.Sampler(0, max_batch=64, max_vocab=32000, max_history=0)
+    s = rlsampler.Sampler(0, max_batch=64, max_vocab=128256, max_history=512)
     try:
         assert s.kernel_times() == []
+        b = workloads.config3(0)
         lg = torch.from_numpy(b.logits).to(dev)
         mask = torch.from_numpy(b.mask.view(np.int32)).to(dev)
         prm = rlsampler.params_tensor(b.params, dev)
@@ -124,6 +125,18 @@ def test_kernel_times_after_a_timed_call():
         ref, _, _ = oracle.spec_sample_batch(b.logits, None, None, b.mask, b.params, b.uniforms)
         assert (st.cpu().numpy() == 0).all()
         assert (tok.cpu().numpy() == ref).mean() > 0.98
+        b2 = workloads.config2(0, rows=list(range(8)))
+        s.sample(torch.from_numpy(b2.logits).to(dev), rlsampler.params_tensor(b2.params, dev),
+                 torch.from_numpy(b2.uniforms).to(dev), torch.from_numpy(b2.hist).to(dev),
+                 torch.from_numpy(b2.hist_len).to(dev))
+        t = s.kernel_times()
+        assert len(t) == 2 and all(0.0 < x < 1000.0 for x in t)
+        b1 = workloads.config1(0)
+        s.sample(torch.from_numpy(b1.logits).to(dev), rlsampler.params_tensor(b1.params, dev),
+                 torch.from_numpy(b1.uniforms).to(dev), torch.from_numpy(b1.hist).to(dev),
+                 torch.from_numpy(b1.hist_len).to(dev))
+        t = s.kernel_times()
+        assert len(t) == 1 and 0.0 < t[0] < 1000.0
         s.set_debug(0)
         s.sample(lg, prm, u, mask=mask)
         assert s.kernel_times() == []
