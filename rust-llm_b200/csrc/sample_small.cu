@@ -1,4 +1,4 @@
-// The spec sampler for short rows: one CTA of 256 threads per row, the
+// The spec sampler for short rows: one CTA of 512 threads per row, the
 // whole row in shared memory, no pipeline and no second kernel.
 //
 // Same semantics as the streaming sampler (sample_spec.cu) and the CPU
@@ -35,7 +35,7 @@
 namespace rl {
 namespace {
 
-constexpr int kQT = 256;
+constexpr int kQT = 512;
 constexpr int kQW = kQT / 32;
 constexpr int kQBatch = 1024;     // keys ordered per batch
 constexpr int kQMaxBatch = 64;    // batch records kept for the draw
@@ -122,22 +122,23 @@ __device__ __forceinline__ double q_scan_d(double v, QShared& sh, double* total)
   return before + inc;
 }
 
-// The key of position i (finite allowed logits; -inf marks an excluded id).
-__device__ __forceinline__ bool q_key(const float* vals, int i, uint64_t prev, uint64_t* k) {
-  const float x = vals[i];
-  if (!(x > RL_NEG_INF)) return false;
-  *k = cand_key(x, static_cast<uint32_t>(i));
+// The key of position i from the row's value keys kv (ord_key of the
+// logit, 0 for an excluded id): (value key, then lower id first).
+__device__ __forceinline__ bool q_key(const uint32_t* kv, int i, uint64_t prev, uint64_t* k) {
+  const uint32_t k32 = kv[i];
+  if (k32 == 0u) return false;
+  *k = (static_cast<uint64_t>(k32) << 32) | static_cast<uint64_t>(0xffffffffu - static_cast<uint32_t>(i));
   return *k < prev;
 }
 
 // The need-th largest key among the keys below prev (1 <= need <= their
 // count): a radix select from the first byte where the keys differ.
-__device__ __noinline__ uint64_t q_select(const float* vals, int V, uint64_t prev, int need, QShared& sh) {
+__device__ __noinline__ uint64_t q_select(const uint32_t* kv, int V, uint64_t prev, int need, QShared& sh) {
   const int tid = threadIdx.x;
   uint64_t kmin = ~0ull, kmax = 0ull;
   for (int i = tid; i < V; i += kQT) {
     uint64_t k;
-    if (q_key(vals, i, prev, &k)) {
+    if (q_key(kv, i, prev, &k)) {
       kmin = k < kmin ? k : kmin;
       kmax = k > kmax ? k : kmax;
     }
@@ -153,7 +154,7 @@ __device__ __noinline__ uint64_t q_select(const float* vals, int V, uint64_t pre
     __syncthreads();
     for (int i = tid; i < V; i += kQT) {
       uint64_t k;
-      if (q_key(vals, i, prev, &k) && (shift + 8 >= 64 || (k >> (shift + 8)) == (prefix >> (shift + 8))))
+      if (q_key(kv, i, prev, &k) && (shift + 8 >= 64 || (k >> (shift + 8)) == (prefix >> (shift + 8))))
         atomicAdd(&sh.bins[(k >> shift) & 255u], 1u);
     }
     __syncthreads();
@@ -197,7 +198,7 @@ __device__ __noinline__ uint64_t q_select(const float* vals, int V, uint64_t pre
       uint64_t mn = ~0ull;
       for (int i = tid; i < V; i += kQT) {
         uint64_t k;
-        if (q_key(vals, i, prev, &k) && (k >> shift) == (prefix >> shift)) mn = k < mn ? k : mn;
+        if (q_key(kv, i, prev, &k) && (k >> shift) == (prefix >> shift)) mn = k < mn ? k : mn;
       }
       return q_minmax_u64(mn, false, sh);
     }
@@ -226,9 +227,11 @@ __device__ __noinline__ void q_sort_desc(uint64_t* a, int P) {
 // Descending bitonic sort of kQT keys, one per thread (thread t holds
 // position t before and after): shuffles within a warp, the shared scratch
 // xs across warps.
-__device__ __forceinline__ uint64_t q_sort_regs(uint64_t v, uint64_t* xs) {
+__device__ __noinline__ uint64_t q_sort_regs(uint64_t v, uint64_t* xs) {
   const int tid = threadIdx.x;
+#pragma unroll 1
   for (int k = 2; k <= kQT; k <<= 1)
+#pragma unroll 1
     for (int j = k >> 1; j > 0; j >>= 1) {
       uint64_t y;
       if (j < 32) {
@@ -266,13 +269,13 @@ __device__ void q_sort_keys(uint64_t* keys, int c) {
 
 // Keys >= tau and below prev into keys[0, c) (unordered); returns c (the
 // writes stop at kQGather, the count does not).
-__device__ int q_gather(const float* vals, int V, uint64_t prev, uint64_t tau, uint64_t* keys, QShared& sh) {
+__device__ __noinline__ int q_gather(const uint32_t* kv, int V, uint64_t prev, uint64_t tau, uint64_t* keys, QShared& sh) {
   __syncthreads();
   if (threadIdx.x == 0) sh.cnt = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < V; i += kQT) {
     uint64_t k;
-    if (q_key(vals, i, prev, &k) && k >= tau) {
+    if (q_key(kv, i, prev, &k) && k >= tau) {
       const int j = atomicAdd(&sh.cnt, 1);
       if (j < kQGather) keys[j] = k;
     }
@@ -282,11 +285,11 @@ __device__ int q_gather(const float* vals, int V, uint64_t prev, uint64_t tau, u
 }
 
 // Count of the keys >= tau below prev.
-__device__ int q_count(const float* vals, int V, uint64_t prev, uint64_t tau, QShared& sh) {
+__device__ __noinline__ int q_count(const uint32_t* kv, int V, uint64_t prev, uint64_t tau, QShared& sh) {
   int c = 0;
   for (int i = threadIdx.x; i < V; i += kQT) {
     uint64_t k;
-    c += (q_key(vals, i, prev, &k) && k >= tau) ? 1 : 0;
+    c += (q_key(kv, i, prev, &k) && k >= tau) ? 1 : 0;
   }
   return q_sum_i(c, sh);
 }
@@ -302,7 +305,7 @@ __device__ int q_count(const float* vals, int V, uint64_t prev, uint64_t tau, QS
 // times) until n <= count <= kQGather; then one gather and one sort. An
 // exact radix select sets the threshold when the sample cannot (heavy
 // ties, or the keys below prev spread unevenly over the sample).
-__device__ int q_batch(const float* vals, int V, uint64_t prev, int left, int elig, float M, const RowT& rt,
+__device__ __noinline__ int q_batch(const uint32_t* kv, int V, uint64_t prev, int left, int elig, float M, const RowT& rt,
                        double Z, double base, uint64_t* keys, double* cum, QShared& sh) {
   const int tid = threadIdx.x;
   const int n = min(kQBatch, left);
@@ -314,7 +317,7 @@ __device__ int q_batch(const float* vals, int V, uint64_t prev, int left, int el
     uint64_t sk = 0ull;
     if (tid * st < V) {
       uint64_t k;
-      if (q_key(vals, tid * st, prev, &k)) sk = k;
+      if (q_key(kv, tid * st, prev, &k)) sk = k;
     }
     const int ns = q_sum_i(sk != 0ull ? 1 : 0, sh);
     keys[tid] = q_sort_regs(sk, keys + kQT);
@@ -324,7 +327,7 @@ __device__ int q_batch(const float* vals, int V, uint64_t prev, int left, int el
       for (int tries = 0; tries < 4 && !ok; ++tries) {
         const int rr = static_cast<int>(min(r, static_cast<long long>(ns - 1)));
         const uint64_t t = keys[rr];
-        const int c = q_count(vals, V, prev, t, sh);
+        const int c = q_count(kv, V, prev, t, sh);
         if (c >= n && c <= kQGather) {
           tau = t;
           ok = true;
@@ -338,8 +341,8 @@ __device__ int q_batch(const float* vals, int V, uint64_t prev, int left, int el
       }
     }
   }
-  if (!ok) tau = q_select(vals, V, prev, n, sh);
-  const int ng = min(q_gather(vals, V, prev, tau, keys, sh), kQGather);
+  if (!ok) tau = q_select(kv, V, prev, n, sh);
+  const int ng = min(q_gather(kv, V, prev, tau, keys, sh), kQGather);
   q_sort_keys(keys, ng);
   // cumulative probabilities, kQT positions per round
   double run = base;
@@ -521,6 +524,14 @@ __global__ void __launch_bounds__(kQT, 1) small_rows_kernel(const __grid_constan
       zf += y;
     }
   const double Z = q_sum_d(static_cast<double>(zf), sh);
+  // the row as value keys from here on (ord_key of the logit with -0 read as
+  // +0; 0, which no finite logit maps to, marks an excluded id)
+  uint32_t* kv = reinterpret_cast<uint32_t*>(vals);
+  for (int i = tid; i < V; i += kQT) {
+    const float v = vals[i];
+    kv[i] = v > RL_NEG_INF ? ord_key(__fadd_rn(v, 0.0f)) : 0u;
+  }
+  __syncthreads();
   // ---- 6.-8. the ordered list in batches: cutoff, then the draw ----
   const int K = (prm.top_k > 0) ? min(prm.top_k, nal) : nal;
   const bool mass = prm.top_p < 1.0f;
@@ -540,7 +551,7 @@ __global__ void __launch_bounds__(kQT, 1) small_rows_kernel(const __grid_constan
       sh.bcum[nb] = base;
       sh.bpos[nb] = pos;
     }
-    const int n = q_batch(vals, V, prev, K - pos, nal - pos, M, rt, Z, base, keys, cum, sh);
+    const int n = q_batch(kv, V, prev, K - pos, nal - pos, M, rt, Z, base, keys, cum, sh);
     ++nb;
     if (cutoff < 0) {
       int c = INT_MAX;
@@ -571,7 +582,7 @@ __global__ void __launch_bounds__(kQT, 1) small_rows_kernel(const __grid_constan
   int b = nb - 1;
   while (b > 0 && sh.bcum[b] > target) --b;
   if (b != nb - 1) {
-    q_batch(vals, V, sh.bprev[b], K - sh.bpos[b], nal - sh.bpos[b], M, rt, Z, sh.bcum[b], keys, cum, sh);
+    q_batch(kv, V, sh.bprev[b], K - sh.bpos[b], nal - sh.bpos[b], M, rt, Z, sh.bcum[b], keys, cum, sh);
   }
   const int p0 = sh.bpos[b];
   const int lim = min(cutoff - p0, kQBatch - 1);  // last position of this batch the draw may take
