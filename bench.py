@@ -577,7 +577,9 @@ def main():
             kern = "the whole step (its kernels timed together)"
         # config 1 samples one token per step and rank: microseconds per token
         value = ms * 1e3 if cfg == 1 else value_units_per_s
-        traffic = committed_traffic().get(f"spec_step_f32_config{cfg}") if cfg == 2 else None
+        traffic = {2: committed_traffic().get("spec_pipe_kernel_f32_config2"),
+                   1: committed_traffic().get("small_rows_kernel_f32_config1"),
+                   }.get(cfg)
         line = {
             "metric": c["metric"], "value": value, "unit": c["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": c["higher"],
@@ -590,7 +592,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "kernel": kern, "algorithmic_bytes_per_launch": alg,
                          "kernel_ms": dom_ms, "step_gbs": step_gbs, "step_frac": step_gbs / peak, "traffic": traffic,
-                         "traffic_source": "profiles/traffic.json (ncu dram__bytes of one launch)" if traffic else None},
+                         "traffic_source": "profiles/traffic.json (ncu dram__bytes of one launch of the kernel above)" if traffic else None},
             "kernel_ms": (({"spec_pipe_kernel": kernel_ms[0], "spec_finish_kernel": kernel_ms[1]}
                            if len(kernel_ms) > 1 else {"small_rows_kernel": kernel_ms[0]}) if kernel_ms else None),
             "gpu_launches": launches_per_step * args.steps,
