@@ -349,6 +349,22 @@ class Sampler:
               "rl_sample_host")
         return out_tok, out_prob
 
+    def decoder_sample(self, logits, temperature, top_p, uniforms, out_tok=None, out_prob=None, stream=None):
+        """rl_decoder_sample: Decoder::sample_with_params semantics on device rows
+        [B, V] f32; temperature / top_p / uniforms are [B] f32 device tensors."""
+        import torch
+
+        B, V = logits.shape
+        dev = logits.device
+        if out_tok is None:
+            out_tok = torch.empty(B, dtype=torch.int32, device=dev)
+        if out_prob is None:
+            out_prob = torch.empty(B, dtype=torch.float32, device=dev)
+        check(lib().rl_decoder_sample(self.h, _ptr(logits), B, V, logits.stride(0), _ptr(temperature), _ptr(top_p),
+                                      _ptr(uniforms), _ptr(out_tok), _ptr(out_prob), _stream(stream)),
+              "rl_decoder_sample")
+        return out_tok, out_prob
+
     def decoder_sample_host(self, logits, temperature, top_p, uniforms):
         """rl_decoder_sample_host: Decoder::sample_with_params semantics on host
         rows [B, V] f32 with per-row temperature / top_p / uniform; returns
