@@ -1,6 +1,6 @@
 // CPU oracle for the logits -> token sampling path of chenyusolar/rust-llm.
 //
-// TEST INFRASTRUCTURE ONLY. This file is the checker for the CUDA sampler:
+// TEST INFRASTRUCTURE ONLY. This file is the oracle the CUDA sampler is tested against:
 // only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
 // legs may load it. The product library never links or calls it.
 //
