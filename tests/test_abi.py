@@ -65,3 +65,37 @@ def test_error_message_is_thread_local():
     t.join()
     assert seen["msg"] == ""
     assert rlsampler.last_error() != ""
+
+
+def test_every_handle_entry_rejects_a_null_handle():
+    """Each entry that takes a handle answers a NULL handle with
+    RL_ERR_INVALID_ARG and a message, before touching any device."""
+    L = rlsampler.lib()
+    P = None
+    calls = {
+        "rl_decoder_sample": lambda: L.rl_decoder_sample(P, P, 1, 10, 10, P, P, P, P, P, P),
+        "rl_decoder_sample_host": lambda: L.rl_decoder_sample_host(P, P, 1, 10, P, P, P, P, P),
+        "rl_greedy_host": lambda: L.rl_greedy_host(P, P, 1, 10, P),
+        "rl_grammar_greedy_host": lambda: L.rl_grammar_greedy_host(P, P, 1, 10, P, 1, P),
+        "rl_specdec_sample": lambda: L.rl_specdec_sample(P, P, 1, 10, 10, P, P, P, P, P),
+        "rl_specdec_verify": lambda: L.rl_specdec_verify(P, P, 1, 10, 10, P, 4, P, P, P, P, P, P, P),
+        "rl_sample_sharded": lambda: L.rl_sample_sharded(P, P, P, 0, 1, 10, 10, 0, 10, P, P, 0, P, 0, P, P, P, P,
+                                                         P, P),
+        "rl_sampler_set_debug": lambda: L.rl_sampler_set_debug(P, 0),
+    }
+    for name, call in calls.items():
+        st = call()
+        assert st == rlsampler.RL_ERR_INVALID_ARG, (name, st)
+        assert rlsampler.last_error(), name
+
+
+def test_selfcheck_and_nccl_helpers_reject_bad_arguments():
+    L = rlsampler.lib()
+    assert L.rl_selfcheck_div(None, -1, None, 1, None, None, None) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_selfcheck_div(None, 0, None, 0, None, None, None) == rlsampler.RL_OK  # nothing to do
+    assert L.rl_nccl_unique_id(None) == rlsampler.RL_ERR_INVALID_ARG
+    comm = ctypes.c_void_p()
+    uid = (ctypes.c_char * rlsampler.NCCL_ID_BYTES)()
+    assert L.rl_nccl_comm_init(ctypes.byref(comm), 2, uid, 5) == rlsampler.RL_ERR_INVALID_ARG  # rank >= nranks
+    assert L.rl_nccl_comm_init(None, 1, uid, 0) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_nccl_comm_destroy(None) == rlsampler.RL_OK
