@@ -151,7 +151,8 @@ class Sampler:
 
     def with_grammar(self, grammar) -> "Sampler":
         """Sampler::with_grammar: `grammar` has get_allowed_tokens(prev_tokens)
-        -> iterable of ids (the reference's Grammar, src/decoder.rs:467-529)."""
+        -> iterable of ids -- grammar.Grammar, the reference's Grammar
+        (src/decoder.rs:378-557), or any object with that method."""
         self.grammar = grammar
         return self
 

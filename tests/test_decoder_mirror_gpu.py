@@ -90,3 +90,19 @@ def test_greedy_sample_last_maximum():
     assert d.greedy_sample(x) == 999 == oracle.greedy(x)
     y = workloads.config1(3).logits[0]
     assert d.greedy_sample(y) == oracle.greedy(y)
+
+
+def test_sampler_with_the_reference_grammar():
+    """Sampler.with_grammar over grammar.Grammar (the reference's parser and
+    state machine): each step's mask comes from the last ten tokens."""
+    import grammar
+
+    g = grammar.Grammar.from_ggnf('a ::= "xy" | [5, 7, 9]\nb ::= a | "z"\nc ::= b | "{" | [0, 1, 2]\n')
+    V = 256
+    rng = np.random.default_rng(21)
+    s = decoder.Sampler().with_grammar(g)
+    for step in range(40):
+        x = rng.normal(0.0, 2.0, V).astype(np.float32)
+        m = g.mask(s.prev_tokens, V)
+        want = oracle.grammar_greedy(x, m)
+        assert s.sample(x) == want, f"step {step}"
