@@ -279,6 +279,37 @@ rl_status rl_specdec_verify(rl_sampler* h, const float* logits, int B, int V, in
                             const float* draw_u, int32_t* out_accepted, int32_t* out_tok, void* stream);
 
 /*
+ * LM head feeding the sampler (src/model.rs:236-262: the final projection of
+ * Model::forward, matmul_vec's logits[i] = sum_j hidden[j] * W[i * H + j]),
+ * batched, on the tensor cores: logits[b, v] = sum_h hidden[b, h] * W[v, h].
+ * hidden [B, ldh] and weight [V, ldw] are bf16 (raw uint16 bits), K-major,
+ * 16-byte aligned, ldh and ldw multiples of 8; H a multiple of 64; the sums
+ * are f32 (products of bf16 values are exact in f32; the order of the
+ * additions is the tensor cores', not the reference's left-to-right loop).
+ * Any B (rows beyond 256 run as further launches that stream the weight
+ * again); B <= max_batch of the handle.
+ *
+ * rl_lmhead_logits: the logits into out_logits [B, ldo] (RL_F32 or RL_BF16,
+ *   rounded to nearest even).
+ * rl_lmhead_greedy: Decoder::greedy_sample (src/decoder.rs:160-167) of those
+ *   logits, LAST maximum on ties, fused into the GEMM's epilogue: out_tok[B]
+ *   and row_status[B] (nullable; RL_ERR_TIMEOUT with token -1 when a device
+ *   wait ran out). out_logits (f32, nullable) also receives the logits; when
+ *   it is NULL the logits are never written to memory.
+ * rl_lmhead_sample: the logits (f32) into the handle's staging buffer, then
+ *   rl_sample_batch on them (no mask); V <= max_vocab of the handle.
+ */
+rl_status rl_lmhead_logits(rl_sampler* h, const uint16_t* hidden, int64_t ldh, const uint16_t* weight, int64_t ldw,
+                           int B, int H, int V, void* out_logits, rl_dtype out_dtype, int64_t ldo, void* stream);
+rl_status rl_lmhead_greedy(rl_sampler* h, const uint16_t* hidden, int64_t ldh, const uint16_t* weight, int64_t ldw,
+                           int B, int H, int V, int32_t* out_tok, int32_t* row_status, float* out_logits, int64_t ldo,
+                           void* stream);
+rl_status rl_lmhead_sample(rl_sampler* h, const uint16_t* hidden, int64_t ldh, const uint16_t* weight, int64_t ldw,
+                           int B, int H, int V, const int32_t* hist, const int32_t* hist_len, int hist_stride,
+                           const rl_row_params* params, const float* uniforms, int32_t* out_tok, float* out_prob,
+                           int32_t* row_status, void* stream);
+
+/*
  * Vocabulary-sharded sampling (a row's logits split by vocabulary across
  * devices). No single reference function: it splits the spec pipeline above
  * so that each device streams only its columns and the devices exchange 4 KB

@@ -42,6 +42,10 @@ struct rl_sampler {
   uint64_t* shard_send = nullptr;  // [max_batch * kRec]
   uint64_t* shard_recv = nullptr;  // [kMergeMaxShards * max_batch * kRec]
   float* zero_u = nullptr;            // uniforms of partial launches (unused, zero)
+  // LM head (rl_lmhead_*): per-CTA row maxima [min(max_batch, 256) * num_sms]
+  // and the GEMM's timeout flag
+  uint64_t* lm_part = nullptr;
+  int* lm_err = nullptr;
 };
 
 namespace rl {

@@ -37,6 +37,7 @@ rl_status alloc_workspace(rl_sampler* h) {
     ok = ok && dalloc(&h->shard_send, B * kRec) && dalloc(&h->shard_recv, static_cast<size_t>(kMergeMaxShards) * B * kRec);
   ok = ok && dalloc(&h->part_keys, B * kN) && dalloc(&h->part_stats, B) && dalloc(&h->beam_params, B) &&
        dalloc(&h->zero_u, B);
+  ok = ok && dalloc(&h->lm_part, (B < 256 ? B : 256) * static_cast<size_t>(h->num_sms)) && dalloc(&h->lm_err, 1);
   for (int i = 0; i < 3 && ok; ++i) ok = cudaEventCreate(&h->ev[i]) == cudaSuccess;
   if (ok) ok = cudaMemset(h->ws.row_done, 0, sizeof(int32_t) * B) == cudaSuccess &&
                cudaMemset(h->zero_u, 0, sizeof(float) * B) == cudaSuccess &&
@@ -77,10 +78,14 @@ void free_workspace(rl_sampler* h) {
   cudaFree(h->part_stats);
   cudaFree(h->beam_params);
   cudaFree(h->zero_u);
+  cudaFree(h->lm_part);
+  cudaFree(h->lm_err);
   h->part_keys = nullptr;
   h->part_stats = nullptr;
   h->beam_params = nullptr;
   h->zero_u = nullptr;
+  h->lm_part = nullptr;
+  h->lm_err = nullptr;
   for (int i = 0; i < 3; ++i)
     if (h->ev[i]) cudaEventDestroy(h->ev[i]);
   if (h->stream) cudaStreamDestroy(h->stream);

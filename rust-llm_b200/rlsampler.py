@@ -140,6 +140,12 @@ def lib():
         L.rl_sampler_set_debug.argtypes = [P, ctypes.c_uint32]
         L.rl_selfcheck_div.restype = I
         L.rl_selfcheck_div.argtypes = [P, I, P, I, P, P, P]
+        L.rl_lmhead_logits.restype = I
+        L.rl_lmhead_logits.argtypes = [P, P, I64, P, I64, I, I, I, P, I, I64, P]
+        L.rl_lmhead_greedy.restype = I
+        L.rl_lmhead_greedy.argtypes = [P, P, I64, P, I64, I, I, I, P, P, P, I64, P]
+        L.rl_lmhead_sample.restype = I
+        L.rl_lmhead_sample.argtypes = [P, P, I64, P, I64, I, I, I, P, P, I, P, P, P, P, P, P]
         _lib = L
     return _lib
 
@@ -433,6 +439,68 @@ class Sampler:
                                       _stream(stream)),
               "rl_specdec_verify")
         return acc, tok
+
+    # -- LM head ------------------------------------------------------------
+    @staticmethod
+    def _lm_operands(hidden, weight):
+        import torch
+
+        if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+            raise ValueError("lmhead: hidden and weight must be bf16")
+        if hidden.stride(1) != 1 or weight.stride(1) != 1:
+            raise ValueError("lmhead: hidden and weight must be row-major (unit inner stride)")
+        B, H = hidden.shape
+        V, H2 = weight.shape
+        if H != H2:
+            raise ValueError(f"lmhead: hidden has {H} columns, weight {H2}")
+        return B, H, V
+
+    def lmhead_logits(self, hidden, weight, out=None, out_dtype=None, stream=None):
+        """rl_lmhead_logits: hidden [B, H] @ weight[V, H]^T on the tensor
+        cores (bf16 operands, f32 sums) into out [B, V] (f32 or bf16)."""
+        import torch
+
+        B, H, V = self._lm_operands(hidden, weight)
+        if out is None:
+            out = torch.empty(B, V, dtype=out_dtype or torch.float32, device=hidden.device)
+        dt = RL_BF16 if out.dtype == torch.bfloat16 else RL_F32
+        check(lib().rl_lmhead_logits(self.h, _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), B, H, V,
+                                     _ptr(out), dt, out.stride(0), _stream(stream)),
+              "rl_lmhead_logits")
+        return out
+
+    def lmhead_greedy(self, hidden, weight, out_logits=None, stream=None):
+        """rl_lmhead_greedy: the last-maximum argmax of each row's logits,
+        fused into the GEMM. Returns (tokens [B], row_status [B]); out_logits
+        (f32 [B, V], optional) also receives the logits."""
+        import torch
+
+        B, H, V = self._lm_operands(hidden, weight)
+        tok = torch.empty(B, dtype=torch.int32, device=hidden.device)
+        st = torch.empty(B, dtype=torch.int32, device=hidden.device)
+        ldo = out_logits.stride(0) if out_logits is not None else V
+        check(lib().rl_lmhead_greedy(self.h, _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), B, H, V,
+                                     _ptr(tok), _ptr(st), _ptr(out_logits), ldo, _stream(stream)),
+              "rl_lmhead_greedy")
+        return tok, st
+
+    def lmhead_sample(self, hidden, weight, params, uniforms, hist=None, hist_len=None, out_tok=None, out_prob=None,
+                      row_status=None, stream=None):
+        """rl_lmhead_sample: the LM head's logits sampled by the batched
+        sampler (same params / uniforms / history as sample())."""
+        import torch
+
+        B, H, V = self._lm_operands(hidden, weight)
+        dev = hidden.device
+        out_tok = out_tok if out_tok is not None else torch.empty(B, dtype=torch.int32, device=dev)
+        out_prob = out_prob if out_prob is not None else torch.empty(B, dtype=torch.float32, device=dev)
+        row_status = row_status if row_status is not None else torch.empty(B, dtype=torch.int32, device=dev)
+        hs = hist.shape[1] if hist is not None else 0
+        check(lib().rl_lmhead_sample(self.h, _ptr(hidden), hidden.stride(0), _ptr(weight), weight.stride(0), B, H, V,
+                                     _ptr(hist), _ptr(hist_len), hs, _ptr(params), _ptr(uniforms), _ptr(out_tok),
+                                     _ptr(out_prob), _ptr(row_status), _stream(stream)),
+              "rl_lmhead_sample")
+        return out_tok, out_prob, row_status
 
     def sample_host_ptrs(self, logits_p, B, V, params_p, u_p, tok_p, prob_p, hist_p=None, hist_len_p=None,
                          hist_stride=0, mask_p=None, mask_stride=0):

@@ -82,6 +82,9 @@ def test_every_handle_entry_rejects_a_null_handle():
         "rl_sample_sharded": lambda: L.rl_sample_sharded(P, P, P, 0, 1, 10, 10, 0, 10, P, P, 0, P, 0, P, P, P, P,
                                                          P, P),
         "rl_sampler_set_debug": lambda: L.rl_sampler_set_debug(P, 0),
+        "rl_lmhead_logits": lambda: L.rl_lmhead_logits(P, P, 64, P, 64, 1, 64, 10, P, 0, 10, P),
+        "rl_lmhead_greedy": lambda: L.rl_lmhead_greedy(P, P, 64, P, 64, 1, 64, 10, P, P, P, 10, P),
+        "rl_lmhead_sample": lambda: L.rl_lmhead_sample(P, P, 64, P, 64, 1, 64, 10, P, P, 0, P, P, P, P, P, P),
     }
     for name, call in calls.items():
         st = call()
