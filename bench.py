@@ -52,6 +52,9 @@ CONFIGS = {
     5: dict(workload="vocab_shard_b1024_v256000_bf16", B=1024, V=256000, H=256,
             metric="sampled tokens/s at batch 1024 x vocab 256000 bf16, vocabulary split across the GPUs",
             unit="tokens/s", higher=True),
+    6: dict(workload="lmhead_sample_b256_h4096_v128256_bf16", B=256, V=128256, H=512, HID=4096,
+            metric="sampled tokens/s from final hidden states at batch 256 x hidden 4096 x vocab 128256 "
+                   "(bf16 LM head on the tensor cores + the batched sampler)", unit="tokens/s", higher=True),
 }
 
 
@@ -300,7 +303,24 @@ def run_reference(args, rank, world):
     cfg = args.config
     B = c["B"]
 
+    if cfg == 6:
+        # hidden states and the random-init weight as bf16 values held in f32
+        # (the reference dequantizes its weights to f32, src/model.rs:237)
+        r = np.random.Generator(np.random.PCG64(6000))
+        HID = c["HID"]
+
+        def bf16_round(a):
+            u = a.view(np.uint32)
+            return ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).view(np.float32)
+
+        weight = bf16_round(r.standard_normal((c["V"], HID), dtype=np.float32) * np.float32(HID ** -0.5 * 3.0))
+
     def batch(i):
+        if cfg == 6:
+            rb = np.random.Generator(np.random.PCG64(6100 + i))
+            p, hist, u = config2_params(600 + i, B, c["V"], c["H"])
+            return dict(hidden=bf16_round(rb.standard_normal((B, c["HID"]), dtype=np.float32)), params=p, hist=hist,
+                        hl=np.full(B, c["H"], np.int32), u=u)
         if cfg == 1:
             b = workloads.config1(i)
         elif cfg == 2:
@@ -316,6 +336,10 @@ def run_reference(args, rank, world):
     steps = [batch(i) for i in range(min(args.steps, 4))]
 
     def run(b):
+        if cfg == 6:
+            lg = oracle.matmul_vec(b["hidden"], weight, nthreads=nthreads)
+            oracle.spec_sample_batch(lg, b["hist"], b["hl"], None, b["params"], b["u"], nthreads=nthreads)
+            return B
         if cfg == 4:
             oracle.beam_step(b.logits, b.items, b.beams, b.scores, b.done, b.lens, b.alpha, b.eos, 1, 2 * b.beams)
             return b.items * b.beams
@@ -337,11 +361,11 @@ def run_reference(args, rank, world):
     dt = time.perf_counter() - t0
     v = units / dt
     value = 1e6 / v if cfg == 1 else v
-    rows = (steps[0].items * steps[0].beams) if cfg == 4 else steps[0].logits.shape[0]
+    rows = (steps[0].items * steps[0].beams) if cfg == 4 else (B if cfg == 6 else steps[0].logits.shape[0])
     line.update({
         "value": value, "n_gpus": args.gpus, "steps": done, "steps_requested": args.steps, "warmup": args.warmup,
         "ms_per_step": dt / done * 1e3, "scaling": "weak" if cfg != 5 else "strong", "vs_baseline": None,
-        "dtype": "bf16" if cfg == 5 else "f32", "data": "synthetic",
+        "dtype": "bf16" if cfg in (5, 6) else "f32", "data": "synthetic",
         "config": {"workload": c["workload"], "rows_per_step": rows, "vocab": c["V"],
                    "distinct_steps": len(steps), "same_config": cfg != 5},
         "cpu_baseline": {"value": value, "unit": c["unit"], "cores": nthreads, "kind": "port", "cpu_model": cpu_model(),
@@ -416,9 +440,168 @@ def shard_step_line(steps, warmup, dev, rank, world, stream):
             "algorithmic_bytes_per_gpu": algorithmic_bytes(5, world)}
 
 
+def lmhead_line(args, dev, rank, world, stream):
+    """Config 6: hidden states -> tokens. The LM head (src/model.rs:236-262)
+    as one tcgen05 GEMM (rl_lmhead_sample: bf16 weight [V, 4096] resident in
+    HBM, f32 logits into the handle's staging buffer) and the batched sampler
+    on config-2 sampling parameters; plus the fused greedy path (no logits
+    written) and single-row decode."""
+    import torch
+
+    import rlsampler
+
+    c = CONFIGS[6]
+    B, V, H, HID = c["B"], c["V"], c["H"], c["HID"]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(6000 + 7919 * rank)
+    weight = (torch.randn((V, HID), generator=gen, device=dev) * HID ** -0.5 * 3.0).to(torch.bfloat16)
+    pool = []
+    for i in range(POOL):
+        d = {"hidden": torch.randn((B, HID), generator=gen, device=dev).to(torch.bfloat16)}
+        p, hist, u = config2_params(600 + i + 100 * rank, B, V, H)
+        d["params"] = rlsampler.params_tensor(p, dev)
+        d["u"] = torch.from_numpy(np.ascontiguousarray(u)).to(dev)
+        d["hist"] = torch.from_numpy(np.ascontiguousarray(hist)).to(dev)
+        d["hl"] = torch.full((B,), H, dtype=torch.int32, device=dev)
+        pool.append(d)
+    s = rlsampler.Sampler(dev.index, max_batch=B, max_vocab=V, max_history=H)
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+
+    def step(i):
+        d = pool[i % POOL]
+        s.lmhead_sample(d["hidden"], weight, d["params"], d["u"], d["hist"], d["hl"], tok, prob, st, stream=stream)
+
+    ms, clocks = timed_loop(step, args.steps, args.warmup, stream, world, dev)
+    bad = int((st != 0).sum().item())
+
+    def ev_loop(fn, n, warm=3):
+        for i in range(warm):
+            fn(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    logits = torch.empty((B, V), dtype=torch.float32, device=dev)
+    gemm_ms = ev_loop(lambda i: s.lmhead_logits(pool[i % POOL]["hidden"], weight, out=logits, stream=stream), 20)
+    greedy_ms = ev_loop(lambda i: s.lmhead_greedy(pool[i % POOL]["hidden"], weight, stream=stream), 20)
+    h1 = pool[0]["hidden"][:1]
+    decode_ms = ev_loop(lambda i: s.lmhead_greedy(h1, weight, stream=stream), 20)
+    flops = 2.0 * B * HID * V
+    w_bytes = V * HID * 2
+    if rank != 0:
+        s.close()
+        return None
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except Exception:
+        pass
+    tf_peak = float(peaks.get("bf16_tflops", 1590.0))
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
+    traffic = committed_traffic().get("lmhead_kernel_b256_h4096_v128256")
+
+    # end to end through the C ABI: pinned host hidden states in, tokens out
+    # (the weight is resident, as in a serving engine)
+    hh = torch.empty((B, HID), dtype=torch.bfloat16, pin_memory=True)
+    hh.copy_(pool[0]["hidden"].cpu())
+    htok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    dh = torch.empty((B, HID), dtype=torch.bfloat16, device=dev)
+    d0 = pool[0]
+
+    def e2e_step():
+        dh.copy_(hh, non_blocking=True)
+        s.lmhead_sample(dh, weight, d0["params"], d0["u"], d0["hist"], d0["hl"], tok, prob, st, stream=stream)
+        htok.copy_(tok, non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    t0 = time.perf_counter()
+    ne = max(args.e2e_steps, 10)
+    for _ in range(ne):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / ne
+    hbm_bytes = w_bytes + B * HID * 2 + B * V * 4
+    line = {
+        "metric": c["metric"], "value": world * B / (ms / 1e3), "unit": c["unit"], "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded hidden states, random-init bf16 weight)",
+        "config": {"workload": c["workload"], "global_batch": B * world, "per_gpu_batch": B, "hidden": HID, "vocab": V,
+                   "history": H, "parallelism": f"rows{world}",
+                   "l2": "the 1.05 GB weight (larger than L2) streams from HBM every step"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tf_peak, "peak_kind": "measured (burst)" if peaks else "fallback",
+                     "kernel": "lmhead_kernel (tcgen05 GEMM, logits written in f32), CUDA events around 20 launches",
+                     "kernel_ms": gemm_ms, "flops_per_launch": flops,
+                     "hbm_view": {"bytes": hbm_bytes, "gbs": hbm_bytes / (gemm_ms * 1e-3) / 1e9, "peak": hbm_peak},
+                     "traffic": traffic,
+                     "traffic_source": "profiles/traffic.json (ncu dram__bytes of one launch)" if traffic else None},
+        "kernel_ms": {"lmhead_kernel": gemm_ms, "sampler (step - GEMM)": ms - gemm_ms},
+        "greedy_fused": {"value": B / (greedy_ms / 1e3), "unit": "tokens/s", "ms_per_step": greedy_ms,
+                         "path": "rl_lmhead_greedy: argmax in the GEMM epilogue, logits never written"},
+        "decode_b1": {"us_per_token": decode_ms * 1e3, "weight_gbs": w_bytes / (decode_ms * 1e-3) / 1e9,
+                      "frac_of_hbm_peak": w_bytes / (decode_ms * 1e-3) / 1e9 / hbm_peak,
+                      "path": "rl_lmhead_greedy at B=1 (weight-streaming GEMV on the tensor cores)"},
+        "gpu_launches": 4 * args.steps,
+        "rows_not_ok": bad,
+        "e2e": {"value": B / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * HID * 2, "d2h_bytes_per_step": B * 4,
+                "ms_per_step": e2e_s * 1e3,
+                "path": "pinned hidden states -> device, rl_lmhead_sample, tokens -> pinned host, sync per step"},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        import oracle
+        from rlsampler import ROW_PARAMS_DTYPE
+
+        x = pool[0]["hidden"].float().cpu().numpy()
+        w = weight.float().cpu().numpy()
+        s.lmhead_logits(pool[0]["hidden"], weight, out=logits, stream=stream)
+        torch.cuda.synchronize()
+        lg_dev = logits.cpu().numpy()
+        p0 = pool[0]["params"].cpu().numpy().view(ROW_PARAMS_DTYPE)
+        hist0, hl0, u0 = pool[0]["hist"].cpu().numpy(), pool[0]["hl"].cpu().numpy(), pool[0]["u"].cpu().numpy()
+        out = {}
+        nall = os.cpu_count() or 1
+        ref = None
+        for label, nth, rows in (("1core", 1, 2), ("all", nall, nall)):
+            rows = min(rows, B)
+            t0 = time.perf_counter()
+            lg = oracle.matmul_vec(x[:rows], w, nthreads=nth)
+            oracle.spec_sample_batch(lg, hist0[:rows], hl0[:rows], None, p0[:rows], u0[:rows], nthreads=nth)
+            dt = time.perf_counter() - t0
+            out[label] = {"value": rows / dt, "rows": rows, "seconds": dt, "threads": nth}
+            ref = lg
+        n = ref.shape[0]
+        bound = HID * 2.0 ** -21 * (np.abs(x[:n]).astype(np.float64) @ np.abs(w).astype(np.float64).T)
+        err = np.abs(lg_dev[:n].astype(np.float64) - ref.astype(np.float64))
+        dtok, _, _ = oracle.spec_sample_batch(lg_dev[:n], hist0[:n], hl0[:n], None, p0[:n], u0[:n], nthreads=nall)
+        s.lmhead_sample(pool[0]["hidden"], weight, pool[0]["params"], pool[0]["u"], pool[0]["hist"], pool[0]["hl"],
+                        tok, prob, st, stream=stream)
+        torch.cuda.synchronize()
+        line["cpu_baseline"] = {"value": out["1core"]["value"], "unit": "tokens/s", "cores": 1, "kind": "port",
+                                "all_cores": out["all"], "cpu_model": cpu_model(),
+                                "sample": f"{out['1core']['rows']} rows (matmul_vec + spec sampler, one thread); "
+                                          f"{out['all']['rows']} rows on {nall} threads"}
+        line["parity_sample"] = {"rows": int(n), "logits_max_abs_err_vs_oracle": float(err.max()),
+                                 "logits_within_f32_sum_bound": bool((err <= bound).all()),
+                                 "tokens_equal_oracle_sampler_on_device_logits":
+                                     int((tok.cpu().numpy()[:n] == dtok).sum())}
+    s.close()
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5, 6])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=10)
@@ -430,7 +613,7 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.steps is None:
-        args.steps = {1: 2000, 2: 200, 3: 500, 4: 200, 5: 50}[args.config]
+        args.steps = {1: 2000, 2: 200, 3: 500, 4: 200, 5: 50, 6: 100}[args.config]
 
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -452,6 +635,14 @@ def main():
     c = CONFIGS[cfg]
     B, V, H = c["B"], c["V"], c["H"]
     stream = torch.cuda.current_stream(dev)
+    if cfg == 6:
+        line = lmhead_line(args, dev, rank, world, stream)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     pool = make_pool(cfg, dev, rank, world) if cfg != 5 else None
 
     out_tok = torch.empty(B, dtype=torch.int32, device=dev)

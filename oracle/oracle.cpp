@@ -20,6 +20,7 @@
 //     BeamSearch::search, one step  src/decoder.rs:217-276  (orc_beam_step, raw logits)
 //     SpeculativeDecoder::sample, softmax_at, verify_and_accept
 //                                   src/inference.rs:335-429 (orc_specdec_*)
+//     Model::matmul_vec (the LM head) src/model.rs:246-261   (orc_matmul_vec)
 //     with rand_secure() (src/decoder.rs:170-188) replaced by an injected
 //     uniform. All arithmetic is f32, sums are sequential left-to-right,
 //     exp is the platform libm expf (what Rust's f32::exp lowers to on Linux),
@@ -178,6 +179,38 @@ int32_t orc_decoder_sample(const float* logits_in, int V, float temperature, flo
   if (out_draw_margin) *out_draw_margin = draw_margin;
   if (out_cut_margin) *out_cut_margin = cut_margin;
   return tok;
+}
+
+// Model::matmul_vec (src/model.rs:246-261), the LM head of Model::forward
+// (:236-241): logits[i] = sum over j < min(hidden, len / vocab) of
+// input[j] * weight[i * hidden + j], left to right in f32, terms whose index
+// passes the weight's length left out. Rows of a batch (rows > 1) are
+// independent calls of the same loop; rows are split over nthreads threads.
+void orc_matmul_vec(const float* input, const float* weight, int64_t weight_len, int hidden, int vocab, int rows,
+                    float* out, int nthreads) {
+  const int64_t kmax = std::min<int64_t>(hidden, weight_len / std::max(vocab, 1));
+  auto run = [&](int r0, int r1) {
+    for (int r = r0; r < r1; ++r) {
+      const float* x = input + static_cast<int64_t>(r) * hidden;
+      float* o = out + static_cast<int64_t>(r) * vocab;
+      for (int i = 0; i < vocab; ++i) {
+        float sum = 0.0f;
+        for (int64_t j = 0; j < kmax; ++j) {
+          const int64_t idx = static_cast<int64_t>(i) * hidden + j;
+          if (idx < weight_len) sum += x[j] * weight[idx];
+        }
+        o[i] = sum;
+      }
+    }
+  };
+  nthreads = std::max(1, std::min(nthreads, rows));
+  if (nthreads == 1) {
+    run(0, rows);
+    return;
+  }
+  std::vector<std::thread> ts;
+  for (int t = 0; t < nthreads; ++t) ts.emplace_back(run, rows * t / nthreads, rows * (t + 1) / nthreads);
+  for (auto& t : ts) t.join();
 }
 
 // Decoder::greedy_sample (src/decoder.rs:160-167): argmax, last maximum wins.

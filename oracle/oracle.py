@@ -96,6 +96,8 @@ def lib():
         L.orc_specdec_softmax_at.argtypes = [P, ctypes.c_int, ctypes.c_int64]
         L.orc_specdec_verify.restype = ctypes.c_int32
         L.orc_specdec_verify.argtypes = [P, ctypes.c_int, P, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, P]
+        L.orc_matmul_vec.restype = None
+        L.orc_matmul_vec.argtypes = [P, P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -115,6 +117,19 @@ def decoder_sample(logits, temperature, top_p, r):
                                    _p(prob), _p(cut), _p(dm), _p(cm))
     return dict(token=int(tok), prob=float(prob[0]), cutoff=int(cut[0]),
                 draw_margin=float(dm[0]), cut_margin=float(cm[0]))
+
+
+def matmul_vec(hidden, weight, nthreads=1):
+    """Model::matmul_vec (src/model.rs:246-261) per row of hidden [rows, H]
+    (f32) against weight [V, H] (f32): sequential f32 sums."""
+    x = np.ascontiguousarray(hidden, np.float32)
+    if x.ndim == 1:
+        x = x[None, :]
+    w = np.ascontiguousarray(weight, np.float32)
+    V, H = w.shape
+    out = np.empty((x.shape[0], V), np.float32)
+    lib().orc_matmul_vec(_p(x), _p(w), ctypes.c_int64(w.size), H, V, x.shape[0], _p(out), nthreads)
+    return out
 
 
 def greedy(logits):

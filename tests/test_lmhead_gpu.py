@@ -2,7 +2,8 @@
 W^T, matmul_vec) on the tensor cores, rl_lmhead_*:
 
 - logits against a float64 product of the same bf16 operands, within the
-  error bound of an f32 sum of H exact products (H * 2^-22 * sum |products|);
+  error bound of an f32 sum of H exact products (H * 2^-22 * sum |products|),
+  and against the oracle's matmul_vec (the reference's sequential f32 loop);
 - bf16 logits equal the f32 logits rounded to nearest even, bit for bit;
 - the fused greedy token equals the last-maximum argmax (the oracle's
   greedy_sample) of the kernel's own f32 logits, with and without writing
@@ -55,6 +56,21 @@ def test_logits_f32(smp, B, H, V):
     got = smp.lmhead_logits(hidden, weight)
     torch.cuda.synchronize()
     check_logits(hidden, weight, got)
+
+
+@pytest.mark.parametrize("B,H,V", [(1, 64, 300), (5, 512, 2000), (17, 1024, 5000)])
+def test_logits_against_the_oracle_matmul_vec(smp, B, H, V):
+    """orc_matmul_vec (src/model.rs:246-261: sequential f32 sums) on the
+    same bf16 values: the two f32 sums differ only in the order of the
+    additions, so they agree within twice the bound of one."""
+    hidden, weight = operands(B, H, V, 40 + B)
+    got = smp.lmhead_logits(hidden, weight)
+    torch.cuda.synchronize()
+    x, w = hidden.float().cpu().numpy(), weight.float().cpu().numpy()
+    ref = oracle.matmul_vec(x, w, nthreads=4)
+    bound = H * 2.0 ** -21 * (np.abs(x).astype(np.float64) @ np.abs(w).astype(np.float64).T) + 1e-30
+    err = np.abs(got.cpu().numpy().astype(np.float64) - ref.astype(np.float64))
+    assert (err <= bound).all(), float(err.max())
 
 
 def test_logits_bf16_is_rounded_f32(smp):
