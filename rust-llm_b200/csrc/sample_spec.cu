@@ -1658,21 +1658,24 @@ __device__ float bin_floor_x(float A, const RowT& rt) {
 // (> kCollect: too many). The stream compares raw logits against the bins'
 // value intervals and leaves out the history ids, which are then tested with
 // their penalised values.
+// With explicit edges (expl): the logits in [xlo_o, xhi_o) instead of bin A
+// (A2 must be NaN then).
 template <typename E, bool SPLIT>
 __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, float A2,
-                                        uint64_t* buf, Ctl* ctl) {
+                                        uint64_t* buf, Ctl* ctl, float xlo_o = 0.0f, float xhi_o = 0.0f,
+                                        bool expl = false) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const RowT rt = mt.rt;
   // the four bin edges, one thread each
   if (tid == 0) {
     ctl->cnt = 0;
-    ctl->cx_lo = bin_floor_x(A, rt);
+    ctl->cx_lo = expl ? xlo_o : bin_floor_x(A, rt);
   } else if (tid == 32) {
-    ctl->cx_hi = bin_floor_x(A + 1.0f, rt);
+    ctl->cx_hi = expl ? xhi_o : bin_floor_x(A + 1.0f, rt);
   } else if (tid == 64) {
-    ctl->cx_lo2 = A2 == A2 ? bin_floor_x(A2, rt) : RL_POS_INF;
+    ctl->cx_lo2 = (!expl && A2 == A2) ? bin_floor_x(A2, rt) : RL_POS_INF;
   } else if (tid == 96) {
-    ctl->cx_hi2 = A2 == A2 ? bin_floor_x(A2 + 1.0f, rt) : RL_NEG_INF;
+    ctl->cx_hi2 = (!expl && A2 == A2) ? bin_floor_x(A2 + 1.0f, rt) : RL_NEG_INF;
   }
   cbar();
   const float xlo = ctl->cx_lo;
@@ -1805,6 +1808,95 @@ __device__ __noinline__ int collect_bin(const SpecArgs& a, const ItemMeta& mt, c
   const int n = ctl->cnt;
   cbar();
   return n;
+}
+
+// A bin too full for the collect buffer, split by one re-read: its allowed
+// logits grouped by order key into kSub sub-ranges of the bin's key range
+// [klo, klo + span), sub-range 0 the highest; per sub-range the count
+// (sm.radix[s]) and the exact mass in probability units (the doubles after
+// the counts). All consumer threads return the bin's klo, span and top edge.
+constexpr int kSub = 256;
+static_assert(kSub == kConsumers, "one sub-range per consumer thread");
+template <typename E, bool SPLIT>
+__device__ __noinline__ void sub_hist(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, float M,
+                                      double Z, uint32_t* klo_out, uint32_t* span_out, float* xhi_out) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  const RowT rt = mt.rt;
+  uint32_t* bcnt = sm.radix;
+  double* bmass = reinterpret_cast<double*>(sm.radix + 256);
+  if (tid == 0) sm.ctl->cx_lo = bin_floor_x(A, rt);
+  else if (tid == 32) sm.ctl->cx_hi = bin_floor_x(A + 1.0f, rt);
+  bcnt[tid] = 0u;
+  bmass[tid] = 0.0;
+  cbar();
+  const float xlo = sm.ctl->cx_lo, xhi = sm.ctl->cx_hi;
+  cbar();
+  const uint32_t klo = ord_key(__fadd_rn(xlo, 0.0f));
+  const uint32_t span = ord_key(xhi) - klo;  // > 0: xlo < xhi
+  stream_row<E, SPLIT>(a, mt, tab, [&](float x, int) {
+    if (x >= xlo && x < xhi) {
+      const uint32_t j = static_cast<uint32_t>(
+          (static_cast<uint64_t>(ord_key(__fadd_rn(x, 0.0f)) - klo) * static_cast<uint64_t>(kSub)) / span);
+      const int sb = kSub - 1 - static_cast<int>(j);
+      atomicAdd(&bcnt[sb], 1u);
+      atomicAdd(&bmass[sb], static_cast<double>(exact_e(x, M, rt)) / Z);
+    }
+  });
+  cbar();
+  *klo_out = klo;
+  *span_out = span;
+  *xhi_out = xhi;
+}
+
+// After sub_hist: the first sub-range (highest first) at whose end the running
+// count c0 + n and mass m0 + m satisfy pred; s = INT_MAX when none. Returns
+// the sub-range's value edges [x1, x2) and the count and mass before it, and
+// the bin's exact totals.
+struct SubPick {
+  int s;
+  int n_total;
+  double m_total;
+  long long c_before;
+  double m_before;
+  float x1, x2;
+};
+template <typename P>
+__device__ SubPick pick_sub(uint32_t klo, uint32_t span, float xhi, long long c0, double m0, P pred) {
+  const Smem sm = smem_map();
+  const int tid = threadIdx.x;
+  const uint32_t n = sm.radix[tid];
+  const double m = reinterpret_cast<const double*>(sm.radix + 256)[tid];
+  const long long ci = c0 + static_cast<long long>(cscan_u32(n, sm.red));
+  double mtot;
+  const double mi = m0 + cscan_d(m, sm.red, &mtot);
+  SubPick r;
+  r.n_total = csum_i(static_cast<int>(n), sm.red);
+  r.m_total = mtot;
+  r.s = cmin_i((n > 0u && pred(ci, mi)) ? tid : INT_MAX, sm.red);
+  r.c_before = 0;
+  r.m_before = 0.0;
+  r.x1 = r.x2 = 0.0f;
+  if (r.s != INT_MAX) {
+    if (tid == r.s) {
+      // keys k of sub-range j: floor((k - klo) kSub / span) = j
+      const uint64_t j = static_cast<uint64_t>(kSub - 1 - tid);
+      const uint64_t kSubU = static_cast<uint64_t>(kSub);
+      const uint32_t ka = klo + static_cast<uint32_t>((j * span + kSubU - 1) / kSubU);
+      const uint32_t kb = klo + static_cast<uint32_t>(((j + 1) * span + kSubU - 1) / kSubU);
+      sm.ctl->res_c = ci - static_cast<long long>(n);
+      sm.ctl->res_d = mi - m;
+      sm.ctl->cx_lo2 = ord_key_inv(ka);
+      sm.ctl->cx_hi2 = (j + 1 == kSubU) ? xhi : ord_key_inv(kb);
+    }
+    cbar();
+    r.c_before = sm.ctl->res_c;
+    r.m_before = sm.ctl->res_d;
+    r.x1 = sm.ctl->cx_lo2;
+    r.x2 = sm.ctl->cx_hi2;
+    cbar();
+  }
+  return r;
 }
 
 // Exact radix walk over re-reads of the row: the first logit in list order
@@ -2252,8 +2344,17 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
       // -- the cutoff bin --
       int i_c = nb, cut_pos = -1;
       double Sx = 0.0, bm_cut = 0.0;
+      double bm_bin = 0.0;    // mass before the cutoff bin
+      bool held_sub = false;  // the held keys are one sub-range of their bin
       bool cut_ok = false;
       int i0 = 0;
+      // a lower bound on the logits of bin i: its mass over the mass of a
+      // logit at its top edge (each of its logits has at most that mass)
+      auto bin_min_count = [&](int i) {
+        const double e_top = exp2((static_cast<double>(A_hi - i + 1) / static_cast<double>(kRbin) -
+                                   static_cast<double>(M) / static_cast<double>(T)) * kLog2e) / Z;
+        return (cm[i] - (i > 0 ? cm[i - 1] : 0.0)) / e_top;
+      };
       for (int guard = 0; guard < nb && !cut_ok && (mass_mode || count_mode); ++guard) {
         int best = INT_MAX;
 #pragma unroll
@@ -2296,9 +2397,45 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             if (b_lo == b_hi && b_lo < f) fd = b_lo;
           }
         }
-        const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
-                                               fd >= 0 ? static_cast<float>(A_hi - fd) : __int_as_float(0x7fc00000), buf, ctl);
-        if (ntot > kCollect) break;
+        const double nmin_f = bin_min_count(f);
+        if (fd >= 0 && nmin_f + bin_min_count(fd) > static_cast<double>(kCollect)) fd = -1;
+        // a bin sure to overflow the buffer goes straight to its sub-ranges
+        int ntot = nmin_f > static_cast<double>(kCollect)
+                       ? kCollect + 1
+                       : collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
+                                               fd >= 0 ? static_cast<float>(A_hi - fd) : __int_as_float(0x7fc00000),
+                                               buf, ctl);
+        if (ntot > kCollect && fd >= 0) {
+          // the two bins together overflow the buffer: the cutoff bin alone
+          // (the draw bin is collected by its own re-read below)
+          fd = -1;
+          ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), __int_as_float(0x7fc00000), buf, ctl);
+        }
+        double mbs = mb;     // mass and count before the held keys
+        long long cbs = cb;
+        bool sub = false;
+        if (ntot > kCollect) {
+          // the bin alone overflows the buffer: its sub-ranges, then the
+          // one where the cutoff falls
+          uint32_t klo, span;
+          float xhi;
+          sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
+          const SubPick sp = pick_sub(klo, span, xhi, cb, mb, [&](long long ci, double mi) {
+            return (count_mode && ci >= static_cast<long long>(K)) || (mass_mode && mi >= pd);
+          });
+          if (sp.s == INT_MAX) {
+            // not in this bin: continue with its exact mass and count
+            corr += sp.m_total - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
+            ccorr += static_cast<long long>(sp.n_total) - static_cast<long long>(cc[f] - (f > 0 ? cc[f - 1] : 0.0));
+            i0 = f + 1;
+            continue;
+          }
+          ntot = collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
+          if (ntot > kCollect) break;
+          mbs = sp.m_before;
+          cbs = sp.c_before;
+          sub = true;
+        }
         csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
         n2 = 0;
         if (fd >= 0) {
@@ -2315,19 +2452,23 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         n1 = ntot - n2;
         double cum_at = 0.0, run_end = 0.0;
         const int g = sweep_sorted(
-            buf + off1, n1, M, Z, rt, mb,
+            buf + off1, n1, M, Z, rt, mbs,
             [&](int j, double cum) {
-              return (count_mode && cb + j == static_cast<long long>(K) - 1) || (mass_mode && cum >= pd);
+              return (count_mode && cbs + j == static_cast<long long>(K) - 1) || (mass_mode && cum >= pd);
             },
             rs, ctl, &cum_at, &run_end);
         if (g != INT_MAX) {
           i_c = f;
           cut_pos = g;
           Sx = cum_at;
-          bm_cut = mb;
+          bm_cut = mbs;
+          bm_bin = mb;
+          held_sub = sub;
           cut_ok = true;
-          dbg_pos = cb + g;  // exact when the bins carry counts (debug launches)
+          dbg_pos = cbs + g;  // exact when the bins carry counts (debug launches)
           dbg_id = static_cast<int>(key_id(buf[off1 + g]));
+        } else if (sub) {
+          break;  // the sub-range's sums disagree at rounding level: exact walk
         } else {
           // the histogram overstated this bin: continue with its exact mass
           corr += (run_end - mb) - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
@@ -2365,28 +2506,67 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             if (f == INT_MAX) break;
             const uint64_t* kb = buf + off1;
             int kn = n1;
-            if (held2 == f) {
+            bool at_cut = cut_pos >= 0 && f == i_c;
+            double mb = at_cut ? bm_cut : base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
+            bool dsub = false;  // the keys swept are one sub-range of bin f
+            if (at_cut && held == f && held_sub && tgt < bm_cut) {
+              // the cutoff bin was split and the draw lies above the
+              // sub-range held: the sub-range of the bin that holds it
+              uint32_t klo, span;
+              float xhi;
+              sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
+              const SubPick sp = pick_sub(klo, span, xhi, 0, bm_bin, [&](long long, double mi) { return mi > tgt; });
+              if (sp.s == INT_MAX || !(sp.m_before < bm_cut)) break;
+              const int ntot =
+                  collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
+              if (ntot > kCollect) break;
+              csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
+              held = -1;  // the cutoff's keys are gone
+              kb = buf;
+              kn = ntot;
+              mb = sp.m_before;
+              at_cut = false;
+              dsub = true;
+            } else if (held2 == f) {
               kb = buf;
               kn = n2;
             } else if (held != f) {
-              const int ntot = collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
+              if (at_cut && held_sub) break;  // the cutoff's sub-range is gone: exact walk
+              int ntot = bin_min_count(f) > static_cast<double>(kCollect)
+                             ? kCollect + 1
+                             : collect_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f),
                                                      __int_as_float(0x7fc00000), buf, ctl);
-              if (ntot > kCollect) break;
+              if (ntot > kCollect) {
+                if (at_cut) break;
+                // the bin overflows the buffer: the sub-range where the draw falls
+                uint32_t klo, span;
+                float xhi;
+                sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
+                const SubPick sp = pick_sub(klo, span, xhi, 0, mb, [&](long long, double mi) { return mi > tgt; });
+                if (sp.s == INT_MAX) {
+                  held = -1;
+                  i_d = f + 1;
+                  continue;
+                }
+                ntot = collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
+                if (ntot > kCollect) break;
+                mb = sp.m_before;
+                dsub = true;
+              }
               csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
-              held = f;
+              held = dsub ? -1 : f;
               held2 = -1;
               off1 = 0;
               n1 = ntot;
               kb = buf;
               kn = ntot;
             }
-            const bool at_cut = cut_pos >= 0 && f == i_c;
-            const double mb = at_cut ? bm_cut : base_m + corr + (f > 0 ? cm[f - 1] : 0.0);
             const int lim = at_cut ? cut_pos + 1 : kn;
             double cum_at = 0.0, run_end = 0.0;
             int g = sweep_sorted(
                 kb, lim, M, Z, rt, mb, [&](int, double cum) { return cum > tgt; }, rs, ctl, &cum_at, &run_end);
             if (g == INT_MAX && at_cut) g = cut_pos;
+            if (g == INT_MAX && dsub) break;  // sums disagree at rounding level: exact walk
             if (g != INT_MAX) {
               const uint64_t key = kb[g];
               token = static_cast<int>(key_id(key));

@@ -194,6 +194,15 @@ DEEP = [
     (4, 128256, 0.8, 0, 0.97, 256, 3.0, False),
     (3, 128256, 1.0, 0, 0.9, 64, 1.0, True),
     (3, 128256, 1.0, 0, 1.0, 0, 2.0, False),
+    # flat rows (Gaussian logits, no prior, high temperature): the cutoff and
+    # draw bins overflow the collect buffer together but not alone (T 1.5),
+    # or a bin alone overflows it and is split into sub-ranges by one more
+    # re-read (T 2 and 3; with top_k beyond the list, counts too)
+    (4, 128256, 1.5, 0, 0.95, 0, 3.0, False),
+    (4, 128256, 2.0, 0, 0.9, 64, 3.0, False),
+    (4, 128256, 3.0, 0, 0.5, 0, 3.0, False),
+    (3, 128256, 3.0, 0, 0.99, 256, 3.0, False),
+    (3, 128256, 2.5, 2000, 0.95, 0, 3.0, False),
 ]
 
 
