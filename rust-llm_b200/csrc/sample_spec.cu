@@ -1834,37 +1834,77 @@ __device__ __noinline__ void sub_hist(const SpecArgs& a, const ItemMeta& mt, con
   cbar();
   const uint32_t klo = ord_key(__fadd_rn(xlo, 0.0f));
   const uint32_t span = ord_key(xhi) - klo;  // > 0: xlo < xhi
-  stream_row<E, SPLIT>(a, mt, tab, [&](float x, int) {
-    if (x >= xlo && x < xhi) {
-      const uint32_t j = static_cast<uint32_t>(
-          (static_cast<uint64_t>(ord_key(__fadd_rn(x, 0.0f)) - klo) * static_cast<uint64_t>(kSub)) / span);
-      const int sb = kSub - 1 - static_cast<int>(j);
-      atomicAdd(&bcnt[sb], 1u);
-      atomicAdd(&bmass[sb], static_cast<double>(exact_e(x, M, rt)) / Z);
+  auto add = [&](float x) {
+    const uint32_t j = static_cast<uint32_t>(
+        (static_cast<uint64_t>(ord_key(__fadd_rn(x, 0.0f)) - klo) * static_cast<uint64_t>(kSub)) / span);
+    const int sb = kSub - 1 - static_cast<int>(j);
+    atomicAdd(&bcnt[sb], 1u);
+    atomicAdd(&bmass[sb], static_cast<double>(exact_e(x, M, rt)) / Z);
+  };
+  // raw values of the ids outside the history (plain loads: the re-read is
+  // mostly an L2 hit), then the history ids with their penalised values
+  const E* rowp = reinterpret_cast<const E*>(a.logits) + static_cast<int64_t>(mt.row) * a.ld;
+  const uint32_t* mrow = mt.mask_on ? a.mask + static_cast<int64_t>(mt.row) * a.mask_stride : nullptr;
+  const int ntab = mt.ntab;
+  const int V = a.V;
+  for (int i0 = 0; i0 < V; i0 += kConsumers * 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kConsumers + tid;
+      v[u] = i < V ? to_f32<E>(__ldcg(rowp + i)) : RL_NEG_INF;
     }
-  });
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int i = i0 + u * kConsumers + tid;
+      const float x = v[u];
+      if (!(x >= xlo && x < xhi && x > RL_NEG_INF)) continue;
+      if (mrow && !((__ldcg(mrow + (i >> 5)) >> (i & 31)) & 1u)) continue;
+      if (ntab > 0 && tab_has(tab, ntab, i)) continue;
+      add(x);
+    }
+  }
+  for (int j = tid; j < ntab; j += kConsumers) {
+    const uint32_t ent = tab[j];
+    const int cnt = static_cast<int>(ent & 2047u);
+    const int id = static_cast<int>(ent >> 11);
+    if (cnt == 0 || id >= V) continue;
+    if (mrow && !((__ldcg(mrow + (id >> 5)) >> (id & 31)) & 1u)) continue;
+    const float raw = to_f32<E>(rowp[id]);
+    if (raw != raw) continue;
+    const float x = pen_value(raw, cnt, mt.rp, mt.freq, mt.pres);
+    if (x >= xlo && x < xhi && x > RL_NEG_INF) add(x);
+  }
   cbar();
   *klo_out = klo;
   *span_out = span;
   *xhi_out = xhi;
 }
 
-// After sub_hist: the first sub-range (highest first) at whose end the running
-// count c0 + n and mass m0 + m satisfy pred; s = INT_MAX when none. Returns
-// the sub-range's value edges [x1, x2) and the count and mass before it, and
-// the bin's exact totals.
+// A bin too full for the collect buffer, resolved to one sub-range: after
+// sub_hist, the first sub-range (highest first) at whose end the running
+// count c0 + n / mass m0 + m passes the test (kind 0, the cutoff: count >= K
+// when count_mode, or mass >= p when mass_mode; kind 1, the draw: mass > p);
+// its logits are collected into buf (*ntot keys, > kCollect: too many).
+// s = INT_MAX when the test passes nowhere in the bin; the bin's exact count
+// and mass are returned either way. Out of line: only rows whose bins
+// overflow the buffer come here.
 struct SubPick {
   int s;
   int n_total;
   double m_total;
   long long c_before;
   double m_before;
-  float x1, x2;
 };
-template <typename P>
-__device__ SubPick pick_sub(uint32_t klo, uint32_t span, float xhi, long long c0, double m0, P pred) {
+template <typename E, bool SPLIT>
+__device__ __noinline__ SubPick split_bin(const SpecArgs& a, const ItemMeta& mt, const uint32_t* tab, float A, float M,
+                                          double Z, long long c0, double m0, int kind, long long K, double p,
+                                          bool count_mode, bool mass_mode, uint64_t* buf, int* ntot) {
   const Smem sm = smem_map();
   const int tid = threadIdx.x;
+  uint32_t klo, span;
+  float xhi;
+  sub_hist<E, SPLIT>(a, mt, tab, A, M, Z, &klo, &span, &xhi);
   const uint32_t n = sm.radix[tid];
   const double m = reinterpret_cast<const double*>(sm.radix + 256)[tid];
   const long long ci = c0 + static_cast<long long>(cscan_u32(n, sm.red));
@@ -1873,29 +1913,29 @@ __device__ SubPick pick_sub(uint32_t klo, uint32_t span, float xhi, long long c0
   SubPick r;
   r.n_total = csum_i(static_cast<int>(n), sm.red);
   r.m_total = mtot;
-  r.s = cmin_i((n > 0u && pred(ci, mi)) ? tid : INT_MAX, sm.red);
+  const bool pass = kind == 0 ? ((count_mode && ci >= K) || (mass_mode && mi >= p)) : (mi > p);
+  r.s = cmin_i((n > 0u && pass) ? tid : INT_MAX, sm.red);
   r.c_before = 0;
   r.m_before = 0.0;
-  r.x1 = r.x2 = 0.0f;
-  if (r.s != INT_MAX) {
-    if (tid == r.s) {
-      // keys k of sub-range j: floor((k - klo) kSub / span) = j
-      const uint64_t j = static_cast<uint64_t>(kSub - 1 - tid);
-      const uint64_t kSubU = static_cast<uint64_t>(kSub);
-      const uint32_t ka = klo + static_cast<uint32_t>((j * span + kSubU - 1) / kSubU);
-      const uint32_t kb = klo + static_cast<uint32_t>(((j + 1) * span + kSubU - 1) / kSubU);
-      sm.ctl->res_c = ci - static_cast<long long>(n);
-      sm.ctl->res_d = mi - m;
-      sm.ctl->cx_lo2 = ord_key_inv(ka);
-      sm.ctl->cx_hi2 = (j + 1 == kSubU) ? xhi : ord_key_inv(kb);
-    }
-    cbar();
-    r.c_before = sm.ctl->res_c;
-    r.m_before = sm.ctl->res_d;
-    r.x1 = sm.ctl->cx_lo2;
-    r.x2 = sm.ctl->cx_hi2;
-    cbar();
+  *ntot = 0;
+  if (r.s == INT_MAX) return r;
+  if (tid == r.s) {
+    // keys k of sub-range j: floor((k - klo) kSub / span) = j
+    const uint64_t j = static_cast<uint64_t>(kSub - 1 - tid);
+    const uint64_t kSubU = static_cast<uint64_t>(kSub);
+    const uint32_t ka = klo + static_cast<uint32_t>((j * span + kSubU - 1) / kSubU);
+    const uint32_t kb = klo + static_cast<uint32_t>(((j + 1) * span + kSubU - 1) / kSubU);
+    sm.ctl->res_c = ci - static_cast<long long>(n);
+    sm.ctl->res_d = mi - m;
+    sm.ctl->cx_lo2 = ord_key_inv(ka);
+    sm.ctl->cx_hi2 = (j + 1 == kSubU) ? xhi : ord_key_inv(kb);
   }
+  cbar();
+  r.c_before = sm.ctl->res_c;
+  r.m_before = sm.ctl->res_d;
+  const float x1 = sm.ctl->cx_lo2, x2 = sm.ctl->cx_hi2;
+  cbar();
+  *ntot = collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, sm.ctl, x1, x2, true);
   return r;
 }
 
@@ -2417,12 +2457,8 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
         if (ntot > kCollect) {
           // the bin alone overflows the buffer: its sub-ranges, then the
           // one where the cutoff falls
-          uint32_t klo, span;
-          float xhi;
-          sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
-          const SubPick sp = pick_sub(klo, span, xhi, cb, mb, [&](long long ci, double mi) {
-            return (count_mode && ci >= static_cast<long long>(K)) || (mass_mode && mi >= pd);
-          });
+          const SubPick sp = split_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, cb, mb, 0,
+                                                 static_cast<long long>(K), pd, count_mode, mass_mode, buf, &ntot);
           if (sp.s == INT_MAX) {
             // not in this bin: continue with its exact mass and count
             corr += sp.m_total - (cm[f] - (f > 0 ? cm[f - 1] : 0.0));
@@ -2430,7 +2466,6 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             i0 = f + 1;
             continue;
           }
-          ntot = collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
           if (ntot > kCollect) break;
           mbs = sp.m_before;
           cbs = sp.c_before;
@@ -2512,14 +2547,10 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
             if (at_cut && held == f && held_sub && tgt < bm_cut) {
               // the cutoff bin was split and the draw lies above the
               // sub-range held: the sub-range of the bin that holds it
-              uint32_t klo, span;
-              float xhi;
-              sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
-              const SubPick sp = pick_sub(klo, span, xhi, 0, bm_bin, [&](long long, double mi) { return mi > tgt; });
-              if (sp.s == INT_MAX || !(sp.m_before < bm_cut)) break;
-              const int ntot =
-                  collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
-              if (ntot > kCollect) break;
+              int ntot = 0;
+              const SubPick sp = split_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, 0, bm_bin, 1, 0,
+                                                     tgt, false, false, buf, &ntot);
+              if (sp.s == INT_MAX || !(sp.m_before < bm_cut) || ntot > kCollect) break;
               csort_desc(buf, ntot, pow2_at_least(max(ntot, 1)));
               held = -1;  // the cutoff's keys are gone
               kb = buf;
@@ -2539,16 +2570,13 @@ __device__ __noinline__ void finish_row(const SpecArgs& a, const ItemMeta& mt, c
               if (ntot > kCollect) {
                 if (at_cut) break;
                 // the bin overflows the buffer: the sub-range where the draw falls
-                uint32_t klo, span;
-                float xhi;
-                sub_hist<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, &klo, &span, &xhi);
-                const SubPick sp = pick_sub(klo, span, xhi, 0, mb, [&](long long, double mi) { return mi > tgt; });
+                const SubPick sp = split_bin<E, SPLIT>(a, mt, tab, static_cast<float>(A_hi - f), M, Z, 0, mb, 1, 0,
+                                                       tgt, false, false, buf, &ntot);
                 if (sp.s == INT_MAX) {
                   held = -1;
                   i_d = f + 1;
                   continue;
                 }
-                ntot = collect_bin<E, SPLIT>(a, mt, tab, 0.0f, __int_as_float(0x7fc00000), buf, ctl, sp.x1, sp.x2, true);
                 if (ntot > kCollect) break;
                 mb = sp.m_before;
                 dsub = true;
