@@ -279,6 +279,49 @@ rl_status rl_specdec_verify(rl_sampler* h, const float* logits, int B, int V, in
                             const float* draw_u, int32_t* out_accepted, int32_t* out_tok, void* stream);
 
 /*
+ * Grammar-constrained decoding with a real GBNF grammar: the step after the
+ * reference's toy Grammar (src/decoder.rs:378-557), whose get_allowed_tokens
+ * (:466-529) matches single tokens against rule variants. A grammar in GBNF
+ * notation ("literal", [class], [^class], ., rule names, ( ... ), * + ?
+ * {m,n}; '#' comments) is compiled against the vocabulary (each token's text
+ * as bytes) into a stack automaton and a byte trie of the tokens. Per
+ * sequence a state; per step rl_gbnf_mask writes the bit-packed allowed row
+ * that rl_sample_batch (mask argument) and rl_grammar_greedy take, and
+ * rl_gbnf_accept advances the state by the sampled token. Host functions:
+ * no device work, no handle; a grammar is read-only after create and may be
+ * shared between threads, a state belongs to one thread at a time.
+ *
+ * rl_gbnf_create: text (NUL-terminated), the start rule's name, V tokens
+ *   (tokens[t], token_len[t] bytes; a token of length 0 never matches) and the
+ *   end-of-sequence id (-1: none), which is allowed exactly when the start rule
+ *   is complete. RL_ERR_INVALID_ARG on a syntax error or an undefined rule,
+ *   RL_ERR_UNSUPPORTED on left recursion (the message names the rule).
+ * rl_gbnf_mask: row[words >= ceil(V/32)] := the allowed tokens; *n_allowed
+ *   (nullable) their count. A row of zeros means none (after the end token);
+ *   the samplers read an all-zero row as "every id", so stop such a sequence.
+ * rl_gbnf_mask_batch: the same for B states into mask[B, mask_stride], rows
+ *   spread over nthreads host threads.
+ * rl_gbnf_accept: advances the state by one token; RL_ERR_INVALID_ARG (state
+ *   unchanged) if the grammar does not allow it.
+ * States grow with the grammar's ambiguity; beyond 4096 stacks or 1024 frames
+ * a call returns RL_ERR_SHAPE.
+ */
+typedef struct rl_gbnf rl_gbnf;
+typedef struct rl_gbnf_state rl_gbnf_state;
+rl_status rl_gbnf_create(const char* text, const char* root, int V, const char* const* tokens,
+                         const int32_t* token_len, int32_t eos_id, rl_gbnf** out);
+void rl_gbnf_destroy(rl_gbnf* g);
+rl_status rl_gbnf_state_create(const rl_gbnf* g, rl_gbnf_state** out);
+void rl_gbnf_state_destroy(rl_gbnf_state* s);
+rl_status rl_gbnf_state_copy(const rl_gbnf_state* src, rl_gbnf_state* dst);
+int rl_gbnf_accepting(const rl_gbnf_state* s);
+rl_status rl_gbnf_accept(const rl_gbnf* g, rl_gbnf_state* s, int32_t token);
+rl_status rl_gbnf_mask(const rl_gbnf* g, const rl_gbnf_state* s, uint32_t* mask_row, int64_t words,
+                       int32_t* n_allowed);
+rl_status rl_gbnf_mask_batch(const rl_gbnf* g, const rl_gbnf_state* const* states, int B, uint32_t* mask,
+                             int64_t mask_stride, int32_t* n_allowed, int nthreads);
+
+/*
  * LM head feeding the sampler (src/model.rs:236-262: the final projection of
  * Model::forward, matmul_vec's logits[i] = sum_j hidden[j] * W[i * H + j]),
  * batched, on the tensor cores: logits[b, v] = sum_h hidden[b, h] * W[v, h].

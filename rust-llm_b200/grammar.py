@@ -126,3 +126,123 @@ class Grammar:
         from decoder import allowed_mask
 
         return allowed_mask(self.get_allowed_tokens(prev_tokens), V)
+
+
+# ---------------------------------------------------------------------------
+# Real GBNF grammars (the step after the toy automaton above): compiled in the
+# native library (rl_gbnf_*), masks written as the bit-packed rows the device
+# samplers take.
+# ---------------------------------------------------------------------------
+class GbnfState:
+    """One sequence's position in a Gbnf grammar (rl_gbnf_state)."""
+
+    def __init__(self, grammar: "Gbnf", handle):
+        self.grammar = grammar
+        self.h = handle
+
+    def copy(self) -> "GbnfState":
+        import rlsampler
+
+        s = self.grammar.new_state()
+        rlsampler.check(rlsampler.lib().rl_gbnf_state_copy(self.h, s.h), "rl_gbnf_state_copy")
+        return s
+
+    @property
+    def accepting(self) -> bool:
+        import rlsampler
+
+        return bool(rlsampler.lib().rl_gbnf_accepting(self.h))
+
+    def __del__(self):
+        try:
+            import rlsampler
+
+            if self.h:
+                rlsampler.lib().rl_gbnf_state_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
+class Gbnf:
+    """A GBNF grammar compiled against a vocabulary (token texts as bytes).
+
+    mask(state) -> (row, n): the allowed tokens as one bit-packed uint32 row
+    (bit j of word w is token 32w + j) and their count; accept(state, token)
+    advances the state (RLError when the grammar does not allow the token).
+    The end-of-sequence id is allowed exactly when the start rule is complete."""
+
+    def __init__(self, text: str, tokens, eos_id: int = -1, root: str = "root"):
+        import ctypes
+
+        import rlsampler
+
+        toks = [t.encode() if isinstance(t, str) else bytes(t) for t in tokens]
+        self.V = len(toks)
+        self.words = (self.V + 31) // 32
+        self.eos_id = eos_id
+        bufs = [ctypes.create_string_buffer(t, max(len(t), 1)) for t in toks]
+        ptrs = (ctypes.c_void_p * self.V)(*[ctypes.cast(b, ctypes.c_void_p) for b in bufs])
+        lens = np.array([len(t) for t in toks], np.int32)
+        h = ctypes.c_void_p()
+        rlsampler.check(rlsampler.lib().rl_gbnf_create(text.encode(), root.encode(), self.V, ptrs,
+                                                       lens.ctypes.data_as(ctypes.c_void_p), eos_id,
+                                                       ctypes.byref(h)), "rl_gbnf_create")
+        self.h = h
+
+    def new_state(self) -> GbnfState:
+        import ctypes
+
+        import rlsampler
+
+        h = ctypes.c_void_p()
+        rlsampler.check(rlsampler.lib().rl_gbnf_state_create(self.h, ctypes.byref(h)), "rl_gbnf_state_create")
+        return GbnfState(self, h)
+
+    def mask(self, state: GbnfState):
+        import ctypes
+
+        import rlsampler
+
+        row = np.zeros(self.words, np.uint32)
+        n = ctypes.c_int32()
+        rlsampler.check(rlsampler.lib().rl_gbnf_mask(self.h, state.h, row.ctypes.data_as(ctypes.c_void_p),
+                                                     self.words, ctypes.byref(n)), "rl_gbnf_mask")
+        return row, n.value
+
+    def mask_batch(self, states, out=None, nthreads: int = 8):
+        """Rows for every state into out [len(states), words] (uint32)."""
+        import ctypes
+
+        import rlsampler
+
+        B = len(states)
+        if out is None:
+            out = np.zeros((B, self.words), np.uint32)
+        n = np.zeros(B, np.int32)
+        hs = (ctypes.c_void_p * max(B, 1))(*[s.h for s in states])
+        rlsampler.check(rlsampler.lib().rl_gbnf_mask_batch(self.h, hs, B, out.ctypes.data_as(ctypes.c_void_p),
+                                                           out.shape[1], n.ctypes.data_as(ctypes.c_void_p),
+                                                           nthreads), "rl_gbnf_mask_batch")
+        return out, n
+
+    def accept(self, state: GbnfState, token: int):
+        import rlsampler
+
+        rlsampler.check(rlsampler.lib().rl_gbnf_accept(self.h, state.h, int(token)), "rl_gbnf_accept")
+
+    def allowed(self, state: GbnfState):
+        """The allowed token ids (sorted)."""
+        row, _ = self.mask(state)
+        bits = np.unpackbits(row.view(np.uint8), bitorder="little")[: self.V]
+        return np.flatnonzero(bits).tolist()
+
+    def __del__(self):
+        try:
+            import rlsampler
+
+            if self.h:
+                rlsampler.lib().rl_gbnf_destroy(self.h)
+                self.h = None
+        except Exception:
+            pass

@@ -140,6 +140,24 @@ def lib():
         L.rl_sampler_set_debug.argtypes = [P, ctypes.c_uint32]
         L.rl_selfcheck_div.restype = I
         L.rl_selfcheck_div.argtypes = [P, I, P, I, P, P, P]
+        L.rl_gbnf_create.restype = I
+        L.rl_gbnf_create.argtypes = [ctypes.c_char_p, ctypes.c_char_p, I, P, P, ctypes.c_int32, ctypes.POINTER(P)]
+        L.rl_gbnf_destroy.restype = None
+        L.rl_gbnf_destroy.argtypes = [P]
+        L.rl_gbnf_state_create.restype = I
+        L.rl_gbnf_state_create.argtypes = [P, ctypes.POINTER(P)]
+        L.rl_gbnf_state_destroy.restype = None
+        L.rl_gbnf_state_destroy.argtypes = [P]
+        L.rl_gbnf_state_copy.restype = I
+        L.rl_gbnf_state_copy.argtypes = [P, P]
+        L.rl_gbnf_accepting.restype = I
+        L.rl_gbnf_accepting.argtypes = [P]
+        L.rl_gbnf_accept.restype = I
+        L.rl_gbnf_accept.argtypes = [P, P, ctypes.c_int32]
+        L.rl_gbnf_mask.restype = I
+        L.rl_gbnf_mask.argtypes = [P, P, P, I64, P]
+        L.rl_gbnf_mask_batch.restype = I
+        L.rl_gbnf_mask_batch.argtypes = [P, P, I, P, I64, P, I]
         L.rl_lmhead_logits.restype = I
         L.rl_lmhead_logits.argtypes = [P, P, I64, P, I64, I, I, I, P, I, I64, P]
         L.rl_lmhead_greedy.restype = I

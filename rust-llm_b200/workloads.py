@@ -160,3 +160,36 @@ def mask_from_allowed(V, allowed_rows):
         for i in ids:
             m[b, i >> 5] |= np.uint32(1 << (i & 31))
     return m
+
+
+# ---------------------------------------------------------------------------
+# Grammar-constrained decoding: a JSON grammar in GBNF notation and a seeded
+# synthetic byte-level vocabulary (no tokenizer files are available offline)
+# ---------------------------------------------------------------------------
+GBNF_JSON = r'''
+root   ::= ws value ws
+value  ::= object | array | string | number | "true" | "false" | "null"
+object ::= "{" ws ( member ( ws "," ws member )* )? ws "}"
+member ::= string ws ":" ws value
+array  ::= "[" ws ( value ( ws "," ws value )* )? ws "]"
+string ::= "\"" ( [^"\\\x00-\x1f] | "\\" ( ["\\/bfnrt] | "u" [0-9a-fA-F]{4} ) )* "\""
+number ::= "-"? ( "0" | [1-9] [0-9]* ) ( "." [0-9]+ )? ( [eE] [-+]? [0-9]+ )?
+ws     ::= [ \t\n]*
+'''
+
+
+def json_vocab(V=32000, seed=31):
+    """V tokens: the 256 single bytes, a few JSON pieces, random 2-6 byte
+    strings over a JSON-like alphabet; the last id is the end token (no
+    bytes)."""
+    rng = np.random.default_rng(seed)
+    toks = [bytes([c]) for c in range(256)]
+    toks += [b'{"', b'":', b'",', b'"}', b"true", b"false", b"null", b"[]", b"{}", b", ", b": "]
+    alpha = list(b'abcdekxyz"{}[]:,0123456789.- ')
+    seen = set(toks)
+    while len(toks) < V - 1:
+        t = bytes(rng.choice(alpha, int(rng.integers(2, 7))).tolist())
+        if t not in seen:
+            seen.add(t)
+            toks.append(t)
+    return toks + [b""]

@@ -102,3 +102,17 @@ def test_selfcheck_and_nccl_helpers_reject_bad_arguments():
     assert L.rl_nccl_comm_init(ctypes.byref(comm), 2, uid, 5) == rlsampler.RL_ERR_INVALID_ARG  # rank >= nranks
     assert L.rl_nccl_comm_init(None, 1, uid, 0) == rlsampler.RL_ERR_INVALID_ARG
     assert L.rl_nccl_comm_destroy(None) == rlsampler.RL_OK
+
+
+def test_gbnf_entries_reject_null_arguments():
+    """The grammar entries are host-only: their argument checks need no GPU."""
+    L = rlsampler.lib()
+    P = None
+    out = ctypes.c_void_p()
+    assert L.rl_gbnf_create(b"root ::= \"a\"", b"root", 1, P, P, -1, ctypes.byref(out)) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_state_create(P, ctypes.byref(out)) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_mask(P, P, P, 1, P) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_accept(P, P, 0) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_mask_batch(P, P, 1, P, 1, P, 1) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_accepting(P) == 0
+    assert rlsampler.last_error()
