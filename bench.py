@@ -440,6 +440,76 @@ def shard_step_line(steps, warmup, dev, rank, world, stream):
             "algorithmic_bytes_per_gpu": algorithmic_bytes(5, world)}
 
 
+def gbnf_line(s, dev, stream, steps=30):
+    """Config 3 with a real grammar: 64 sequences constrained by the JSON
+    grammar (GBNF) over a 32,000-token synthetic vocabulary. A step: the
+    allowed rows on the host (rl_gbnf_mask_batch, all host threads), their
+    copy to the device, the masked batched sampler, the tokens back, and each
+    token accepted into its sequence's state (a finished sequence restarts)."""
+    import statistics
+
+    import torch
+
+    import grammar
+    import rlsampler
+    import workloads
+
+    toks = workloads.json_vocab(32000)
+    V = len(toks)
+    eos = V - 1
+    g = grammar.Gbnf(workloads.GBNF_JSON, toks, eos_id=eos)
+    B = 64
+    rng = np.random.default_rng(33)
+    states = [g.new_state() for _ in range(B)]
+    p = np.zeros(B, rlsampler.ROW_PARAMS_DTYPE)
+    p["temperature"] = 0.8
+    p["top_k"] = 50
+    p["top_p"] = 0.95
+    p["repeat_penalty"] = 1.0
+    pd = rlsampler.params_tensor(p, dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3300)
+    logits = [torch.randn((B, V), generator=gen, device=dev) * 3.0 for _ in range(4)]
+    u = torch.from_numpy(rng.random((steps + 3, B)).astype(np.float32)).to(dev)
+    hmask = torch.empty((B, g.words), dtype=torch.int32, pin_memory=True)
+    hrows = hmask.numpy().view(np.uint32)
+    dmask = torch.empty((B, g.words), dtype=torch.int32, device=dev)
+    tok = torch.empty(B, dtype=torch.int32, device=dev)
+    prob = torch.empty(B, dtype=torch.float32, device=dev)
+    st = torch.empty(B, dtype=torch.int32, device=dev)
+    htok = torch.empty(B, dtype=torch.int32, pin_memory=True)
+    nthreads = os.cpu_count() or 1
+    t_mask, t_dev, t_acc, allowed, finished = [], [], [], [], 0
+    for i in range(steps + 3):
+        t0 = time.perf_counter()
+        _, n = g.mask_batch(states, out=hrows, nthreads=nthreads)
+        t1 = time.perf_counter()
+        dmask.copy_(hmask, non_blocking=True)
+        s.sample(logits[i % 4], pd, u[i], None, None, dmask, tok, prob, st, stream=stream)
+        htok.copy_(tok, non_blocking=True)
+        stream.synchronize()
+        t2 = time.perf_counter()
+        for b, t in enumerate(htok.numpy().tolist()):
+            g.accept(states[b], t)
+            if t == eos:
+                states[b] = g.new_state()
+                finished += 1
+        t3 = time.perf_counter()
+        if i >= 3:
+            t_mask.append(t1 - t0)
+            t_dev.append(t2 - t1)
+            t_acc.append(t3 - t2)
+            allowed += n.tolist()
+    step = statistics.median([a + b + c for a, b, c in zip(t_mask, t_dev, t_acc)])
+    return {"value": B / step, "unit": "tokens/s", "ms_per_step": step * 1e3,
+            "mask_ms": statistics.median(t_mask) * 1e3, "device_ms": statistics.median(t_dev) * 1e3,
+            "accept_ms": statistics.median(t_acc) * 1e3, "host_threads": nthreads,
+            "allowed_tokens_median": int(statistics.median(allowed)), "allowed_tokens_max": int(max(allowed)),
+            "documents_finished": finished, "batch": B, "vocab": V, "steps": steps,
+            "path": "rl_gbnf_mask_batch (host) -> mask H2D -> rl_sample_batch with masks -> tokens D2H -> "
+                    "rl_gbnf_accept per row; medians over the steps"}
+
+
 def lmhead_line(args, dev, rank, world, stream):
     """Config 6: hidden states -> tokens. The LM head (src/model.rs:236-262)
     as one tcgen05 GEMM (rl_lmhead_sample: bf16 weight [V, 4096] resident in
@@ -748,6 +818,8 @@ def main():
         e2e = {"value": e2e_us, "unit": "us/token", "h2d_bytes_per_step": V * 4 + H * 4 + 4 + 24 + 4,
                "d2h_bytes_per_step": 8, "path": "rl_sample_host, one call per token (host logits in, token out)"}
 
+    gbnf = gbnf_line(s, dev, stream) if cfg == 3 and world == 1 else None
+
     shards = None
     if cfg == 2 and not args.no_shards:
         shards = shard_step_line(20, 3, dev, rank, world, stream)
@@ -793,6 +865,8 @@ def main():
         }
         if shards:
             line["vocab_shards"] = shards
+        if gbnf:
+            line["gbnf_json"] = gbnf
         if not args.no_cpu_baseline and world == 1 and cfg != 5:
             if cfg == 4:
                 import oracle
