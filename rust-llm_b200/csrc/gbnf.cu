@@ -34,6 +34,7 @@
 #include <cstdint>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <unordered_map>
@@ -484,8 +485,34 @@ bool accepting(const StackSet& s) { return !s.empty() && s.front().empty(); }
 }  // namespace gbnf
 }  // namespace rl
 
+// The grammar and a cache of finished mask rows by state: a state seen
+// before (they recur: the same position inside a string, a value, an array at
+// the same depth) is answered by a copy. Bounded (kCacheRows rows, emptied
+// when full); guarded by a mutex, so one grammar may serve several threads.
+namespace rl {
+namespace gbnf {
+struct SetHash {
+  size_t operator()(const StackSet& s) const {
+    uint64_t h = 1469598103934665603ull;
+    for (const Stack& st : s) {
+      for (uint32_t x : st) h = (h ^ x) * 1099511628211ull;
+      h = (h ^ 0xffffffffull) * 1099511628211ull;
+    }
+    return static_cast<size_t>(h);
+  }
+};
+struct CachedRow {
+  std::vector<uint32_t> row;
+  int count;
+};
+constexpr size_t kCacheBytes = 64u << 20;  // rows kept at most: 64 MB of them
+}  // namespace gbnf
+}  // namespace rl
+
 struct rl_gbnf {
   rl::gbnf::Grammar g;
+  mutable std::mutex mu;
+  mutable std::unordered_map<rl::gbnf::StackSet, rl::gbnf::CachedRow, rl::gbnf::SetHash> cache;
 };
 struct rl_gbnf_state {
   rl::gbnf::StackSet set;
@@ -554,6 +581,16 @@ rl_status mask_one(const rl_gbnf* G, const rl_gbnf_state* s, uint32_t* row, int6
   const Grammar& g = G->g;
   std::fill(row, row + words, 0u);
   int count = 0;
+  const int64_t vw = (g.V + 31) / 32;
+  if (!s->finished && !s->set.empty()) {
+    std::lock_guard<std::mutex> lk(G->mu);
+    auto it = G->cache.find(s->set);
+    if (it != G->cache.end()) {
+      std::copy(it->second.row.begin(), it->second.row.end(), row);
+      if (n_allowed) *n_allowed = it->second.count;
+      return RL_OK;
+    }
+  }
   if (!s->finished && !s->set.empty()) {
     Walk w(g);
     StackSet start = s->set;
@@ -564,6 +601,9 @@ rl_status mask_one(const rl_gbnf* G, const rl_gbnf_state* s, uint32_t* row, int6
       row[g.eos >> 5] |= 1u << (g.eos & 31);
       ++count;
     }
+    std::lock_guard<std::mutex> lk(G->mu);
+    if ((G->cache.size() + 1) * static_cast<size_t>(vw) * 4u > kCacheBytes) G->cache.clear();
+    G->cache[s->set] = CachedRow{std::vector<uint32_t>(row, row + vw), count};
   }
   if (n_allowed) *n_allowed = count;
   return RL_OK;
@@ -745,10 +785,37 @@ rl_status rl_gbnf_mask_batch(const rl_gbnf* G, const rl_gbnf_state* const* state
     return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_mask_batch: mask_stride < ceil(V/32)");
   for (int b = 0; b < B; ++b)
     if (!states[b]) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_mask_batch: NULL state");
-  nthreads = std::max(1, std::min(nthreads, B));
+  // rows whose state is cached are copied here; the others are walked, on
+  // up to nthreads threads when there are several
   std::vector<rl_status> st(static_cast<size_t>(B), RL_OK);
-  auto run = [&](int b0, int b1) {
-    for (int b = b0; b < b1; ++b) {
+  std::vector<int> miss;
+  {
+    const Grammar& g = G->g;
+    const int64_t vw = (g.V + 31) / 32;
+    std::lock_guard<std::mutex> lk(G->mu);
+    for (int b = 0; b < B; ++b) {
+      uint32_t* row = mask + static_cast<int64_t>(b) * mask_stride;
+      const rl_gbnf_state* s = states[b];
+      if (s->finished || s->set.empty()) {
+        std::fill(row, row + mask_stride, 0u);
+        if (n_allowed) n_allowed[b] = 0;
+        continue;
+      }
+      auto it = G->cache.find(s->set);
+      if (it == G->cache.end()) {
+        miss.push_back(b);
+        continue;
+      }
+      std::copy(it->second.row.begin(), it->second.row.end(), row);
+      std::fill(row + vw, row + mask_stride, 0u);
+      if (n_allowed) n_allowed[b] = it->second.count;
+    }
+  }
+  const int M = static_cast<int>(miss.size());
+  nthreads = std::max(1, std::min(nthreads, M));
+  auto run = [&](int i0, int i1) {
+    for (int i = i0; i < i1; ++i) {
+      const int b = miss[i];
       try {
         st[b] = mask_one(G, states[b], mask + static_cast<int64_t>(b) * mask_stride, mask_stride,
                          n_allowed ? n_allowed + b : nullptr);
@@ -758,10 +825,10 @@ rl_status rl_gbnf_mask_batch(const rl_gbnf* G, const rl_gbnf_state* const* state
     }
   };
   if (nthreads == 1) {
-    run(0, B);
+    run(0, M);
   } else {
     std::vector<std::thread> ts;
-    for (int t = 0; t < nthreads; ++t) ts.emplace_back(run, B * t / nthreads, B * (t + 1) / nthreads);
+    for (int t = 0; t < nthreads; ++t) ts.emplace_back(run, M * t / nthreads, M * (t + 1) / nthreads);
     for (auto& t : ts) t.join();
   }
   for (int b = 0; b < B; ++b)
