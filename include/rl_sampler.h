@@ -283,8 +283,10 @@ rl_status rl_specdec_verify(rl_sampler* h, const float* logits, int B, int V, in
  * reference's toy Grammar (src/decoder.rs:378-557), whose get_allowed_tokens
  * (:466-529) matches single tokens against rule variants. A grammar in GBNF
  * notation ("literal", [class], [^class], ., rule names, ( ... ), * + ?
- * {m,n}; '#' comments) is compiled against the vocabulary (each token's text
- * as bytes) into a stack automaton and a byte trie of the tokens. Per
+ * {m,n}; '#' comments; \xHH \uHHHH \UHHHHHHHH escapes; classes and '.' are
+ * over Unicode characters) is compiled against the vocabulary (each token's
+ * text as UTF-8 bytes; a character may span tokens) into a stack automaton
+ * over bytes and a byte trie of the tokens. Per
  * sequence a state; per step rl_gbnf_mask writes the bit-packed allowed row
  * that rl_sample_batch (mask argument) and rl_grammar_greedy take, and
  * rl_gbnf_accept advances the state by the sampled token. Host functions:

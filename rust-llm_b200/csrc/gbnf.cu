@@ -9,15 +9,19 @@
 // Grammar notation (one rule per `name ::= ...`; a rule's alternatives may
 // continue on lines that start with '|'; inside parentheses newlines are
 // free; '#' starts a comment):
-//   "literal"   bytes, with escapes \n \r \t \\ \" \' \[ \] \- \xHH
-//   [a-z_0-9]   one byte in the class; [^...] one byte outside it
-//   .           any byte
+//   "literal"   characters, with escapes \n \r \t \\ \" \' \[ \] \- and
+//               \xHH \uHHHH \UHHHHHHHH (code points)
+//   [a-z_0-9]   one character in the class; [^...] one character outside it
+//               (ranges of code points; surrogates excluded)
+//   .           any character
 //   name        a rule (defined anywhere in the text)
 //   ( ... )     a group of alternatives
 //   x* x+ x?    repetition of the preceding element (literal, class, rule or
 //               group); x{m} x{m,} x{m,n} bounded repetition
-// Matching is over the bytes of the tokens' text (UTF-8 text matches as its
-// bytes; a class range of non-ASCII characters is a range of single bytes).
+// The grammar text is UTF-8. Matching is over the bytes of the tokens' text:
+// a character is its UTF-8 encoding, so a class with non-ASCII members
+// compiles into a rule whose alternatives are byte-class sequences (the ASCII
+// part stays one byte class), and a character may span several tokens.
 //
 // Automaton: a state is a set of stacks of element positions. A stack's top
 // is always a byte class (or the stack is empty: the start rule is complete,
@@ -178,11 +182,35 @@ struct Parser {
     if (c >= 'A' && c <= 'F') return c - 'A' + 10;
     return -1;
   }
-  // one (possibly escaped) byte of a literal or class
-  bool byte_of(int* out) {
+  // one (possibly escaped) character of a literal or class, as a code point:
+  // the grammar text is UTF-8; \xHH, \uHHHH and \UHHHHHHHH name code points
+  bool hex_cp(int digits, uint32_t* out) {
+    if (end - p < digits) return fail("bad hexadecimal escape");
+    uint32_t v = 0;
+    for (int i = 0; i < digits; ++i) {
+      const int h = hexval(p[i]);
+      if (h < 0) return fail("bad hexadecimal escape");
+      v = v * 16 + static_cast<uint32_t>(h);
+    }
+    p += digits;
+    *out = v;
+    return true;
+  }
+  bool cp_of(uint32_t* out) {
     if (p >= end) return fail("unexpected end of grammar");
-    if (*p != '\\') {
-      *out = static_cast<unsigned char>(*p++);
+    const unsigned char c0 = static_cast<unsigned char>(*p);
+    if (c0 != '\\') {
+      // UTF-8 sequence of the grammar text
+      int n = c0 < 0x80 ? 1 : (c0 >> 5) == 6 ? 2 : (c0 >> 4) == 14 ? 3 : (c0 >> 3) == 30 ? 4 : 0;
+      if (n == 0 || end - p < n) return fail("invalid UTF-8 in the grammar text");
+      uint32_t v = n == 1 ? c0 : (c0 & (0x7Fu >> n));
+      for (int i = 1; i < n; ++i) {
+        const unsigned char ci = static_cast<unsigned char>(p[i]);
+        if ((ci & 0xC0) != 0x80) return fail("invalid UTF-8 in the grammar text");
+        v = (v << 6) | (ci & 0x3Fu);
+      }
+      p += n;
+      *out = v;
       return true;
     }
     ++p;
@@ -192,15 +220,135 @@ struct Parser {
       case 'n': *out = '\n'; return true;
       case 'r': *out = '\r'; return true;
       case 't': *out = '\t'; return true;
-      case '\\': case '"': case '\'': case '[': case ']': case '-': case '^': *out = c; return true;
-      case 'x': {
-        if (end - p < 2 || hexval(p[0]) < 0 || hexval(p[1]) < 0) return fail("bad \\x escape");
-        *out = hexval(p[0]) * 16 + hexval(p[1]);
-        p += 2;
-        return true;
-      }
+      case '\\': case '"': case '\'': case '[': case ']': case '-': case '^': *out = static_cast<unsigned char>(c); return true;
+      case 'x': return hex_cp(2, out);
+      case 'u': return hex_cp(4, out);
+      case 'U': return hex_cp(8, out);
       default: return fail(std::string("unknown escape \\") + c);
     }
+  }
+  static bool valid_cp(uint32_t v) { return v <= 0x10FFFFu && !(v >= 0xD800u && v <= 0xDFFFu); }
+  static int utf8_encode(uint32_t v, uint8_t* b) {
+    if (v < 0x80u) {
+      b[0] = static_cast<uint8_t>(v);
+      return 1;
+    }
+    if (v < 0x800u) {
+      b[0] = static_cast<uint8_t>(0xC0u | (v >> 6));
+      b[1] = static_cast<uint8_t>(0x80u | (v & 0x3Fu));
+      return 2;
+    }
+    if (v < 0x10000u) {
+      b[0] = static_cast<uint8_t>(0xE0u | (v >> 12));
+      b[1] = static_cast<uint8_t>(0x80u | ((v >> 6) & 0x3Fu));
+      b[2] = static_cast<uint8_t>(0x80u | (v & 0x3Fu));
+      return 3;
+    }
+    b[0] = static_cast<uint8_t>(0xF0u | (v >> 18));
+    b[1] = static_cast<uint8_t>(0x80u | ((v >> 12) & 0x3Fu));
+    b[2] = static_cast<uint8_t>(0x80u | ((v >> 6) & 0x3Fu));
+    b[3] = static_cast<uint8_t>(0x80u | (v & 0x3Fu));
+    return 4;
+  }
+  // The code points [lo, hi] (no surrogates, one encoded length n > 1) as
+  // sequences of byte classes: split until every byte position of the
+  // encodings ranges freely below a common prefix (the UTF-8 range split
+  // that regular-expression engines use, after Russ Cox's utf8 ranges).
+  void utf8_seqs(uint32_t lo, uint32_t hi, std::vector<Seq>* out) {
+    static const uint32_t kMaxOfLen[4] = {0x7Fu, 0x7FFu, 0xFFFFu, 0x10FFFFu};
+    for (int k = 0; k < 3; ++k)
+      if (lo <= kMaxOfLen[k] && hi > kMaxOfLen[k]) {
+        utf8_seqs(lo, kMaxOfLen[k], out);
+        utf8_seqs(kMaxOfLen[k] + 1, hi, out);
+        return;
+      }
+    uint8_t a[4], b[4];
+    const int n = utf8_encode(lo, a);
+    for (int i = 1; i < n; ++i) {
+      const uint32_t m = (1u << (6 * i)) - 1u;
+      if ((lo & ~m) != (hi & ~m)) {
+        if ((lo & m) != 0u) {
+          utf8_seqs(lo, lo | m, out);
+          utf8_seqs((lo | m) + 1u, hi, out);
+          return;
+        }
+        if ((hi & m) != m) {
+          utf8_seqs(lo, (hi & ~m) - 1u, out);
+          utf8_seqs(hi & ~m, hi, out);
+          return;
+        }
+      }
+    }
+    utf8_encode(hi, b);
+    Seq sq;
+    for (int i = 0; i < n; ++i) {
+      ByteSet bs;
+      for (int c = a[i]; c <= b[i]; ++c) bs.add(c);
+      sq.push_back({kChars, set_of(bs)});
+    }
+    out->push_back(std::move(sq));
+  }
+  // One character from the code-point ranges (sorted, disjoint, valid): a
+  // single byte class when they are all ASCII, else a rule whose
+  // alternatives are the ASCII byte class and the multi-byte sequences.
+  bool char_element(const std::string& rule, const std::vector<std::pair<uint32_t, uint32_t>>& ranges, Seq* seq) {
+    ByteSet ascii;
+    bool any_ascii = false;
+    std::vector<Seq> alts;
+    for (const auto& r : ranges) {
+      uint32_t lo = r.first, hi = r.second;
+      if (lo <= 0x7Fu) {
+        for (uint32_t c = lo; c <= std::min(hi, 0x7Fu); ++c) ascii.add(static_cast<int>(c));
+        any_ascii = true;
+        if (hi <= 0x7Fu) continue;
+        lo = 0x80u;
+      }
+      utf8_seqs(lo, hi, &alts);
+    }
+    if (alts.empty()) {
+      if (!any_ascii) return fail("a class that matches no character in rule " + rule);
+      seq->push_back({kChars, set_of(ascii)});
+      return true;
+    }
+    if (any_ascii) {
+      Seq a1;
+      a1.push_back({kChars, set_of(ascii)});
+      alts.insert(alts.begin(), std::move(a1));
+    }
+    const uint32_t r = new_rule(rule);
+    bodies[r] = std::move(alts);
+    seq->push_back({kRef, r});
+    return true;
+  }
+  // ranges -> sorted, merged, without surrogates; complemented when neg
+  static std::vector<std::pair<uint32_t, uint32_t>> normalize_ranges(std::vector<std::pair<uint32_t, uint32_t>> v,
+                                                                     bool neg) {
+    std::sort(v.begin(), v.end());
+    std::vector<std::pair<uint32_t, uint32_t>> m;
+    for (const auto& r : v) {
+      if (!m.empty() && r.first <= m.back().second + 1u) m.back().second = std::max(m.back().second, r.second);
+      else m.push_back(r);
+    }
+    if (neg) {
+      std::vector<std::pair<uint32_t, uint32_t>> c;
+      uint32_t next = 0;
+      for (const auto& r : m) {
+        if (r.first > next) c.push_back({next, r.first - 1u});
+        next = r.second + 1u;
+      }
+      if (next <= 0x10FFFFu) c.push_back({next, 0x10FFFFu});
+      m.swap(c);
+    }
+    std::vector<std::pair<uint32_t, uint32_t>> out;
+    for (const auto& r : m) {
+      if (r.first <= 0xDFFFu && r.second >= 0xD800u) {
+        if (r.first < 0xD800u) out.push_back({r.first, 0xD7FFu});
+        if (r.second > 0xDFFFu) out.push_back({0xE000u, r.second});
+      } else {
+        out.push_back(r);
+      }
+    }
+    return out;
   }
   bool alternatives(const std::string& rule, bool nested, std::vector<Seq>* out) {
     Seq s;
@@ -229,11 +377,16 @@ struct Parser {
       if (*p == '"') {
         ++p;
         while (p < end && *p != '"') {
-          int c;
-          if (!byte_of(&c)) return false;
-          ByteSet b;
-          b.add(c);
-          seq->push_back({kChars, set_of(b)});
+          uint32_t v;
+          if (!cp_of(&v)) return false;
+          if (!valid_cp(v)) return fail("a literal's character is not a Unicode scalar value in rule " + rule);
+          uint8_t b8[4];
+          const int nb = utf8_encode(v, b8);
+          for (int i = 0; i < nb; ++i) {
+            ByteSet b;
+            b.add(b8[i]);
+            seq->push_back({kChars, set_of(b)});
+          }
         }
         if (p >= end) return fail("unterminated literal in rule " + rule);
         ++p;
@@ -248,27 +401,25 @@ struct Parser {
           neg = true;
           ++p;
         }
-        ByteSet b;
+        std::vector<std::pair<uint32_t, uint32_t>> ranges;
         while (p < end && *p != ']') {
-          int lo;
-          if (!byte_of(&lo)) return false;
-          int hi = lo;
+          uint32_t lo;
+          if (!cp_of(&lo)) return false;
+          uint32_t hi = lo;
           if (p + 1 < end && *p == '-' && p[1] != ']') {
             ++p;
-            if (!byte_of(&hi)) return false;
+            if (!cp_of(&hi)) return false;
             if (hi < lo) return fail("empty range in a class of rule " + rule);
           }
-          for (int c = lo; c <= hi; ++c) b.add(c);
+          if (hi > 0x10FFFFu) return fail("a class range beyond U+10FFFF in rule " + rule);
+          ranges.push_back({lo, hi});
         }
         if (p >= end) return fail("unterminated class in rule " + rule);
         ++p;
-        if (neg) b.invert();
-        seq->push_back({kChars, set_of(b)});
+        if (!char_element(rule, normalize_ranges(std::move(ranges), neg), seq)) return false;
       } else if (*p == '.') {
         ++p;
-        ByteSet b;
-        b.invert();
-        seq->push_back({kChars, set_of(b)});
+        if (!char_element(rule, normalize_ranges({{0u, 0x10FFFFu}}, false), seq)) return false;
       } else if (*p == '(') {
         ++p;
         space(true);

@@ -212,3 +212,53 @@ def test_right_recursion_does_not_deepen_the_stacks():
     assert g.allowed(s) == [0, 1]
     g.accept(s, 1)
     assert g.allowed(s) == [2]
+
+
+UCASES = [
+    # classes and '.' are over characters (code points), matched as their UTF-8 bytes
+    ('root ::= [α-ω]+ "." [^a-z]', r"[α-ω]+\.[^a-z]"),
+    ('root ::= "x" . "y"', r"(?s)x.y"),
+    ('root ::= "\\u00e9" [\\u4e00-\\u9fff]{1,2} "\\U0001F600"?', "é[一-鿿]{1,2}(?:\U0001F600)?"),
+    ('root ::= [^é中]+ "!"', r"[^é中]+!"),
+]
+UALPHA = list("abxy.!") + list("αβγωé中文字") + ["\U0001F600", "ÿ", "ࠀ", "\n"]
+
+
+@pytest.mark.parametrize("case", range(len(UCASES)))
+def test_unicode_masks_equal_the_regex_oracle(case):
+    text, pattern = UCASES[case]
+    rng = np.random.default_rng(200 + case)
+    toks = set(UALPHA)
+    while len(toks) < 200:
+        toks.add("".join(rng.choice(UALPHA, int(rng.integers(2, 4)))))
+    toks = sorted(toks) + [""]
+    eos = len(toks) - 1
+    g = grammar.Gbnf(text, toks, eos_id=eos)
+    for walk in range(6):
+        s = g.new_state()
+        prefix = ""
+        for step in range(15):
+            got = set(g.allowed(s))
+            want = oracle_mask(pattern, prefix, toks, eos)
+            assert got == want, (case, walk, step, repr(prefix), sorted(got ^ want)[:10])
+            choices = sorted(want - {eos})
+            if not choices:
+                break
+            t = int(rng.choice(choices))
+            g.accept(s, t)
+            prefix += toks[t]
+
+
+def test_tokens_that_split_a_character():
+    """Byte-level tokens may end inside a UTF-8 sequence: the automaton
+    follows the character across them."""
+    toks = [b"\xc3", b"\xa9", b"x", "é".encode(), b""]
+    g = grammar.Gbnf('root ::= "é" "x"', toks, eos_id=4)
+    s = g.new_state()
+    assert g.allowed(s) == [0, 3]
+    g.accept(s, 0)
+    assert g.allowed(s) == [1]
+    g.accept(s, 1)
+    assert g.allowed(s) == [2]
+    g.accept(s, 2)
+    assert g.allowed(s) == [4]
