@@ -489,11 +489,11 @@ def gbnf_line(s, dev, stream, steps=30):
         htok.copy_(tok, non_blocking=True)
         stream.synchronize()
         t2 = time.perf_counter()
-        for b, t in enumerate(htok.numpy().tolist()):
-            g.accept(states[b], t)
-            if t == eos:
-                states[b] = g.new_state()
-                finished += 1
+        toks_np = htok.numpy()
+        g.accept_batch(states, toks_np, nthreads=nthreads)
+        for b in np.flatnonzero(toks_np == eos).tolist():
+            states[b] = g.new_state()
+            finished += 1
         t3 = time.perf_counter()
         if i >= 3:
             t_mask.append(t1 - t0)
@@ -507,7 +507,7 @@ def gbnf_line(s, dev, stream, steps=30):
             "allowed_tokens_median": int(statistics.median(allowed)), "allowed_tokens_max": int(max(allowed)),
             "documents_finished": finished, "batch": B, "vocab": V, "steps": steps,
             "path": "rl_gbnf_mask_batch (host) -> mask H2D -> rl_sample_batch with masks -> tokens D2H -> "
-                    "rl_gbnf_accept per row; medians over the steps"}
+                    "rl_gbnf_accept_batch; medians over the steps"}
 
 
 def lmhead_line(args, dev, rank, world, stream):

@@ -320,6 +320,11 @@ int rl_gbnf_accepting(const rl_gbnf_state* s);
 rl_status rl_gbnf_accept(const rl_gbnf* g, rl_gbnf_state* s, int32_t token);
 rl_status rl_gbnf_mask(const rl_gbnf* g, const rl_gbnf_state* s, uint32_t* mask_row, int64_t words,
                        int32_t* n_allowed);
+/* rl_gbnf_accept for B states and their tokens, rows spread over host
+ * threads; row_status[B] (nullable) gets each row's status (a refused row's
+ * state is unchanged); the call returns the first failing row's status. */
+rl_status rl_gbnf_accept_batch(const rl_gbnf* g, rl_gbnf_state* const* states, const int32_t* tokens, int B,
+                               int32_t* row_status, int nthreads);
 rl_status rl_gbnf_mask_batch(const rl_gbnf* g, const rl_gbnf_state* const* states, int B, uint32_t* mask,
                              int64_t mask_stride, int32_t* n_allowed, int nthreads);
 

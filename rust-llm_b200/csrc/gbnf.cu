@@ -917,6 +917,32 @@ rl_status rl_gbnf_accept(const rl_gbnf* G, rl_gbnf_state* s, int32_t token) {
   }
 }
 
+rl_status rl_gbnf_accept_batch(const rl_gbnf* G, rl_gbnf_state* const* states, const int32_t* tokens, int B,
+                               int32_t* row_status, int nthreads) {
+  if (!G || (B > 0 && (!states || !tokens))) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept_batch: NULL argument");
+  if (B < 0) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept_batch: B < 0");
+  std::vector<rl_status> st(static_cast<size_t>(B), RL_OK);
+  // a few microseconds a row: threads only pay for larger batches
+  nthreads = std::max(1, std::min(nthreads, B / 16));
+  auto run = [&](int b0, int b1) {
+    for (int b = b0; b < b1; ++b) st[b] = rl_gbnf_accept(G, states[b], tokens[b]);
+  };
+  if (nthreads == 1) {
+    run(0, B);
+  } else {
+    std::vector<std::thread> ts;
+    for (int t = 0; t < nthreads; ++t) ts.emplace_back(run, B * t / nthreads, B * (t + 1) / nthreads);
+    for (auto& t : ts) t.join();
+  }
+  rl_status first = RL_OK;
+  for (int b = 0; b < B; ++b) {
+    if (row_status) row_status[b] = st[b];
+    if (first == RL_OK) first = st[b];
+  }
+  if (first != RL_OK) return rl::set_error(first, "rl_gbnf_accept_batch: a row's token was refused (see row_status)");
+  return RL_OK;
+}
+
 rl_status rl_gbnf_mask(const rl_gbnf* G, const rl_gbnf_state* s, uint32_t* mask_row, int64_t words,
                        int32_t* n_allowed) {
   if (!G || !s || !mask_row) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_mask: NULL argument");

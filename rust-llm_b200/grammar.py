@@ -231,6 +231,22 @@ class Gbnf:
 
         rlsampler.check(rlsampler.lib().rl_gbnf_accept(self.h, state.h, int(token)), "rl_gbnf_accept")
 
+    def accept_batch(self, states, tokens, nthreads: int = 8):
+        """accept() for every state and its token (rows over host threads);
+        RLError if any row's token is refused (those rows stay unchanged)."""
+        import ctypes
+
+        import rlsampler
+
+        B = len(states)
+        toks = np.ascontiguousarray(tokens, np.int32)
+        st = np.zeros(B, np.int32)
+        hs = (ctypes.c_void_p * max(B, 1))(*[s.h for s in states])
+        rlsampler.check(rlsampler.lib().rl_gbnf_accept_batch(self.h, hs, toks.ctypes.data_as(ctypes.c_void_p), B,
+                                                             st.ctypes.data_as(ctypes.c_void_p), nthreads),
+                        "rl_gbnf_accept_batch")
+        return st
+
     def allowed(self, state: GbnfState):
         """The allowed token ids (sorted)."""
         row, _ = self.mask(state)

@@ -156,6 +156,8 @@ def lib():
         L.rl_gbnf_accept.argtypes = [P, P, ctypes.c_int32]
         L.rl_gbnf_mask.restype = I
         L.rl_gbnf_mask.argtypes = [P, P, P, I64, P]
+        L.rl_gbnf_accept_batch.restype = I
+        L.rl_gbnf_accept_batch.argtypes = [P, P, P, I, P, I]
         L.rl_gbnf_mask_batch.restype = I
         L.rl_gbnf_mask_batch.argtypes = [P, P, I, P, I64, P, I]
         L.rl_lmhead_logits.restype = I

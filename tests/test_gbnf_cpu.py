@@ -262,3 +262,27 @@ def test_tokens_that_split_a_character():
     assert g.allowed(s) == [2]
     g.accept(s, 2)
     assert g.allowed(s) == [4]
+
+
+def test_accept_batch_equals_single_accepts():
+    rng = np.random.default_rng(10)
+    toks = json_vocab(rng)
+    eos = len(toks) - 1
+    by = {t: i for i, t in enumerate(toks) if t}
+    g = grammar.Gbnf(JSON, toks, eos_id=eos)
+    docs = [greedy_tokens(json.dumps(random_json(rng)), by) for _ in range(40)]
+    a = [g.new_state() for _ in docs]
+    b = [g.new_state() for _ in docs]
+    for step in range(max(len(d) for d in docs)):
+        live = [i for i, d in enumerate(docs) if step < len(d)]
+        g.accept_batch([a[i] for i in live], [docs[i][step] for i in live], nthreads=4)
+        for i in live:
+            g.accept(b[i], docs[i][step])
+    for x, y in zip(a, b):
+        assert g.allowed(x) == g.allowed(y) and x.accepting
+    # a refused token: that row's status, the others advance
+    s1, s2 = g.new_state(), g.new_state()
+    with pytest.raises(rlsampler.RLError):
+        g.accept_batch([s1, s2], [by[b"{"], by[b"}"]])
+    assert g.allowed(s2) == g.allowed(g.new_state())
+    assert by[b"}"] in set(g.allowed(s1))  # s1 took '{'
