@@ -657,6 +657,34 @@ struct CachedRow {
   int count;
 };
 constexpr size_t kCacheBytes = 64u << 20;  // rows kept at most: 64 MB of them
+
+// The accept path's lazy automaton: stack sets interned as they are met,
+// each (set, byte) transition computed once and kept, so accepting a token
+// is a table walk once its bytes have been seen from that state. Bounded
+// (kDfaMax sets, about 1 KB of transitions each): when full it is emptied and
+// its epoch advances, which tells the states that their ids are stale.
+constexpr size_t kDfaMax = 16384;
+struct Dfa {
+  std::unordered_map<StackSet, int32_t, SetHash> ids;
+  std::vector<const StackSet*> sets;  // id -> its set (the map's keys do not move)
+  std::vector<int32_t> next;          // [id * 256 + byte]: -2 unknown, -1 refused, else the next id
+  uint32_t epoch = 1;
+  int32_t intern(const StackSet& st) {
+    auto it = ids.find(st);
+    if (it != ids.end()) return it->second;
+    if (sets.size() >= kDfaMax) {
+      ids.clear();
+      sets.clear();
+      next.clear();
+      ++epoch;
+    }
+    const int32_t id = static_cast<int32_t>(sets.size());
+    auto ins = ids.emplace(st, id).first;
+    sets.push_back(&ins->first);
+    next.resize(next.size() + 256, -2);
+    return id;
+  }
+};
 }  // namespace gbnf
 }  // namespace rl
 
@@ -664,10 +692,14 @@ struct rl_gbnf {
   rl::gbnf::Grammar g;
   mutable std::mutex mu;
   mutable std::unordered_map<rl::gbnf::StackSet, rl::gbnf::CachedRow, rl::gbnf::SetHash> cache;
+  mutable std::mutex dfa_mu;
+  mutable rl::gbnf::Dfa dfa;
 };
 struct rl_gbnf_state {
   rl::gbnf::StackSet set;
-  int finished = 0;  // the end-of-sequence token was accepted
+  int finished = 0;        // the end-of-sequence token was accepted
+  int32_t dfa_id = -1;     // the set's id in the grammar's lazy automaton,
+  uint32_t dfa_epoch = 0;  // valid while the automaton's epoch is this one
 };
 
 namespace {
@@ -898,19 +930,50 @@ rl_status rl_gbnf_accept(const rl_gbnf* G, rl_gbnf_state* s, int32_t token) {
       if (!accepting(s->set)) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept: the grammar is not complete");
       s->finished = 1;
       s->set.clear();
+      s->dfa_id = -1;
       return RL_OK;
     }
     if (g.tb_begin[token + 1] == g.tb_begin[token])
       return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept: the token has no bytes");
-    StackSet cur = s->set, next;
-    const std::vector<uint8_t> bytes(g.tb.begin() + g.tb_begin[token], g.tb.begin() + g.tb_begin[token + 1]);
-    for (uint8_t c : bytes) {
-      if (!advance(g, cur, c, next))
-        return rl::set_error(RL_ERR_SHAPE, "rl_gbnf_accept: the grammar's state grew beyond its stack limits");
-      if (next.empty()) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept: the grammar does not allow the token");
-      cur.swap(next);
+    std::lock_guard<std::mutex> lk(G->dfa_mu);
+    Dfa& d = G->dfa;
+    int32_t id = (s->dfa_epoch == d.epoch && s->dfa_id >= 0) ? s->dfa_id : d.intern(s->set);
+    const uint32_t epoch0 = d.epoch;
+    for (uint32_t k = g.tb_begin[token]; k < g.tb_begin[token + 1]; ++k) {
+      const int c = g.tb[k];
+      int32_t n = d.next[static_cast<size_t>(id) * 256 + static_cast<size_t>(c)];
+      if (n == -2) {
+        StackSet out;
+        if (!advance(g, *d.sets[id], c, out))
+          return rl::set_error(RL_ERR_SHAPE, "rl_gbnf_accept: the grammar's state grew beyond its stack limits");
+        if (out.empty()) {
+          n = -1;
+        } else {
+          n = d.intern(out);
+          if (d.epoch != epoch0) {
+            // the automaton was emptied to make room: walk this token again
+            // from the state's own set, uncached
+            StackSet cur = s->set, nx;
+            for (uint32_t q = g.tb_begin[token]; q < g.tb_begin[token + 1]; ++q) {
+              if (!advance(g, cur, g.tb[q], nx))
+                return rl::set_error(RL_ERR_SHAPE, "rl_gbnf_accept: the grammar's state grew beyond its stack limits");
+              if (nx.empty())
+                return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept: the grammar does not allow the token");
+              cur.swap(nx);
+            }
+            s->set.swap(cur);
+            s->dfa_id = -1;
+            return RL_OK;
+          }
+        }
+        d.next[static_cast<size_t>(id) * 256 + static_cast<size_t>(c)] = n;
+      }
+      if (n < 0) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept: the grammar does not allow the token");
+      id = n;
     }
-    s->set.swap(cur);
+    s->set = *d.sets[id];
+    s->dfa_id = id;
+    s->dfa_epoch = d.epoch;
     return RL_OK;
   } catch (...) {
     return rl::set_error(RL_ERR_OOM, "rl_gbnf_accept: host allocation failed");
@@ -922,8 +985,9 @@ rl_status rl_gbnf_accept_batch(const rl_gbnf* G, rl_gbnf_state* const* states, c
   if (!G || (B > 0 && (!states || !tokens))) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept_batch: NULL argument");
   if (B < 0) return rl::set_error(RL_ERR_INVALID_ARG, "rl_gbnf_accept_batch: B < 0");
   std::vector<rl_status> st(static_cast<size_t>(B), RL_OK);
-  // a few microseconds a row: threads only pay for larger batches
-  nthreads = std::max(1, std::min(nthreads, B / 16));
+  // a few microseconds a row, under the lazy automaton's lock: threads only
+  // pay for large batches (measured slower than one thread at 64 rows)
+  nthreads = std::max(1, std::min(nthreads, B / 256));
   auto run = [&](int b0, int b1) {
     for (int b = b0; b < b1; ++b) st[b] = rl_gbnf_accept(G, states[b], tokens[b]);
   };

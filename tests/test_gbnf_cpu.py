@@ -286,3 +286,28 @@ def test_accept_batch_equals_single_accepts():
         g.accept_batch([s1, s2], [by[b"{"], by[b"}"]])
     assert g.allowed(s2) == g.allowed(g.new_state())
     assert by[b"}"] in set(g.allowed(s1))  # s1 took '{'
+
+
+def test_accept_automaton_past_its_bound():
+    """More distinct states than the accept path's lazy automaton keeps
+    (16,384): it is emptied and refilled on the way, and the states walk on
+    exactly as a second grammar's do."""
+    toks = [chr(c) for c in range(ord("a"), ord("z") + 1)] + [""]
+    eos = len(toks) - 1
+    text = 'root ::= ("a" [b-z]{0,60}){0,1000}'  # unambiguous: 'a' always opens a group
+    g1 = grammar.Gbnf(text, toks, eos_id=eos)
+    g2 = grammar.Gbnf(text, toks, eos_id=eos)
+    rng = np.random.default_rng(12)
+    s1, s2 = g1.new_state(), g2.new_state()
+    for step in range(20000):
+        allowed = [t for t in g1.allowed(s1) if t != eos]
+        if not allowed:
+            break
+        rest = [x for x in allowed if x != 0]
+        t = 0 if (not rest or rng.random() < 0.03) else int(rng.choice(rest))  # a new group now and then
+        g1.accept(s1, t)
+        g2.accept(s2, t)
+        if step % 997 == 0:
+            assert g1.allowed(s1) == g2.allowed(s2)
+    assert step > 16384
+    assert g1.allowed(s1) == g2.allowed(s2) and s1.accepting == s2.accepting
