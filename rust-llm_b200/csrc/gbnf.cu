@@ -34,6 +34,8 @@
 // Masks: the vocabulary's token bytes form a trie walked depth first from the
 // state; a subtree is cut at the first byte no stack accepts, so the cost is
 // the number of trie nodes the grammar allows next, not the vocabulary size.
+// Finished rows are cached by state. Accepts walk a lazy automaton (interned
+// stack sets, byte transitions computed once) that the grammar's states share.
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
