@@ -114,5 +114,6 @@ def test_gbnf_entries_reject_null_arguments():
     assert L.rl_gbnf_mask(P, P, P, 1, P) == rlsampler.RL_ERR_INVALID_ARG
     assert L.rl_gbnf_accept(P, P, 0) == rlsampler.RL_ERR_INVALID_ARG
     assert L.rl_gbnf_mask_batch(P, P, 1, P, 1, P, 1) == rlsampler.RL_ERR_INVALID_ARG
+    assert L.rl_gbnf_accept_batch(P, P, P, 1, P, 1) == rlsampler.RL_ERR_INVALID_ARG
     assert L.rl_gbnf_accepting(P) == 0
     assert rlsampler.last_error()
