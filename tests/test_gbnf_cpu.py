@@ -311,3 +311,32 @@ def test_accept_automaton_past_its_bound():
             assert g1.allowed(s1) == g2.allowed(s2)
     assert step > 16384
     assert g1.allowed(s1) == g2.allowed(s2) and s1.accepting == s2.accepting
+
+
+def test_generated_documents_parse_as_json():
+    """Random walks through the masks (any allowed token; after a while the
+    closing tokens and the end token are preferred) end only in documents
+    that json.loads accepts."""
+    rng = np.random.default_rng(13)
+    toks = json_vocab(rng)
+    eos = len(toks) - 1
+    g = grammar.Gbnf(JSON, toks, eos_id=eos)
+    closers = {i for i, t in enumerate(toks) if t in (b"]", b"}", b'"', b"0", b"1")}
+    finished = 0
+    for walk in range(60):
+        s = g.new_state()
+        text = b""
+        for step in range(400):
+            allowed = g.allowed(s)
+            if step > 20:
+                pref = [t for t in allowed if t == eos or t in closers]
+                if pref:
+                    allowed = pref
+            t = eos if eos in allowed and step > 20 else int(rng.choice(allowed))
+            g.accept(s, t)
+            if t == eos:
+                json.loads(text.decode("utf-8", errors="surrogateescape"))
+                finished += 1
+                break
+            text += toks[t]
+    assert finished >= 50
